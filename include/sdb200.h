@@ -1,0 +1,172 @@
+/* sdb200.h - C ABI of the B200 (sm_100a) backend for StableDiffusion-cpp's dense
+ * contraction path.
+ *
+ * Every entry point takes plain device pointers, sizes in elements and leading
+ * dimensions in elements, exactly like the reference backend API
+ * (src/backend_cuda.h, namespace sd::cuda); the comment above each declaration names
+ * the reference function it replaces as "backend_cuda.h:<line>". The same shared
+ * library also exports the reference's C++ symbols (sd::cuda::gemm_nt_bf16, ...) with
+ * identical signatures, so the reference's `make CUDA=1` link line can take
+ * libsdb200.so in place of build/backend_cuda.o; those C++ wrappers call the functions
+ * below and throw std::runtime_error(message) on a non-zero status, as the reference
+ * does (backend_cuda.cu:41-48).
+ *
+ * Conventions
+ *   - Row-major; C[M,N] = A[M,K] * B[N,K]^T (+ bias[N]) (+ C when accumulate != 0).
+ *   - M <= 0 or N <= 0 is a no-op (backend_cuda.cu:455, :464).
+ *   - bf16 values are uint16_t bit patterns: the top 16 bits of an IEEE float
+ *     (tensor.h:43-45, :137-142).
+ *   - Every op is enqueued on the current device's stream (sdb200_set_stream; default
+ *     the legacy default stream) and returns without synchronising, except
+ *     sdb200_download and sdb200_synchronize.
+ *   - Return value: 0 on success, otherwise an SDB200_ERR_* code; the message of the
+ *     last failure on the calling thread is returned by sdb200_last_error().
+ *   - Thread model: one host thread (or process) per GPU. Calls for one device must
+ *     not run concurrently from several threads on the same stream's workspace.
+ */
+#ifndef SDB200_H
+#define SDB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SDB200_ABI_VERSION 1
+
+#define SDB200_OK 0
+#define SDB200_ERR_INVALID_ARG 1 /* bad size, leading dimension, alignment or null pointer */
+#define SDB200_ERR_NO_DEVICE 2
+#define SDB200_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define SDB200_ERR_DEVICE_WAIT 4 /* a kernel's bounded wait expired; see sdb200_device_error_word */
+#define SDB200_ERR_OUT_OF_MEMORY 5
+#define SDB200_ERR_UNSUPPORTED 6
+
+/* ---- library / device ---------------------------------------------------------- */
+int sdb200_version(void);
+const char* sdb200_last_error(void);
+/* backend_cuda.h:24 available(): 1 if a B200-class (sm_100) device is usable. */
+int sdb200_available(void);
+int sdb200_device_count(void);
+/* backend_cuda.h:26 device_name() */
+const char* sdb200_device_name(void);
+/* backend_cuda.h:27 device_memory() */
+size_t sdb200_device_memory(void);
+/* Extension (the reference hard-wires device 0, backend_cuda.cu:64-72): selects the
+ * calling thread's device. */
+int sdb200_set_device(int device);
+/* Extension (the reference uses the default stream only, backend_cuda.cu:10-11):
+ * every later op of the current device is issued on `stream` (a cudaStream_t). */
+int sdb200_set_stream(void* stream);
+void* sdb200_get_stream(void);
+/* Synchronises the stream, then reads the device error word that kernels set when a
+ * bounded wait expires (0 = none) without clearing it. */
+int sdb200_device_error_word(int* out);
+
+/* ---- memory (backend_cuda.h:29-36) --------------------------------------------- */
+/* backend_cuda.h:30 malloc(): size-class caching allocator; NULL on failure. */
+void* sdb200_malloc(size_t bytes);
+/* backend_cuda.h:31 free() */
+int sdb200_free(void* p);
+/* backend_cuda.h:32 upload() host -> device (stream-ordered) */
+int sdb200_upload(void* dst, const void* src, size_t bytes);
+/* backend_cuda.h:33 download() device -> host; synchronises */
+int sdb200_download(void* dst, const void* src, size_t bytes);
+/* backend_cuda.h:34 copy() device -> device */
+int sdb200_copy(void* dst, const void* src, size_t bytes);
+/* backend_cuda.h:35 zero() */
+int sdb200_zero(void* dst, size_t bytes);
+/* backend_cuda.h:36 synchronize(); also reports an expired device wait as
+ * SDB200_ERR_DEVICE_WAIT (and clears the error word). */
+int sdb200_synchronize(void);
+
+/* ---- GEMM (the hot path) ------------------------------------------------------- */
+/* backend_cuda.h:39-40 gemm_nt_f32(): fp32 weights. Both operands are rounded to tf32
+ * (nearest even) and multiplied on tcgen05 kind::tf32 with fp32 accumulation; M <= 16
+ * uses an exact fp32 memory-bound kernel. */
+int sdb200_gemm_nt_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                       float* C, int64_t ldc, const float* bias, int accumulate);
+/* backend_cuda.h:42-43 gemm_nt_bf16(): bf16 weights; A is rounded to bf16 (nearest
+ * even, as backend_cuda.cu:466-467 does) and multiplied on tcgen05 kind::f16 with fp32
+ * accumulation in TMEM; M <= 16 uses an exact fp32-A memory-bound kernel. */
+int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
+                        int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
+/* Extension of backend_cuda.h:42-43 for producers that already emit bf16 activations:
+ * A is bf16 [M, lda]. */
+int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
+                         int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
+
+/* Fused-epilogue GEMM (extension; the reference runs these as separate kernels after
+ * the GEMM: swiglu backend_cuda.h:61, geglu :60, bias backend_cuda.cu:239-241).
+ *   epi 0: Y = A B^T + bias (fp32 or bf16 Y)
+ *   epi 1: SwiGLU. B rows are interleaved in blocks of 16: rows [32j, 32j+16) are gate
+ *          rows, [32j+16, 32j+32) the matching up rows; Y[m, 16j+i] = silu(g) * u.
+ *          Y has N/2 columns.
+ *   epi 2: GEGLU with the same interleave; Y = value * gelu_erf(gate).
+ * A is bf16 when a_bf16 != 0, else fp32 (rounded to bf16). y_bf16 != 0 stores Y as
+ * bf16 (ldy in bf16 elements). */
+int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, int a_bf16,
+                              const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, int y_bf16, const float* bias,
+                              int epi);
+
+/* Tuning extension (no reference counterpart): forces the GEMM tile width N (64, 128,
+ * 192 or 256) for later calls of this process; 0 restores the automatic choice. */
+int sdb200_set_gemm_tile(int bn);
+
+/* ---- attention ------------------------------------------------------------------- */
+/* backend_cuda.h:58-59 attention(): q [N, Sq, heads*d]; k, v [N, Skv, kv_heads*d];
+ * out [N, Sq, heads*d]; softmax(q k^T / sqrt(d)) v per head, query head h reads kv
+ * head h / (heads / kv_heads); causal keeps keys j <= query row i. */
+int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                     int heads, int kv_heads, int64_t d, int causal);
+
+/* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
+/* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */
+int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
+                  int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo);
+/* backend_cuda.h:48-49 group_norm() */
+int sdb200_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                      const float* beta, float eps);
+/* backend_cuda.h:50 layer_norm() */
+int sdb200_layer_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta,
+                      float eps);
+/* backend_cuda.h:51 rms_norm() */
+int sdb200_rms_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, float eps);
+/* backend_cuda.h:52 rms_norm_heads() (in place) */
+int sdb200_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma, float eps);
+/* backend_cuda.h:54-55 rope() (in place): x [N, S, inner]; cos/sin [S, dim] */
+int sdb200_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const float* cos, const float* sin,
+                int interleaved);
+/* backend_cuda.h:56 softmax_rows() (in place) */
+int sdb200_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, int causal);
+/* backend_cuda.h:60 geglu(): x [rows, 2D] -> y [rows, D] */
+int sdb200_geglu(const float* x, float* y, int64_t rows, int64_t D);
+/* backend_cuda.h:61 swiglu() */
+int sdb200_swiglu(const float* gate, const float* up, float* y, int64_t n);
+
+/* ---- elementwise / shape (backend_cuda.h:64-80) --------------------------------- */
+int sdb200_silu(float* x, int64_t n);                       /* backend_cuda.h:64 */
+int sdb200_tanh(float* x, int64_t n);                       /* backend_cuda.h:65 */
+int sdb200_gelu(float* x, int64_t n);                       /* backend_cuda.h:66 */
+int sdb200_quick_gelu(float* x, int64_t n);                 /* backend_cuda.h:67 */
+int sdb200_add(float* a, const float* b, int64_t n);        /* backend_cuda.h:68 */
+int sdb200_scale(float* x, float s, int64_t n);             /* backend_cuda.h:69 */
+int sdb200_affine(float* x, float a, float b, int64_t n);   /* backend_cuda.h:70 */
+int sdb200_mul_rows(float* x, const float* v, int64_t rows, int64_t dim);                      /* backend_cuda.h:71 */
+int sdb200_add_rows_scaled(float* x, const float* y, const float* g, int64_t rows, int64_t dim); /* backend_cuda.h:72 */
+int sdb200_add_channel_bias(float* x, const float* b, int64_t N, int64_t C, int64_t HW);        /* backend_cuda.h:73 */
+int sdb200_upsample_nearest2x(const float* x, float* y, int64_t NC, int64_t H, int64_t W);      /* backend_cuda.h:74 */
+int sdb200_concat_channels(const float* a, const float* b, float* y, int64_t N, int64_t Ca, int64_t Cb,
+                           int64_t HW);                                                          /* backend_cuda.h:75 */
+int sdb200_nchw_to_nlc(const float* x, float* y, int64_t N, int64_t C, int64_t HW);            /* backend_cuda.h:76 */
+int sdb200_nlc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW);            /* backend_cuda.h:77 */
+int sdb200_patchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p);         /* backend_cuda.h:79 */
+int sdb200_unpatchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p);       /* backend_cuda.h:80 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDB200_H */

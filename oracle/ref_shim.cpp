@@ -1,0 +1,191 @@
+// ref_shim.cpp - TEST INFRASTRUCTURE ONLY (the checker, never the product).
+//
+// Exposes the reference's own CPU implementation (StableDiffusion-cpp src/tensor.cpp,
+// src/zimage.cpp, src/modules.cpp, compiled unmodified from their location in the
+// reference tree by oracle/Makefile) through plain C entry points, so the parity tests
+// and the CPU baseline can call it with numpy buffers. Every function copies its
+// inputs into sd::Tensor objects, runs the reference op, and copies the result out.
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "safetensors.h"
+#include "tensor.h"
+#include "zimage.h"
+
+using namespace sd;
+
+namespace {
+thread_local std::string g_err;
+
+Tensor make(const float* p, std::vector<int64_t> shape) {
+  Tensor t(shape);
+  if (t.numel()) std::memcpy(t.ptr(), p, (size_t)t.numel() * sizeof(float));
+  return t;
+}
+void put(const Tensor& t, float* out) { std::memcpy(out, t.ptr(), (size_t)t.numel() * sizeof(float)); }
+
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+}  // namespace
+
+extern "C" {
+
+const char* sdref_last_error() { return g_err.c_str(); }
+void sdref_set_num_threads(int n) { set_num_threads(n); }
+int sdref_num_threads() { return num_threads(); }
+
+uint16_t sdref_f32_to_bf16(float f) { return f32_to_bf16(f); }
+void sdref_f32_to_bf16_array(const float* x, uint16_t* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = f32_to_bf16(x[i]);
+}
+
+// tensor.cpp:354 gemm_nt
+void sdref_gemm_nt(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+                   int64_t ldc, const float* bias, int acc) {
+  gemm_nt(M, N, K, A, lda, B, ldb, C, ldc, bias, acc != 0);
+}
+// tensor.cpp:412 gemm_nt_bf16
+void sdref_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                        float* C, int64_t ldc, const float* bias, int acc) {
+  gemm_nt_bf16(M, N, K, A, lda, B, ldb, C, ldc, bias, acc != 0);
+}
+
+// tensor.cpp:776 attention; q [N,Sq,heads*d], k/v [N,Skv,kv_heads*d]
+int sdref_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                    int heads, int kv_heads, int64_t d, int causal) {
+  return guard([&] {
+    Tensor tq = make(q, {N, Sq, heads * d});
+    Tensor tk = make(k, {N, Skv, kv_heads * d});
+    Tensor tv = make(v, {N, Skv, kv_heads * d});
+    put(attention(tq, tk, tv, heads, causal != 0, kv_heads), out);
+  });
+}
+
+// tensor.cpp:752 softmax_rows_ (in place)
+void sdref_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, int causal) {
+  softmax_rows_(x, rows, cols, scale, causal != 0);
+}
+
+int sdref_rms_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, float eps) {
+  return guard([&] {
+    Tensor tx = make(x, {rows, C});
+    Tensor g = gamma ? make(gamma, {C}) : Tensor();
+    put(rms_norm(tx, gamma ? &g : nullptr, eps), y);
+  });
+}
+int sdref_layer_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta,
+                     float eps) {
+  return guard([&] {
+    Tensor tx = make(x, {rows, C});
+    Tensor g = gamma ? make(gamma, {C}) : Tensor();
+    Tensor b = beta ? make(beta, {C}) : Tensor();
+    put(layer_norm(tx, gamma ? &g : nullptr, beta ? &b : nullptr, eps), y);
+  });
+}
+int sdref_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma, float eps) {
+  return guard([&] {
+    Tensor tx = make(x, {groups, dim});
+    Tensor g = gamma ? make(gamma, {dim}) : Tensor();
+    rms_norm_heads_(tx, dim, gamma ? &g : nullptr, eps);
+    put(tx, x);
+  });
+}
+int sdref_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const float* cs, const float* sn,
+               int interleaved) {
+  return guard([&] {
+    Tensor tx = make(x, {N, S, inner});
+    Tensor c = make(cs, {S, dim}), s = make(sn, {S, dim});
+    rope_(tx, dim, c, s, interleaved != 0);
+    put(tx, x);
+  });
+}
+int sdref_swiglu(const float* g, const float* u, float* y, int64_t n) {
+  return guard([&] { put(swiglu(make(g, {n}), make(u, {n})), y); });
+}
+int sdref_geglu(const float* x, float* y, int64_t rows, int64_t D) {
+  return guard([&] { put(geglu(make(x, {rows, 2 * D})), y); });
+}
+int sdref_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                     const float* beta, float eps) {
+  return guard([&] {
+    put(group_norm(make(x, {N, C, HW, 1}), groups, make(gamma, {C}), make(beta, {C}), eps), y);
+  });
+}
+int sdref_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
+                 int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out) {
+  return guard([&] {
+    Tensor tw = make(w, {Cout, Cin, kh, kw});
+    Tensor b = bias ? make(bias, {Cout}) : Tensor();
+    put(conv2d(make(x, {N, Cin, H, W}), tw, bias ? &b : nullptr, stride, pad), out);
+  });
+}
+int sdref_mul_rows(float* x, const float* v, int64_t rows, int64_t dim) {
+  return guard([&] {
+    Tensor tx = make(x, {rows, dim});
+    mul_rows_(tx, make(v, {dim}));
+    put(tx, x);
+  });
+}
+int sdref_add_rows_scaled(float* x, const float* y, const float* g, int64_t rows, int64_t dim) {
+  return guard([&] {
+    Tensor tx = make(x, {rows, dim});
+    add_rows_scaled_(tx, make(y, {rows, dim}), make(g, {dim}));
+    put(tx, x);
+  });
+}
+
+// ---- Z-Image transformer (zimage.cpp) on an in-memory random-init Weights ----------
+void* sdref_weights_new() { return new Weights(); }
+void sdref_weights_free(void* w) { delete static_cast<Weights*>(w); }
+// Adds tensor `name`; bf16 != 0 stores it as BF16 with the reference's rounding
+// (Tensor::to_bf16, tensor.cpp:128-134), as the loader does for large weights.
+int sdref_weights_add(void* w, const char* name, const int64_t* shape, int ndim, const float* data, int bf16) {
+  return guard([&] {
+    std::vector<int64_t> s(shape, shape + ndim);
+    Tensor t = make(data, s);
+    if (bf16) t.to_bf16();
+    static_cast<Weights*>(w)->tensors[name] = std::move(t);
+  });
+}
+void* sdref_zimage_new(void* w, int heads, int patch, float norm_eps, float rope_theta, float t_scale, int ax0,
+                       int ax1, int ax2) {
+  try {
+    ZImageTransformer::Config c;
+    c.heads = heads;
+    c.patch = patch;
+    c.norm_eps = norm_eps;
+    c.rope_theta = rope_theta;
+    c.t_scale = t_scale;
+    c.axes_dims[0] = ax0;
+    c.axes_dims[1] = ax1;
+    c.axes_dims[2] = ax2;
+    return new ZImageTransformer(*static_cast<Weights*>(w), c);
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void sdref_zimage_free(void* m) { delete static_cast<ZImageTransformer*>(m); }
+// x [1, C, H, W], cap [1, L, capdim] -> out [1, C, H, W]
+int sdref_zimage_forward(void* m, const float* x, int64_t C, int64_t H, int64_t W, float t, const float* cap,
+                         int64_t L, int64_t capdim, float* out) {
+  return guard([&] {
+    Tensor tx = make(x, {1, C, H, W});
+    Tensor tc = make(cap, {1, L, capdim});
+    put(static_cast<ZImageTransformer*>(m)->forward(tx, t, tc), out);
+  });
+}
+
+}  // extern "C"

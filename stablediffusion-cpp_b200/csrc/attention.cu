@@ -1,0 +1,130 @@
+// attention.cu - softmax(q k^T / sqrt(d)) v per head with grouped key/value heads and
+// an optional causal mask: the replacement for the reference's attention
+// (backend_cuda.cu:550-586, CPU tensor.cpp:771-810), which materialises the full
+// Sq x Skv score matrix per head in HBM.
+//
+// This file holds the exact-fp32 streaming kernel (online softmax, no score matrix in
+// memory): K/V tiles of 32 keys are staged in shared memory and shared by the query
+// rows of a block; each warp owns one query row and keeps its running max, sum and
+// output accumulator in registers. It serves every head dim up to 256 and is the path
+// for shapes the tensor-core kernel (attention_tc.cu) does not take.
+#include <algorithm>
+#include <cmath>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sdb {
+namespace {
+
+constexpr int kRows = 8;   // query rows (warps) per block
+constexpr int kKeys = 32;  // keys per shared-memory tile
+
+template <int DV>  // DV = ceil(d / 32): output dims owned per lane
+__global__ void __launch_bounds__(kRows * 32)
+    k_attention_simt(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                     float* __restrict__ out, int64_t Sq, int64_t Skv, int heads, int kv_heads, int d, int causal,
+                     float scale) {
+  extern __shared__ float sm[];
+  float* sk = sm;                   // [kKeys][d]
+  float* sv = sk + kKeys * d;       // [kKeys][d]
+  float* sq = sv + kKeys * d;       // [kRows][d]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int h = blockIdx.y, n = blockIdx.z;
+  const int group = heads / kv_heads, kvh = h / group;
+  const int64_t inner = (int64_t)heads * d, kv_inner = (int64_t)kv_heads * d;
+  const int64_t i = (int64_t)blockIdx.x * kRows + w;  // query row of this warp
+  const float* qb = q + (int64_t)n * Sq * inner + (int64_t)h * d;
+  const float* kb = k + (int64_t)n * Skv * kv_inner + (int64_t)kvh * d;
+  const float* vb = v + (int64_t)n * Skv * kv_inner + (int64_t)kvh * d;
+  for (int t = lane; t < d; t += 32) sq[w * d + t] = i < Sq ? qb[i * inner + t] * scale : 0.0f;
+  float m = -INFINITY, l = 0.0f, o[DV];
+#pragma unroll
+  for (int c = 0; c < DV; ++c) o[c] = 0.0f;
+  // Keys needed by this block: all, or up to the last row's diagonal when causal.
+  const int64_t last_row = std::min<int64_t>(Sq, (int64_t)(blockIdx.x + 1) * kRows) - 1;
+  const int64_t kend = causal ? std::min<int64_t>(Skv, last_row + 1) : Skv;
+  for (int64_t j0 = 0; j0 < kend; j0 += kKeys) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < kKeys * d; e += blockDim.x) {
+      const int r = e / d, t = e - r * d;
+      const int64_t j = j0 + r;
+      sk[e] = j < Skv ? kb[j * kv_inner + t] : 0.0f;
+      sv[e] = j < Skv ? vb[j * kv_inner + t] : 0.0f;
+    }
+    __syncthreads();
+    // lane r scores key j0 + r
+    const int64_t j = j0 + lane;
+    float s = 0.0f;
+    for (int t = 0; t < d; ++t) s = fmaf(sq[w * d + t], sk[lane * d + t], s);
+    const bool valid = (j < Skv) && (!causal || j <= i);
+    s = valid ? s : -INFINITY;
+    float mx = s;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float m_new = fmaxf(m, mx);
+    if (m_new == -INFINITY) continue;  // nothing valid yet for this row
+    const float corr = expf(m - m_new);
+    const float p = valid ? expf(s - m_new) : 0.0f;
+    float ps = p;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+    l = l * corr + ps;
+    m = m_new;
+#pragma unroll
+    for (int c = 0; c < DV; ++c) o[c] *= corr;
+    for (int r = 0; r < kKeys; ++r) {
+      const float pr = __shfl_sync(0xffffffffu, p, r);
+#pragma unroll
+      for (int c = 0; c < DV; ++c) {
+        const int t = lane + 32 * c;
+        if (t < d) o[c] = fmaf(pr, sv[r * d + t], o[c]);
+      }
+    }
+  }
+  if (i < Sq) {
+    float* ob = out + (int64_t)n * Sq * inner + i * inner + (int64_t)h * d;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+    for (int c = 0; c < DV; ++c) {
+      const int t = lane + 32 * c;
+      if (t < d) ob[t] = o[c] * inv;
+    }
+  }
+}
+
+template <int DV>
+void launch_simt(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                 int heads, int kv_heads, int64_t d, bool causal) {
+  const size_t smem = (size_t)(2 * kKeys + kRows) * d * sizeof(float);
+  if (smem > 48 * 1024)
+    check_cuda(cudaFuncSetAttribute(k_attention_simt<DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+               "attention attr");
+  dim3 grid((unsigned)((Sq + kRows - 1) / kRows), (unsigned)heads, (unsigned)N);
+  k_attention_simt<DV><<<grid, kRows * 32, smem, ctx().stream>>>(q, k, v, out, Sq, Skv, heads, kv_heads, (int)d,
+                                                                 causal ? 1 : 0, 1.0f / sqrtf((float)d));
+  check_launch("attention_simt");
+}
+
+}  // namespace
+
+void launch_attention_simt(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
+                           int64_t Skv, int heads, int kv_heads, int64_t d, bool causal) {
+  switch ((d + 31) / 32) {
+    case 1: return launch_simt<1>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 2: return launch_simt<2>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 3: return launch_simt<3>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 4: return launch_simt<4>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 5: return launch_simt<5>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 6: return launch_simt<6>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 7: return launch_simt<7>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    default: return launch_simt<8>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+  }
+}
+
+void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                      int heads, int kv_heads, int64_t d, bool causal) {
+  launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+}
+
+}  // namespace sdb

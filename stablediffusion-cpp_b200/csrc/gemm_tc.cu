@@ -1,0 +1,457 @@
+// gemm_tc.cu - the dense contraction C[M,N] = A[M,K] * B[N,K]^T on 5th-generation
+// tensor cores (sm_100a), the B200 replacement for the cuBLAS call inside the
+// reference's gemm_nt_bf16 / gemm_nt_f32 (backend_cuda.cu:453-477).
+//
+// Design
+//   * Persistent kernel, one CTA per SM, 192 threads in four roles:
+//       warp 0   TMA producer: streams 128-byte-wide K slices of A and B into a
+//                ring of shared-memory stages (128B swizzle), one mbarrier per stage
+//       warp 1   MMA issuer: allocates TMEM, issues tcgen05.mma (M=128, N=BN) from
+//                the stages into one of two TMEM accumulators, commits each stage
+//                back to the producer and each finished tile to the epilogue
+//       warps 2-5 epilogue: tcgen05.ld the accumulator (warp w owns TMEM lanes
+//                32*(w%4)...), apply bias / gated activation / accumulate and store
+//                with 16-byte vector stores; the TMEM buffer is released after the
+//                last load so the next tile's MMAs overlap this tile's stores
+//   * Operands: kind::f16 (bf16 x bf16) or kind::tf32 (fp32 x fp32), both K-major,
+//     fp32 accumulation in TMEM. 128 B of K per stage = 64 bf16 or 32 fp32.
+//   * Tiles are walked in groups of 16 M-blocks so that the CTAs running at the same
+//     time share A and B tiles through L2.
+//   * Edges: TMA zero-fills out-of-range rows/columns/K; the epilogue masks stores.
+//   * Every mbarrier wait is bounded (ptx.cuh): a stuck pipeline sets the device error
+//     word and the CTA drains and frees TMEM instead of hanging the GPU.
+#include <algorithm>
+#include <cstdio>
+#include <string>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sdb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles, num_tiles, k_blocks;
+  void* C;
+  long long ldc;
+  const float* bias;
+  int accumulate;
+  int epi;       // Epi
+  int out_bf16;  // store bf16 instead of fp32
+  int vec_ok;    // C base and ldc allow 16-byte stores
+  int* err;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = kBM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr uint32_t TMEM_COLS =
+      (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
+  const int per_group = kGroupM * n_tiles;
+  const int g = t / per_group;
+  const int first = g * kGroupM;
+  const int gs = min(m_tiles - first, kGroupM);
+  const int r = t - g * per_group;
+  mb = first + r % gs;
+  nb = r / gs;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+__device__ __forceinline__ float gelu_erf_f(float g) { return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f)); }
+
+// Stores 32 consecutive fp32 results of one row (columns col0..col0+31).
+__device__ __forceinline__ void store_row32(const GemmParams& p, int row, int col0, float (&v)[32]) {
+  if (p.out_bf16) {
+    uint16_t* c = reinterpret_cast<uint16_t*>(p.C) + (long long)row * p.ldc + col0;
+    if (p.vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(v[j], v[j + 1]);
+        w.y = pack_bf16x2(v[j + 2], v[j + 3]);
+        w.z = pack_bf16x2(v[j + 4], v[j + 5]);
+        w.w = pack_bf16x2(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(c + j) = w;
+      }
+    } else {
+      const int n = min(32, p.N - col0);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < n) c[j] = f32_to_bf16_rne(v[j]);
+    }
+    return;
+  }
+  float* c = reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + col0;
+  if (p.vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      if (p.accumulate) {
+        const float4 old = *reinterpret_cast<const float4*>(c + j);
+        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+      }
+      *reinterpret_cast<float4*>(c + j) = o;
+    }
+  } else {
+    const int n = min(32, p.N - col0);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n) c[j] = p.accumulate ? c[j] + v[j] : v[j];
+  }
+}
+
+// Stores 16 gated results (from 16 gate + 16 up columns) at output column ocol0.
+__device__ __forceinline__ void store_row16(const GemmParams& p, int row, int ocol0, const float (&y)[16]) {
+  const int on = p.N / 2;
+  if (p.out_bf16) {
+    uint16_t* c = reinterpret_cast<uint16_t*>(p.C) + (long long)row * p.ldc + ocol0;
+    if (p.vec_ok && ocol0 + 16 <= on) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(y[j], y[j + 1]);
+        w.y = pack_bf16x2(y[j + 2], y[j + 3]);
+        w.z = pack_bf16x2(y[j + 4], y[j + 5]);
+        w.w = pack_bf16x2(y[j + 6], y[j + 7]);
+        *reinterpret_cast<uint4*>(c + j) = w;
+      }
+    } else {
+      const int n = min(16, on - ocol0);
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < n) c[j] = f32_to_bf16_rne(y[j]);
+    }
+    return;
+  }
+  float* c = reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + ocol0;
+  if (p.vec_ok && ocol0 + 16 <= on) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(c + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+  } else {
+    const int n = min(16, on - ocol0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < n) c[j] = y[j];
+  }
+}
+
+template <int BN, bool TF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using C_ = Cfg<BN>;
+  constexpr int STAGES = C_::STAGES;
+  constexpr int ESZ = TF32 ? 4 : 2;
+  constexpr int BK = 128 / ESZ;        // K elements per stage (one swizzle row)
+  constexpr int KSTEPS = 4;            // MMAs per stage: 32 bytes of K each
+  constexpr uint32_t IDESC = make_idesc(TF32 ? 2u : 1u, 0, 0, kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C_::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C_::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* drain = acc_empty + 2;       // [1] MMA completion before TMEM is freed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;  // bit s: stage s has a load whose completion was not yet observed
+      uint32_t last_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+          tma_load_2d(sA + stage * C_::A_BYTES, &tmA, &full[stage], kb * BK, mb * kBM);
+          tma_load_2d(sB + stage * C_::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Aborted: wait (bounded) for this CTA's loads still in flight before exiting.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[s], (last_par >> s) & 1u))
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(p.err, kErrWaitDrain);
+                break;
+              }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C_::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * C_::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k) {
+            const uint64_t ad = sdesc_k_sw128(a0 + k * 32);
+            const uint64_t bd = sdesc_k_sw128(b0 + k * 32);
+            if (TF32)
+              umma_tf32_ss(d, ad, bd, IDESC, (kb | k) != 0);
+            else
+              umma_f16_ss(d, ad, bd, IDESC, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Every MMA this thread issued must have completed before TMEM is freed. In the
+      // normal path the epilogue already observed the last tile's commit; after an
+      // abort, wait (bounded) for a final commit.
+      umma_commit(drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kErrWaitDrain);
+          break;
+        }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int row = mb * kBM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the masked stores
+        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        const int col0 = nb * BN + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (p.bias) {
+          if (col0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+          }
+        }
+        if (p.epi == (int)Epi::kStore) {
+          store_row32(p, row, col0, v);
+        } else {
+          // Interleaved pairs: columns [16j, 16j+16) are gates (SwiGLU) / values
+          // (GEGLU) and [16j+16, 16j+32) the matching up / gate columns.
+          float y[16];
+          if (p.epi == (int)Epi::kSwiglu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = silu_f(v[j]) * v[16 + j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = v[j] * gelu_erf_f(v[16 + j]);
+          }
+          store_row16(p, row, col0 / 2, y);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // Teardown: all roles are done; the MMA thread has seen its final commit.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();  // lane 0 ran the MMA loop alone; dealloc is .sync.aligned
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+template <int BN, bool TF32>
+void launch_bn(const GemmCall& g, const GemmParams& p, int num_sms) {
+  using C_ = Cfg<BN>;
+  const int esz = TF32 ? 4 : 2;
+  const uint32_t bk = 128 / esz;
+  CUtensorMap ta, tb;
+  const CUtensorMapDataType dt = TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.M};
+    const uint64_t strides[1] = {(uint64_t)g.lda * esz};
+    const uint32_t box[2] = {bk, (uint32_t)kBM};
+    encode_tmap(&ta, dt, 2, g.A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.N};
+    const uint64_t strides[1] = {(uint64_t)g.ldb * esz};
+    const uint32_t box[2] = {bk, (uint32_t)BN};
+    encode_tmap(&tb, dt, 2, g.B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  auto kern = k_gemm_tc<BN, TF32>;
+  static bool attr_set[64] = {};
+  const int dev = ctx().device;
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM),
+               "cudaFuncSetAttribute(gemm)");
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(p.num_tiles, num_sms);
+  kern<<<grid, kThreads, C_::SMEM, ctx().stream>>>(ta, tb, p);
+  check_launch("gemm_tc");
+}
+
+int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
+  (void)epi;  // every candidate BN is a multiple of the 32-column gated chunk
+  const int cands[4] = {256, 192, 128, 64};
+  int best = 256;
+  double best_cost = 1e30;
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  for (int bn : cands) {
+    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + num_sms - 1) / num_sms;
+    // Per-tile time grows with BN; 48 columns of fixed cost model the lower
+    // efficiency of narrow tiles (more A traffic per FLOP, more epilogue overhead).
+    const double cost = (double)waves * (bn + 48);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+// Tile-width override for tuning and tests (0 = automatic choice).
+static int g_forced_bn = 0;
+void set_gemm_tile(int bn) { g_forced_bn = bn; }
+
+void launch_gemm_tc(const GemmCall& g) {
+  DeviceContext& c = ctx();
+  GemmParams p{};
+  p.M = (int)g.M;
+  p.N = (int)g.N;
+  p.K = (int)g.K;
+  const int bn = g.bn ? g.bn : g_forced_bn ? g_forced_bn : choose_bn(g.M, g.N, c.num_sms, g.epi);
+  p.m_tiles = (int)((g.M + kBM - 1) / kBM);
+  p.n_tiles = (int)((g.N + bn - 1) / bn);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  const int bk = g.tf32 ? 32 : 64;
+  p.k_blocks = (int)((g.K + bk - 1) / bk);
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.bias = g.bias;
+  p.accumulate = g.accumulate ? 1 : 0;
+  p.epi = (int)g.epi;
+  p.out_bf16 = g.out_bf16 ? 1 : 0;
+  const int oesz = g.out_bf16 ? 2 : 4;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * oesz) % 16 == 0);
+  p.err = c.err_word;
+  if (g.tf32) {
+    switch (bn) {
+      case 256: launch_bn<256, true>(g, p, c.num_sms); break;
+      case 192: launch_bn<192, true>(g, p, c.num_sms); break;
+      case 128: launch_bn<128, true>(g, p, c.num_sms); break;
+      default: launch_bn<64, true>(g, p, c.num_sms); break;
+    }
+  } else {
+    switch (bn) {
+      case 256: launch_bn<256, false>(g, p, c.num_sms); break;
+      case 192: launch_bn<192, false>(g, p, c.num_sms); break;
+      case 128: launch_bn<128, false>(g, p, c.num_sms); break;
+      default: launch_bn<64, false>(g, p, c.num_sms); break;
+    }
+  }
+}
+
+}  // namespace sdb

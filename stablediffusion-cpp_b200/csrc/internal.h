@@ -1,0 +1,110 @@
+// internal.h - state shared by the library's translation units: the per-device
+// context (stream, SM count, device error word, workspace), the thread-local error
+// message, and the launch entry points each kernel file exports to runtime.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace sdb {
+
+// Thrown inside the library; the C-ABI boundary converts it to a status code plus a
+// message readable through sdb200_last_error().
+struct Error {
+  int code;
+  std::string msg;
+};
+[[noreturn]] void fail(int code, const std::string& msg);
+void check_cuda(cudaError_t e, const char* what);
+// Checks the launch status of the last kernel (does not synchronise).
+void check_launch(const char* what);
+
+// Status codes of the C ABI.
+enum : int {
+  kOk = 0,
+  kErrInvalidArg = 1,   // bad size, leading dimension, alignment or null pointer
+  kErrNoDevice = 2,     // no CUDA device / driver
+  kErrCuda = 3,         // a CUDA runtime call failed
+  kErrDeviceWait = 4,   // a kernel's bounded wait expired (device error word set)
+  kErrOutOfMemory = 5,
+  kErrUnsupported = 6,
+};
+
+struct DeviceContext {
+  int device = -1;
+  int num_sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t total_mem = 0;
+  std::string name;
+  cudaStream_t stream = nullptr;   // stream every op of this device is issued on
+  int* err_word = nullptr;         // device int, OR-ed by kernels on bounded-wait expiry
+  // Workspace for operand packing (grown on demand, never shrunk). Ops on one stream
+  // run in order, so one workspace per context is safe.
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+};
+
+// Context of the calling thread's current device (created on first use).
+DeviceContext& ctx();
+// Returns a workspace pointer of at least `bytes` bytes (256-byte aligned).
+void* workspace(size_t bytes);
+// Encodes a 2-D/3-D tiled tensor map through the driver entry point.
+void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
+// ------------------------------------------------------------------------------
+// Kernel entry points (host launchers). All take device pointers, validate their
+// arguments, enqueue on ctx().stream and return without synchronising.
+// ------------------------------------------------------------------------------
+// GEMM core: C[M,N] = A[M,K] * B[N,K]^T (+bias[N]) (+C if accumulate).
+// a_bf16/b_bf16 select the operand types: bf16 x bf16 -> kind::f16,
+// fp32 x fp32 -> kind::tf32. Pointers must be 16-byte aligned and leading dimensions
+// (in elements) must give 16-byte multiples; the callers in gemm_api.cu repack
+// operands that do not.
+enum class Epi : int {
+  kStore = 0,      // C = acc (+bias) (+C)
+  kSwiglu = 1,     // columns interleaved gate/up per 16: Y[m, n/2] = silu(g) * u
+  kGeglu = 2,      // columns interleaved value/gate per 16: Y[m, n/2] = v * gelu_erf(g)
+};
+struct GemmCall {
+  int64_t M, N, K;
+  const void* A;
+  int64_t lda;      // elements
+  const void* B;
+  int64_t ldb;      // elements
+  void* C;
+  int64_t ldc;      // elements of the output type
+  const float* bias;
+  bool accumulate;
+  bool tf32;        // operands fp32 (kind::tf32) instead of bf16
+  Epi epi;
+  bool out_bf16;    // store C as bf16 (ldc in bf16 elements); no accumulate
+  int bn;           // 0 = choose
+};
+void launch_gemm_tc(const GemmCall& g);
+// Forces the tile width of later launch_gemm_tc calls (0 = automatic).
+void set_gemm_tile(int bn);
+// Small-M (M <= 16) GEMM through a memory-bound SIMT kernel (weights streamed once).
+void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
+                        bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate);
+
+// fp32 [rows, cols] (ld) -> bf16 [rows, cols] (ldo), RNE as the reference rounds.
+void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols);
+// Strided 2-D copy of 16-bit or 32-bit elements into a dense destination.
+void launch_copy2d(const void* src, int64_t ld, void* dst, int64_t ldo, int64_t rows, int64_t cols, int esize);
+// C[m, n] = bias[n] (or += when accumulate), used when K == 0.
+void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, bool accumulate);
+
+// Attention (attention.cu).
+void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                      int heads, int kv_heads, int64_t d, bool causal);
+// Attention on bf16 operands already laid out [N, heads, S, dp] (dp = padded head dim).
+void launch_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out, int64_t out_ld,
+                           int64_t N, int64_t Sq, int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp,
+                           bool causal, float scale, bool out_bf16);
+
+}  // namespace sdb

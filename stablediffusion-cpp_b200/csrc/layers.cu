@@ -1,0 +1,594 @@
+// layers.cu - the memory-bound kernels of the backend: operand packing for the
+// tensor-core GEMM, the small-M GEMM, and every layer / elementwise / layout op of
+// the reference backend API (backend_cuda.h:45-80) that is not a contraction.
+//
+// These are HBM-bound (a few flops per byte), so they are written as plain SIMT
+// kernels: 16-byte vector loads/stores where the layout allows, grids sized in
+// multiples of the SM count, fp32 warp-shuffle reductions. Numerics follow the
+// reference CPU loops in tensor.cpp (cited per kernel); reductions that the CPU
+// does in double are done here in fp32 tree order, well inside the reference's own
+// GPU-vs-CPU tolerances (test_ops.cpp:356-477).
+#include <algorithm>
+#include <cmath>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sdb {
+namespace {
+
+constexpr int kT = 256;
+
+unsigned grid_for(int64_t n, int per_thread = 1) {
+  const int64_t blocks = (n / per_thread + kT - 1) / kT;
+  const int64_t cap = (int64_t)std::max(1, ctx().num_sms) * 16;
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, cap));
+}
+
+#define GRID_STRIDE(i, n) \
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (int64_t)gridDim.x * blockDim.x)
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Block-wide sum; every thread gets the result. `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : -INFINITY;
+  t = warp_max(t);
+  return t;
+}
+
+// ---------------------------------------------------------------------------------
+// Packing
+// ---------------------------------------------------------------------------------
+// fp32 -> bf16 (reference rounding), 8 elements per thread when rows allow it.
+__global__ void k_pack_bf16_vec(const float* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
+                                int64_t rows, int64_t cols8) {
+  GRID_STRIDE(i, rows * cols8) {
+    const int64_t r = i / cols8, c = (i - r * cols8) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(src + r * ld + c);
+    const float4 b = *reinterpret_cast<const float4*>(src + r * ld + c + 4);
+    uint4 o;
+    o.x = pack_bf16x2(a.x, a.y);
+    o.y = pack_bf16x2(a.z, a.w);
+    o.z = pack_bf16x2(b.x, b.y);
+    o.w = pack_bf16x2(b.z, b.w);
+    *reinterpret_cast<uint4*>(dst + r * ldo + c) = o;
+  }
+}
+__global__ void k_pack_bf16(const float* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
+                            int64_t rows, int64_t cols) {
+  GRID_STRIDE(i, rows * cols) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[r * ldo + c] = f32_to_bf16_rne(src[r * ld + c]);
+  }
+}
+// fp32 -> fp32 rounded to the tf32 grid (10 explicit mantissa bits, nearest even), so
+// that kind::tf32 sees an unbiased operand whatever the hardware does with low bits.
+__device__ __forceinline__ float round_tf32(float f) {
+  uint32_t b = __float_as_uint(f);
+  if ((b & 0x7F800000u) == 0x7F800000u) return f;
+  b += 0xFFFu + ((b >> 13) & 1u);
+  return __uint_as_float(b & 0xFFFFE000u);
+}
+__global__ void k_pack_tf32(const float* __restrict__ src, int64_t ld, float* __restrict__ dst, int64_t ldo,
+                            int64_t rows, int64_t cols) {
+  GRID_STRIDE(i, rows * cols) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[r * ldo + c] = round_tf32(src[r * ld + c]);
+  }
+}
+__global__ void k_copy2d_16(const uint16_t* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
+                            int64_t rows, int64_t cols) {
+  GRID_STRIDE(i, rows * cols) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[r * ldo + c] = src[r * ld + c];
+  }
+}
+__global__ void k_copy2d_32(const float* __restrict__ src, int64_t ld, float* __restrict__ dst, int64_t ldo,
+                            int64_t rows, int64_t cols) {
+  GRID_STRIDE(i, rows * cols) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[r * ldo + c] = src[r * ld + c];
+  }
+}
+__global__ void k_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, int acc) {
+  GRID_STRIDE(i, M * N) {
+    const int64_t r = i / N, c = i - r * N;
+    const float b = bias ? bias[c] : 0.0f;
+    float* p = C + r * ldc + c;
+    *p = acc ? *p + b : b;
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Small-M GEMM: C[M,N] = A[M,K] B[N,K]^T (+bias) (+C), M <= 16, A staged in shared
+// memory, each warp streams whole rows of B (the weights) once. HBM-bound on B.
+// ---------------------------------------------------------------------------------
+template <bool BF16>
+__global__ void __launch_bounds__(256) k_gemm_skinny(int M, int N, int K, const float* __restrict__ A, int64_t lda,
+                                                     const void* __restrict__ Bv, int64_t ldb, float* __restrict__ C,
+                                                     int64_t ldc, const float* __restrict__ bias, int acc, int vec) {
+  extern __shared__ float sa[];  // [M][K]
+  for (int i = threadIdx.x; i < M * K; i += blockDim.x) sa[i] = A[(int64_t)(i / K) * lda + (i % K)];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int64_t w0 = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5);
+  const int64_t wstep = (int64_t)gridDim.x * wpb;
+  for (int64_t n = w0; n < N; n += wstep) {
+    float s[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) s[m] = 0.0f;
+    int k0 = 0;
+    if (BF16) {
+      const uint16_t* b = reinterpret_cast<const uint16_t*>(Bv) + n * ldb;
+      if (vec) {
+        const int kv = K & ~255;
+        for (int k = lane * 8; k < kv; k += 256) {
+          const uint4 w = __ldg(reinterpret_cast<const uint4*>(b + k));
+          float bf[8];
+          bf[0] = __uint_as_float(w.x << 16); bf[1] = __uint_as_float(w.x & 0xFFFF0000u);
+          bf[2] = __uint_as_float(w.y << 16); bf[3] = __uint_as_float(w.y & 0xFFFF0000u);
+          bf[4] = __uint_as_float(w.z << 16); bf[5] = __uint_as_float(w.z & 0xFFFF0000u);
+          bf[6] = __uint_as_float(w.w << 16); bf[7] = __uint_as_float(w.w & 0xFFFF0000u);
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            if (m < M) {
+              const float* a = sa + m * K + k;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) s[m] = fmaf(a[j], bf[j], s[m]);
+            }
+        }
+        k0 = kv;
+      }
+      for (int k = k0 + lane; k < K; k += 32) {
+        const float bf = bf16_to_f32(b[k]);
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < M) s[m] = fmaf(sa[m * K + k], bf, s[m]);
+      }
+    } else {
+      const float* b = reinterpret_cast<const float*>(Bv) + n * ldb;
+      if (vec) {
+        const int kv = K & ~127;
+        for (int k = lane * 4; k < kv; k += 128) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(b + k));
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            if (m < M) {
+              const float* a = sa + m * K + k;
+              s[m] = fmaf(a[0], w.x, s[m]);
+              s[m] = fmaf(a[1], w.y, s[m]);
+              s[m] = fmaf(a[2], w.z, s[m]);
+              s[m] = fmaf(a[3], w.w, s[m]);
+            }
+        }
+        k0 = kv;
+      }
+      for (int k = k0 + lane; k < K; k += 32) {
+        const float bf = b[k];
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+          if (m < M) s[m] = fmaf(sa[m * K + k], bf, s[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      if (m < M) {
+        const float t = warp_sum(s[m]);
+        if (lane == 0) {
+          float* c = C + (int64_t)m * ldc + n;
+          const float v = t + (bias ? bias[n] : 0.0f);
+          *c = acc ? *c + v : v;
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Norms (tensor.cpp:588-679, :681-699)
+// ---------------------------------------------------------------------------------
+// GroupNorm: one block per (sample, group); two passes (mean, then variance), as the
+// reference CPU path does in double (tensor.cpp:603-624).
+__global__ void k_group_norm(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t HW, int groups,
+                             const float* __restrict__ gamma, const float* __restrict__ beta, float eps) {
+  __shared__ float red[32];
+  const int64_t n = blockIdx.x / groups, g = blockIdx.x % groups, cg = C / groups, len = cg * HW;
+  const float* p = x + (n * C + g * cg) * HW;
+  float* q = y + (n * C + g * cg) * HW;
+  float s = 0.0f;
+  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) s += p[i];
+  const float mean = block_sum(s, red) / (float)len;
+  float v = 0.0f;
+  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
+    const float d = p[i] - mean;
+    v += d * d;
+  }
+  const float var = block_sum(v, red) / (float)len;
+  const float rstd = rsqrtf(var + eps);
+  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
+    const int64_t ch = g * cg + i / HW;
+    const float a = rstd * gamma[ch];
+    q[i] = p[i] * a + (beta[ch] - mean * a);
+  }
+}
+// LayerNorm / RMSNorm over rows of C (tensor.cpp:628-679).
+__global__ void k_row_norm(const float* __restrict__ x, float* __restrict__ y, int64_t C, const float* __restrict__ gamma,
+                           const float* __restrict__ beta, float eps, int rms) {
+  __shared__ float red[32];
+  const float* p = x + (int64_t)blockIdx.x * C;
+  float* q = y + (int64_t)blockIdx.x * C;
+  float mean = 0.0f;
+  if (!rms) {
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < C; i += blockDim.x) s += p[i];
+    mean = block_sum(s, red) / (float)C;
+  }
+  float v = 0.0f;
+  for (int64_t i = threadIdx.x; i < C; i += blockDim.x) {
+    const float d = p[i] - mean;
+    v += d * d;
+  }
+  const float rstd = rsqrtf(block_sum(v, red) / (float)C + eps);
+  for (int64_t i = threadIdx.x; i < C; i += blockDim.x) {
+    float o = (p[i] - mean) * rstd;
+    if (gamma) o *= gamma[i];
+    if (beta) o += beta[i];
+    q[i] = o;
+  }
+}
+// Per-head RMSNorm in place: one warp per group of `dim` values (tensor.cpp:681-699).
+__global__ void k_rms_norm_heads(float* __restrict__ x, int64_t groups, int64_t dim, const float* __restrict__ gamma,
+                                 float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= groups) return;
+  float* p = x + w * dim;
+  float s = 0.0f;
+  for (int64_t i = lane; i < dim; i += 32) s += p[i] * p[i];
+  const float rstd = rsqrtf(warp_sum(s) / (float)dim + eps);
+  for (int64_t i = lane; i < dim; i += 32) p[i] = p[i] * rstd * (gamma ? gamma[i] : 1.0f);
+}
+
+// RoPE in place on x [N*S, inner], tables [S, dim] (tensor.cpp:701-730).
+__global__ void k_rope(float* __restrict__ x, int64_t NS, int64_t S, int64_t inner, int64_t dim,
+                       const float* __restrict__ cs, const float* __restrict__ sn, int interleaved) {
+  const int64_t half = dim / 2, heads = inner / dim;
+  GRID_STRIDE(i, NS * heads * half) {
+    const int64_t ns = i / (heads * half), rem = i - ns * heads * half, h = rem / half, j = rem - h * half;
+    const int64_t s = ns % S;
+    float* p = x + ns * inner + h * dim;
+    const float* c = cs + s * dim;
+    const float* sv = sn + s * dim;
+    if (interleaved) {
+      const int64_t a = 2 * j;
+      const float u = p[a], w = p[a + 1];
+      p[a] = u * c[a] - w * sv[a];
+      p[a + 1] = w * c[a] + u * sv[a];
+    } else {
+      const float u = p[j], w = p[j + half];
+      p[j] = u * c[j] - w * sv[j];
+      p[j + half] = w * c[j + half] + u * sv[j + half];
+    }
+  }
+}
+
+// Scaled, max-subtracted softmax per row; causal rows keep (r % rows_per_head) + 1
+// entries and zero the rest (tensor.cpp:752-769).
+__global__ void k_softmax_rows(float* __restrict__ x, int64_t cols, float scale, int causal, int64_t rows_per_head) {
+  __shared__ float red[32];
+  float* p = x + (int64_t)blockIdx.x * cols;
+  const int64_t r = (int64_t)blockIdx.x % rows_per_head;
+  const int64_t valid = causal ? min(cols, r + 1) : cols;
+  float m = -INFINITY;
+  for (int64_t j = threadIdx.x; j < valid; j += blockDim.x) m = fmaxf(m, p[j] * scale);
+  m = block_max(m, red);
+  float s = 0.0f;
+  for (int64_t j = threadIdx.x; j < valid; j += blockDim.x) {
+    const float e = expf(p[j] * scale - m);
+    p[j] = e;
+    s += e;
+  }
+  const float inv = 1.0f / block_sum(s, red);
+  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) p[j] = j < valid ? p[j] * inv : 0.0f;
+}
+
+// ---------------------------------------------------------------------------------
+// Activations and elementwise (tensor.cpp:732-748, :813-935)
+// ---------------------------------------------------------------------------------
+__global__ void k_geglu(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t D) {
+  GRID_STRIDE(i, rows * D) {
+    const int64_t r = i / D, c = i - r * D;
+    const float a = x[r * 2 * D + c], g = x[r * 2 * D + D + c];
+    y[i] = a * 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+  }
+}
+__global__ void k_swiglu(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ y, int64_t n) {
+  GRID_STRIDE(i, n) y[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+}
+__global__ void k_unary(float* __restrict__ x, int64_t n, int op) {
+  GRID_STRIDE(i, n) {
+    const float v = x[i];
+    float o;
+    switch (op) {
+      case 0: o = v / (1.0f + expf(-v)); break;                               // silu
+      case 1: o = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); break;  // gelu (erf)
+      case 2: o = v / (1.0f + expf(-1.702f * v)); break;                       // quick_gelu
+      default: o = tanhf(v); break;                                            // tanh
+    }
+    x[i] = o;
+  }
+}
+__global__ void k_add(float* __restrict__ a, const float* __restrict__ b, int64_t n) { GRID_STRIDE(i, n) a[i] += b[i]; }
+__global__ void k_affine(float* __restrict__ x, float a, float b, int64_t n) { GRID_STRIDE(i, n) x[i] = x[i] * a + b; }
+__global__ void k_mul_rows(float* __restrict__ x, const float* __restrict__ v, int64_t n, int64_t dim) {
+  GRID_STRIDE(i, n) x[i] *= v[i % dim];
+}
+__global__ void k_add_rows_scaled(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ g,
+                                  int64_t n, int64_t dim) {
+  GRID_STRIDE(i, n) x[i] += g[i % dim] * y[i];
+}
+__global__ void k_add_channel_bias(float* __restrict__ x, const float* __restrict__ b, int64_t n, int64_t HW) {
+  GRID_STRIDE(i, n) x[i] += b[i / HW];
+}
+__global__ void k_add_bias_rows(float* __restrict__ C, int64_t ldc, int64_t M, int64_t N, const float* __restrict__ b) {
+  GRID_STRIDE(i, M * N) {
+    const int64_t r = i / N, c = i - r * N;
+    C[r * ldc + c] += b[r];
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Layout ops (tensor.cpp:936-1090)
+// ---------------------------------------------------------------------------------
+__global__ void k_upsample2x(const float* __restrict__ x, float* __restrict__ y, int64_t NC, int64_t H, int64_t W) {
+  GRID_STRIDE(i, NC * 4 * H * W) {
+    const int64_t W2 = 2 * W, H2 = 2 * H;
+    const int64_t nc = i / (H2 * W2), rem = i - nc * H2 * W2, yy = rem / W2, xx = rem - yy * W2;
+    y[i] = x[(nc * H + yy / 2) * W + xx / 2];
+  }
+}
+__global__ void k_concat_channels(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
+                                  int64_t N, int64_t Ca, int64_t Cb, int64_t HW) {
+  GRID_STRIDE(i, N * (Ca + Cb) * HW) {
+    const int64_t C = Ca + Cb, n = i / (C * HW), rem = i - n * C * HW, c = rem / HW, s = rem - c * HW;
+    y[i] = c < Ca ? a[(n * Ca + c) * HW + s] : b[(n * Cb + (c - Ca)) * HW + s];
+  }
+}
+__global__ void k_nchw_to_nlc(const float* __restrict__ x, float* __restrict__ y, int64_t N, int64_t C, int64_t HW) {
+  GRID_STRIDE(i, N * C * HW) {  // i indexes y [N, HW, C]
+    const int64_t n = i / (HW * C), rem = i - n * HW * C, s = rem / C, c = rem - s * C;
+    y[i] = x[(n * C + c) * HW + s];
+  }
+}
+__global__ void k_nlc_to_nchw(const float* __restrict__ x, float* __restrict__ y, int64_t N, int64_t C, int64_t HW) {
+  GRID_STRIDE(i, N * C * HW) {  // i indexes y [N, C, HW]
+    const int64_t n = i / (C * HW), rem = i - n * C * HW, c = rem / HW, s = rem - c * HW;
+    y[i] = x[(n * HW + s) * C + c];
+  }
+}
+__global__ void k_patchify(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t H, int64_t W, int p) {
+  const int64_t Wt = W / p, F = (int64_t)p * p * C;
+  GRID_STRIDE(idx, C * H * W) {  // idx indexes the image [C, H, W]
+    const int64_t c = idx / (H * W), hh = (idx / W) % H, ww = idx % W;
+    const int64_t h = hh / p, ph = hh % p, w = ww / p, pw = ww % p;
+    y[(h * Wt + w) * F + (ph * p + pw) * C + c] = x[idx];
+  }
+}
+__global__ void k_unpatchify(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t H, int64_t W,
+                             int p) {
+  const int64_t Wt = W / p, F = (int64_t)p * p * C;
+  GRID_STRIDE(idx, C * H * W) {
+    const int64_t c = idx / (H * W), hh = (idx / W) % H, ww = idx % W;
+    const int64_t h = hh / p, ph = hh % p, w = ww / p, pw = ww % p;
+    y[idx] = x[(h * Wt + w) * F + (ph * p + pw) * C + c];
+  }
+}
+// im2col rows for pixels p0..p0+P-1: cols[p, (ci, ky, kx)] (tensor.cpp:551-575).
+__global__ void k_im2col(const float* __restrict__ x, float* __restrict__ cols, int64_t Cin, int64_t H, int64_t W,
+                         int64_t kh, int64_t kw, int64_t Wo, int stride, int pad, int64_t p0, int64_t P, int64_t K,
+                         int64_t ldk) {
+  GRID_STRIDE(i, P * K) {
+    const int64_t p = i / K, k = i - p * K;
+    const int64_t ci = k / (kh * kw), r = k - ci * kh * kw, ky = r / kw, kx = r - ky * kw;
+    const int64_t oy = (p0 + p) / Wo, ox = (p0 + p) % Wo;
+    const int64_t iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+    cols[p * ldk + k] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? x[(ci * H + iy) * W + ix] : 0.0f;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------------
+void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return;
+  const bool vec = (cols % 8 == 0) && (ld % 4 == 0) && (ldo % 8 == 0) && ((uintptr_t)src % 16 == 0) &&
+                   ((uintptr_t)dst % 16 == 0);
+  if (vec)
+    k_pack_bf16_vec<<<grid_for(rows * cols, 8), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols / 8);
+  else
+    k_pack_bf16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
+  check_launch("pack_bf16");
+}
+void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return;
+  k_pack_tf32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
+  check_launch("pack_tf32");
+}
+void launch_copy2d(const void* src, int64_t ld, void* dst, int64_t ldo, int64_t rows, int64_t cols, int esize) {
+  if (rows <= 0 || cols <= 0) return;
+  if (esize == 2)
+    k_copy2d_16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>((const uint16_t*)src, ld, (uint16_t*)dst, ldo, rows,
+                                                                 cols);
+  else
+    k_copy2d_32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>((const float*)src, ld, (float*)dst, ldo, rows, cols);
+  check_launch("copy2d");
+}
+void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, bool accumulate) {
+  if (M <= 0 || N <= 0) return;
+  k_bias_fill<<<grid_for(M * N), kT, 0, ctx().stream>>>(C, ldc, M, N, bias, accumulate ? 1 : 0);
+  check_launch("bias_fill");
+}
+void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
+                        bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate) {
+  const size_t smem = (size_t)(M * K) * sizeof(float);
+  const int wpb = 8;
+  const int64_t blocks = std::min<int64_t>((N + wpb - 1) / wpb, (int64_t)ctx().num_sms * 8);
+  if (b_bf16) {
+    const bool vec = (ldb % 8 == 0) && ((uintptr_t)B % 16 == 0);
+    if (smem > 48 * 1024)
+      check_cuda(cudaFuncSetAttribute(k_gemm_skinny<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "skinny attr");
+    k_gemm_skinny<true><<<(unsigned)blocks, wpb * 32, smem, ctx().stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C,
+                                                                            ldc, bias, accumulate, vec);
+  } else {
+    const bool vec = (ldb % 4 == 0) && ((uintptr_t)B % 16 == 0);
+    if (smem > 48 * 1024)
+      check_cuda(cudaFuncSetAttribute(k_gemm_skinny<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "skinny attr");
+    k_gemm_skinny<false><<<(unsigned)blocks, wpb * 32, smem, ctx().stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C,
+                                                                             ldc, bias, accumulate, vec);
+  }
+  check_launch("gemm_skinny");
+}
+
+// Public layer ops (called from runtime.cu's C ABI after argument checks).
+void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                   const float* beta, float eps) {
+  if (N <= 0 || C <= 0 || HW <= 0) return;
+  k_group_norm<<<(unsigned)(N * groups), 512, 0, ctx().stream>>>(x, y, C, HW, groups, gamma, beta, eps);
+  check_launch("group_norm");
+}
+void op_row_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta, float eps,
+                 bool rms) {
+  if (rows <= 0) return;
+  k_row_norm<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, y, C, gamma, beta, eps, rms ? 1 : 0);
+  check_launch(rms ? "rms_norm" : "layer_norm");
+}
+void op_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma, float eps) {
+  if (groups <= 0) return;
+  const int64_t blocks = (groups + 7) / 8;
+  k_rms_norm_heads<<<(unsigned)blocks, kT, 0, ctx().stream>>>(x, groups, dim, gamma, eps);
+  check_launch("rms_norm_heads");
+}
+void op_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const float* cs, const float* sn,
+             bool interleaved) {
+  const int64_t total = N * S * (inner / dim) * (dim / 2);
+  if (total <= 0) return;
+  k_rope<<<grid_for(total), kT, 0, ctx().stream>>>(x, N * S, S, inner, dim, cs, sn, interleaved ? 1 : 0);
+  check_launch("rope");
+}
+void op_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, bool causal, int64_t rows_per_head) {
+  if (rows <= 0) return;
+  k_softmax_rows<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, cols, scale, causal ? 1 : 0, rows_per_head);
+  check_launch("softmax_rows");
+}
+void op_geglu(const float* x, float* y, int64_t rows, int64_t D) {
+  if (rows * D <= 0) return;
+  k_geglu<<<grid_for(rows * D), kT, 0, ctx().stream>>>(x, y, rows, D);
+  check_launch("geglu");
+}
+void op_swiglu(const float* g, const float* u, float* y, int64_t n) {
+  if (n <= 0) return;
+  k_swiglu<<<grid_for(n), kT, 0, ctx().stream>>>(g, u, y, n);
+  check_launch("swiglu");
+}
+void op_unary(float* x, int64_t n, int op) {
+  if (n <= 0) return;
+  k_unary<<<grid_for(n), kT, 0, ctx().stream>>>(x, n, op);
+  check_launch("unary");
+}
+void op_add(float* a, const float* b, int64_t n) {
+  if (n <= 0) return;
+  k_add<<<grid_for(n), kT, 0, ctx().stream>>>(a, b, n);
+  check_launch("add");
+}
+void op_affine(float* x, float a, float b, int64_t n) {
+  if (n <= 0) return;
+  k_affine<<<grid_for(n), kT, 0, ctx().stream>>>(x, a, b, n);
+  check_launch("affine");
+}
+void op_mul_rows(float* x, const float* v, int64_t rows, int64_t dim) {
+  if (rows * dim <= 0) return;
+  k_mul_rows<<<grid_for(rows * dim), kT, 0, ctx().stream>>>(x, v, rows * dim, dim);
+  check_launch("mul_rows");
+}
+void op_add_rows_scaled(float* x, const float* y, const float* g, int64_t rows, int64_t dim) {
+  if (rows * dim <= 0) return;
+  k_add_rows_scaled<<<grid_for(rows * dim), kT, 0, ctx().stream>>>(x, y, g, rows * dim, dim);
+  check_launch("add_rows_scaled");
+}
+void op_add_channel_bias(float* x, const float* b, int64_t N, int64_t C, int64_t HW) {
+  if (N * C * HW <= 0) return;
+  k_add_channel_bias<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, b, N * C * HW, HW);
+  check_launch("add_channel_bias");
+}
+void op_add_bias_rows(float* C, int64_t ldc, int64_t M, int64_t N, const float* b) {
+  if (M * N <= 0) return;
+  k_add_bias_rows<<<grid_for(M * N), kT, 0, ctx().stream>>>(C, ldc, M, N, b);
+  check_launch("add_bias_rows");
+}
+void op_upsample2x(const float* x, float* y, int64_t NC, int64_t H, int64_t W) {
+  if (NC * H * W <= 0) return;
+  k_upsample2x<<<grid_for(NC * 4 * H * W), kT, 0, ctx().stream>>>(x, y, NC, H, W);
+  check_launch("upsample_nearest2x");
+}
+void op_concat_channels(const float* a, const float* b, float* y, int64_t N, int64_t Ca, int64_t Cb, int64_t HW) {
+  if (N * (Ca + Cb) * HW <= 0) return;
+  k_concat_channels<<<grid_for(N * (Ca + Cb) * HW), kT, 0, ctx().stream>>>(a, b, y, N, Ca, Cb, HW);
+  check_launch("concat_channels");
+}
+void op_nchw_to_nlc(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
+  if (N * C * HW <= 0) return;
+  k_nchw_to_nlc<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, y, N, C, HW);
+  check_launch("nchw_to_nlc");
+}
+void op_nlc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
+  if (N * C * HW <= 0) return;
+  k_nlc_to_nchw<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, y, N, C, HW);
+  check_launch("nlc_to_nchw");
+}
+void op_patchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
+  if (C * H * W <= 0) return;
+  k_patchify<<<grid_for(C * H * W), kT, 0, ctx().stream>>>(x, y, C, H, W, p);
+  check_launch("patchify");
+}
+void op_unpatchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
+  if (C * H * W <= 0) return;
+  k_unpatchify<<<grid_for(C * H * W), kT, 0, ctx().stream>>>(x, y, C, H, W, p);
+  check_launch("unpatchify");
+}
+void op_im2col(const float* x, float* cols, int64_t Cin, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t Wo,
+               int stride, int pad, int64_t p0, int64_t P, int64_t K, int64_t ldk) {
+  if (P * K <= 0) return;
+  k_im2col<<<grid_for(P * K), kT, 0, ctx().stream>>>(x, cols, Cin, H, W, kh, kw, Wo, stride, pad, p0, P, K, ldk);
+  check_launch("im2col");
+}
+
+}  // namespace sdb

@@ -1,0 +1,365 @@
+// ops_api.cu - the compute half of the C ABI (sdb200.h): argument validation, operand
+// preparation for the tensor-core GEMM, path selection, and the layer ops.
+//
+// GEMM path selection (gemm_nt_bf16 / gemm_nt_f32, backend_cuda.cu:453-477):
+//   K == 0         C = bias (or C += bias)          - no contraction
+//   M <= 16        memory-bound SIMT kernel, exact fp32 A (weights streamed once)
+//   otherwise      tcgen05 GEMM (gemm_tc.cu). A fp32 is packed to bf16 (bf16 path,
+//                  the reference's rounding) or rounded to tf32 (fp32 path) in the
+//                  workspace with 16-byte-aligned rows; B is used in place when its
+//                  base and row pitch meet TMA's 16-byte rule, else packed too.
+#include <algorithm>
+#include <cmath>
+#include <string>
+
+#include "internal.h"
+#include "sdb200.h"
+
+namespace sdb {
+void set_last_error(const std::string& s);
+void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
+void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float);
+void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const float*, float, bool);
+void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
+void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);
+void op_softmax_rows(float*, int64_t, int64_t, float, bool, int64_t);
+void op_geglu(const float*, float*, int64_t, int64_t);
+void op_swiglu(const float*, const float*, float*, int64_t);
+void op_unary(float*, int64_t, int);
+void op_add(float*, const float*, int64_t);
+void op_affine(float*, float, float, int64_t);
+void op_mul_rows(float*, const float*, int64_t, int64_t);
+void op_add_rows_scaled(float*, const float*, const float*, int64_t, int64_t);
+void op_add_channel_bias(float*, const float*, int64_t, int64_t, int64_t);
+void op_add_bias_rows(float*, int64_t, int64_t, int64_t, const float*);
+void op_upsample2x(const float*, float*, int64_t, int64_t, int64_t);
+void op_concat_channels(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t);
+void op_nchw_to_nlc(const float*, float*, int64_t, int64_t, int64_t);
+void op_nlc_to_nchw(const float*, float*, int64_t, int64_t, int64_t);
+void op_patchify(const float*, float*, int64_t, int64_t, int64_t, int);
+void op_unpatchify(const float*, float*, int64_t, int64_t, int64_t, int);
+void op_im2col(const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int, int, int64_t, int64_t,
+               int64_t, int64_t);
+
+namespace {
+
+constexpr int64_t kMaxDim = (int64_t)1 << 31;
+
+void require(bool ok, const char* op, const std::string& what) {
+  if (!ok) fail(kErrInvalidArg, std::string(op) + ": " + what);
+}
+void require_ptr(const void* p, const char* op, const char* name) {
+  if (!p) fail(kErrInvalidArg, std::string(op) + ": null pointer " + name);
+}
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+inline size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+void check_gemm_args(const char* op, int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                     int64_t ldb, const void* C, int64_t ldc) {
+  require(M < kMaxDim && N < kMaxDim && K < kMaxDim, op, "dimension >= 2^31");
+  require(K >= 0, op, "K < 0");
+  require_ptr(C, op, "C");
+  require(ldc >= N, op, "ldc < N");
+  if (K > 0) {
+    require_ptr(A, op, "A");
+    require_ptr(B, op, "B");
+    require(lda >= K, op, "lda < K");
+    require(ldb >= K, op, "ldb < K");
+  }
+  require((reinterpret_cast<uintptr_t>(C) & 3) == 0, op, "C not 4-byte aligned");
+}
+
+// bf16 x bf16 GEMM with A either fp32 (packed here) or bf16.
+void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
+                    int64_t ldb, void* C, int64_t ldc, bool c_bf16, const float* bias, bool acc, Epi epi) {
+  const int64_t Kp = round_up(K, 8);  // 16-byte rows of bf16
+  const bool a_direct = a_bf16 && aligned16(A) && (lda % 8 == 0);
+  const bool b_direct = aligned16(B) && (ldb % 8 == 0);
+  const size_t a_bytes = a_direct ? 0 : align256((size_t)(M * Kp) * 2);
+  const size_t b_bytes = b_direct ? 0 : align256((size_t)(N * Kp) * 2);
+  uint8_t* ws = (a_bytes + b_bytes) ? static_cast<uint8_t*>(workspace(a_bytes + b_bytes)) : nullptr;
+  const void* Ause = A;
+  int64_t lda_use = lda;
+  if (!a_direct) {
+    uint16_t* pa = reinterpret_cast<uint16_t*>(ws);
+    if (a_bf16)
+      launch_copy2d(A, lda, pa, Kp, M, K, 2);
+    else
+      launch_pack_bf16(static_cast<const float*>(A), lda, pa, Kp, M, K);
+    Ause = pa;
+    lda_use = Kp;
+  }
+  const uint16_t* Buse = B;
+  int64_t ldb_use = ldb;
+  if (!b_direct) {
+    uint16_t* pb = reinterpret_cast<uint16_t*>(ws + a_bytes);
+    launch_copy2d(B, ldb, pb, Kp, N, K, 2);
+    Buse = pb;
+    ldb_use = Kp;
+  }
+  GemmCall g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.A = Ause;
+  g.lda = lda_use;
+  g.B = Buse;
+  g.ldb = ldb_use;
+  g.C = C;
+  g.ldc = ldc;
+  g.bias = bias;
+  g.accumulate = acc;
+  g.tf32 = false;
+  g.epi = epi;
+  g.out_bf16 = c_bf16;
+  g.bn = 0;
+  launch_gemm_tc(g);
+}
+
+void gemm_f32_core(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+                   int64_t ldc, const float* bias, bool acc) {
+  const int64_t Kp = round_up(K, 4);  // 16-byte rows of fp32
+  const size_t a_bytes = align256((size_t)(M * Kp) * 4);
+  const size_t b_bytes = align256((size_t)(N * Kp) * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(a_bytes + b_bytes));
+  float* pa = reinterpret_cast<float*>(ws);
+  float* pb = reinterpret_cast<float*>(ws + a_bytes);
+  launch_pack_tf32(A, lda, pa, Kp, M, K);
+  launch_pack_tf32(B, ldb, pb, Kp, N, K);
+  GemmCall g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.A = pa;
+  g.lda = Kp;
+  g.B = pb;
+  g.ldb = Kp;
+  g.C = C;
+  g.ldc = ldc;
+  g.bias = bias;
+  g.accumulate = acc;
+  g.tf32 = true;
+  g.epi = Epi::kStore;
+  g.out_bf16 = false;
+  g.bn = 0;
+  launch_gemm_tc(g);
+}
+
+bool skinny_ok(int64_t M, int64_t K) { return M <= 16 && (size_t)(M * K) * 4 <= 160 * 1024; }
+
+}  // namespace
+
+// Shared by the C ABI and by the DiT runner.
+void gemm_nt_bf16_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                       float* C, int64_t ldc, const float* bias, bool acc) {
+  if (M <= 0 || N <= 0) return;  // no-op before any check, as backend_cuda.cu:455/:464
+  check_gemm_args("gemm_nt_bf16", M, N, K, A, lda, B, ldb, C, ldc);
+  if (K == 0) return launch_bias_fill(C, ldc, M, N, bias, acc);
+  if (skinny_ok(M, K)) return launch_gemm_skinny(M, N, K, A, lda, B, ldb, true, C, ldc, bias, acc);
+  gemm_bf16_core(M, N, K, A, lda, false, B, ldb, C, ldc, false, bias, acc, Epi::kStore);
+}
+void gemm_nt_bf16a_impl(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
+                        int64_t ldb, float* C, int64_t ldc, const float* bias, bool acc) {
+  if (M <= 0 || N <= 0) return;  // no-op before any check, as backend_cuda.cu:455/:464
+  check_gemm_args("gemm_nt_bf16a", M, N, K, A, lda, B, ldb, C, ldc);
+  if (K == 0) return launch_bias_fill(C, ldc, M, N, bias, acc);
+  gemm_bf16_core(M, N, K, A, lda, true, B, ldb, C, ldc, false, bias, acc, Epi::kStore);
+}
+void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                      float* C, int64_t ldc, const float* bias, bool acc) {
+  if (M <= 0 || N <= 0) return;  // no-op before any check, as backend_cuda.cu:455/:464
+  check_gemm_args("gemm_nt_f32", M, N, K, A, lda, B, ldb, C, ldc);
+  if (K == 0) return launch_bias_fill(C, ldc, M, N, bias, acc);
+  if (skinny_ok(M, K)) return launch_gemm_skinny(M, N, K, A, lda, B, ldb, false, C, ldc, bias, acc);
+  gemm_f32_core(M, N, K, A, lda, B, ldb, C, ldc, bias, acc);
+}
+void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16,
+                             const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, bool y_bf16, const float* bias,
+                             int epi) {
+  const char* op = "gemm_bf16_epilogue";
+  require(epi >= 0 && epi <= 2, op, "epi must be 0, 1 or 2");
+  const int64_t ncols = epi == 0 ? N : N / 2;
+  if (epi != 0) require(N % 32 == 0, op, "gated epilogues need N % 32 == 0 (16 + 16 interleaved columns)");
+  if (M <= 0 || N <= 0) return;
+  check_gemm_args(op, M, ncols, K, A, lda, B, ldb, Y, ldy);
+  require(K > 0, op, "K == 0");
+  gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, Y, ldy, y_bf16, bias, false, (Epi)epi);
+}
+
+// conv2d as im2col + tf32 GEMM, writing NCHW directly (ldc = HW), as
+// backend_cuda.cu:479-510 does with cuBLAS.
+void conv2d_impl(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
+                 int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo) {
+  const char* op = "conv2d";
+  require(N >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && kh > 0 && kw > 0 && stride > 0 && pad >= 0, op,
+          "bad shape");
+  require_ptr(x, op, "x");
+  require_ptr(w, op, "w");
+  require_ptr(out, op, "out");
+  const int64_t K = Cin * kh * kw, HW = Ho * Wo;
+  if (N == 0 || HW <= 0) return;
+  const int64_t Kp = round_up(K, 4);
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(HW, ((int64_t)1 << 26) / Kp));
+  // cols live in pool memory so that the GEMM's own workspace stays free.
+  void* pool_malloc(size_t);
+  void pool_free(void*);
+  float* cols = static_cast<float*>(pool_malloc((size_t)(chunk * Kp) * 4));
+  try {
+    for (int64_t n = 0; n < N; ++n) {
+      const float* xin = x + n * Cin * H * W;
+      float* o = out + n * Cout * HW;
+      for (int64_t p0 = 0; p0 < HW; p0 += chunk) {
+        const int64_t P = std::min(chunk, HW - p0);
+        op_im2col(xin, cols, Cin, H, W, kh, kw, Wo, stride, pad, p0, P, K, Kp);
+        // out[co, p0 + p] = sum_k w[co, k] * cols[p, k]
+        gemm_nt_f32_impl(Cout, P, K, w, K, cols, Kp, o + p0, HW, nullptr, false);
+      }
+      if (bias) op_add_bias_rows(o, HW, Cout, HW, bias);
+    }
+  } catch (...) {
+    pool_free(cols);
+    throw;
+  }
+  // The GEMMs above are stream-ordered; freeing into the cache is safe because the
+  // next user of this block is also issued on the same stream.
+  pool_free(cols);
+}
+
+}  // namespace sdb
+
+// ===================================================================================
+using namespace sdb;
+
+#define SDB_GUARD(body)                 \
+  try {                                 \
+    body;                               \
+    return kOk;                         \
+  } catch (const sdb::Error& e) {       \
+    sdb::set_last_error(e.msg);         \
+    return e.code;                      \
+  } catch (const std::exception& e) {   \
+    sdb::set_last_error(e.what());      \
+    return kErrCuda;                    \
+  }
+
+extern "C" {
+
+int sdb200_set_gemm_tile(int bn) {
+  SDB_GUARD({
+    require(bn == 0 || bn == 64 || bn == 128 || bn == 192 || bn == 256, "set_gemm_tile",
+            "bn must be 0, 64, 128, 192 or 256");
+    sdb::set_gemm_tile(bn);
+  })
+}
+
+int sdb200_gemm_nt_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                       float* C, int64_t ldc, const float* bias, int accumulate) {
+  SDB_GUARD(gemm_nt_f32_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
+}
+int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
+                        int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
+  SDB_GUARD(gemm_nt_bf16_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
+}
+int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
+                         int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
+  SDB_GUARD(gemm_nt_bf16a_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
+}
+int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, int a_bf16,
+                              const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, int y_bf16, const float* bias,
+                              int epi) {
+  SDB_GUARD(gemm_bf16_epilogue_impl(M, N, K, A, lda, a_bf16 != 0, B, ldb, Y, ldy, y_bf16 != 0, bias, epi))
+}
+
+int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
+                     int heads, int kv_heads, int64_t d, int causal) {
+  SDB_GUARD({
+    const char* op = "attention";
+    require(N >= 0 && Sq >= 0 && Skv >= 0 && d > 0, op, "bad shape");
+    require(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, op, "heads must be a multiple of kv_heads");
+    if (N == 0 || Sq == 0) return kOk;
+    require(Skv > 0, op, "Skv == 0");
+    require(d <= 256, op, "head dim > 256 is not supported");
+    require_ptr(q, op, "q");
+    require_ptr(k, op, "k");
+    require_ptr(v, op, "v");
+    require_ptr(out, op, "out");
+    launch_attention(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal != 0);
+  })
+}
+
+int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
+                  int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo) {
+  SDB_GUARD(conv2d_impl(x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo))
+}
+int sdb200_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                      const float* beta, float eps) {
+  SDB_GUARD({
+    require(groups > 0 && C % groups == 0, "group_norm", "channels not divisible by groups");
+    require_ptr(gamma, "group_norm", "gamma");
+    require_ptr(beta, "group_norm", "beta");
+    op_group_norm(x, y, N, C, HW, groups, gamma, beta, eps);
+  })
+}
+int sdb200_layer_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta,
+                      float eps) {
+  SDB_GUARD(op_row_norm(x, y, rows, C, gamma, beta, eps, false))
+}
+int sdb200_rms_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, float eps) {
+  SDB_GUARD(op_row_norm(x, y, rows, C, gamma, nullptr, eps, true))
+}
+int sdb200_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma, float eps) {
+  SDB_GUARD(op_rms_norm_heads(x, groups, dim, gamma, eps))
+}
+int sdb200_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const float* cos, const float* sin,
+                int interleaved) {
+  SDB_GUARD({
+    require(dim > 0 && dim % 2 == 0 && inner % dim == 0, "rope", "inner must be a multiple of an even dim");
+    op_rope(x, N, S, inner, dim, cos, sin, interleaved != 0);
+  })
+}
+int sdb200_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, int causal) {
+  SDB_GUARD(op_softmax_rows(x, rows, cols, scale, causal != 0, rows > 0 ? rows : 1))
+}
+int sdb200_geglu(const float* x, float* y, int64_t rows, int64_t D) { SDB_GUARD(op_geglu(x, y, rows, D)) }
+int sdb200_swiglu(const float* gate, const float* up, float* y, int64_t n) { SDB_GUARD(op_swiglu(gate, up, y, n)) }
+int sdb200_silu(float* x, int64_t n) { SDB_GUARD(op_unary(x, n, 0)) }
+int sdb200_gelu(float* x, int64_t n) { SDB_GUARD(op_unary(x, n, 1)) }
+int sdb200_quick_gelu(float* x, int64_t n) { SDB_GUARD(op_unary(x, n, 2)) }
+int sdb200_tanh(float* x, int64_t n) { SDB_GUARD(op_unary(x, n, 3)) }
+int sdb200_add(float* a, const float* b, int64_t n) { SDB_GUARD(op_add(a, b, n)) }
+int sdb200_scale(float* x, float s, int64_t n) { SDB_GUARD(op_affine(x, s, 0.0f, n)) }
+int sdb200_affine(float* x, float a, float b, int64_t n) { SDB_GUARD(op_affine(x, a, b, n)) }
+int sdb200_mul_rows(float* x, const float* v, int64_t rows, int64_t dim) { SDB_GUARD(op_mul_rows(x, v, rows, dim)) }
+int sdb200_add_rows_scaled(float* x, const float* y, const float* g, int64_t rows, int64_t dim) {
+  SDB_GUARD(op_add_rows_scaled(x, y, g, rows, dim))
+}
+int sdb200_add_channel_bias(float* x, const float* b, int64_t N, int64_t C, int64_t HW) {
+  SDB_GUARD(op_add_channel_bias(x, b, N, C, HW))
+}
+int sdb200_upsample_nearest2x(const float* x, float* y, int64_t NC, int64_t H, int64_t W) {
+  SDB_GUARD(op_upsample2x(x, y, NC, H, W))
+}
+int sdb200_concat_channels(const float* a, const float* b, float* y, int64_t N, int64_t Ca, int64_t Cb, int64_t HW) {
+  SDB_GUARD(op_concat_channels(a, b, y, N, Ca, Cb, HW))
+}
+int sdb200_nchw_to_nlc(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
+  SDB_GUARD(op_nchw_to_nlc(x, y, N, C, HW))
+}
+int sdb200_nlc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
+  SDB_GUARD(op_nlc_to_nchw(x, y, N, C, HW))
+}
+int sdb200_patchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
+  SDB_GUARD({
+    require(p > 0 && H % p == 0 && W % p == 0, "patchify", "H and W must be multiples of p");
+    op_patchify(x, y, C, H, W, p);
+  })
+}
+int sdb200_unpatchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
+  SDB_GUARD({
+    require(p > 0 && H % p == 0 && W % p == 0, "unpatchify", "H and W must be multiples of p");
+    op_unpatchify(x, y, C, H, W, p);
+  })
+}
+
+}  // extern "C"

@@ -1,0 +1,131 @@
+"""GPU parity of attention and of the layer / elementwise / layout ops against the
+golden vectors the reference produced, through the C ABI.
+
+Tolerances follow the reference's own GPU-vs-CPU checks (tests/test_ops.cpp:356-477):
+norms 1e-4, rope / swiglu / geglu / activations 1e-5, row helpers 1e-6, layout ops
+exact. conv2d runs on the tf32 tensor-core GEMM, so it is held to the GEMM gate
+(relative Frobenius <= 2e-3) instead of the reference's fp32-SGEMM 1e-3 abs.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, load_golden, rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _np(t):
+    import torch
+
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def test_golden_attention(sdb):
+    """MHA, causal, GQA 4/2 and 8/2 (Qwen3-like), head dims 4..128, Skv != Sq."""
+    for f in sorted(glob.glob(os.path.join(GOLDEN, "attention_*.npz"))):
+        g = np.load(f)
+        N, Sq, Skv, H, KVH, d, causal = (int(v) for v in g["dims"])
+        o = sdb.backend.attention(_t(g["q"]), _t(g["k"]), _t(g["v"]), H, bool(causal), KVH)
+        assert np.abs(_np(o) - g["out"]).max() <= 1e-4, f
+
+
+def test_attention_dit_shape(sdb, orc):
+    """One Z-Image head group at reduced length: 30 heads x d128, 640 tokens."""
+    rng = np.random.default_rng(3)
+    S, H, d = 640, 30, 128
+    q = rng.standard_normal((1, S, H * d)).astype(np.float32)
+    k = rng.standard_normal((1, S, H * d)).astype(np.float32)
+    v = rng.standard_normal((1, S, H * d)).astype(np.float32)
+    want = orc.attention(q, k, v, H, H, False)
+    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), H))
+    assert rel_fro(got, want) <= 2e-3
+
+
+def test_golden_layers(sdb):
+    g = load_golden("layers")
+    be = sdb.backend
+    assert np.abs(_np(be.rms_norm(_t(g["rms_x"]), _t(g["rms_g"]), 1e-6)) - g["rms_y"]).max() <= 1e-4
+    assert np.abs(_np(be.layer_norm(_t(g["ln_x"]), _t(g["ln_g"]), _t(g["ln_b"]), 1e-5)) - g["ln_y"]).max() <= 1e-4
+    assert np.abs(_np(be.layer_norm(_t(g["ln_x"]), None, None, 1e-6)) - g["ln_y_noaff"]).max() <= 1e-4
+    x = _t(g["rms_x"])
+    be.rms_norm_heads_(x, 8, _t(g["rmsh_g"]), 1e-6)
+    assert np.abs(_np(x) - g["rmsh_y"]).max() <= 1e-4
+    for inter, key in ((False, "rope_half"), (True, "rope_inter")):
+        x = _t(g["rope_x"])
+        be.rope_(x, 8, _t(g["rope_cos"]), _t(g["rope_sin"]), inter)
+        assert np.abs(_np(x) - g[key]).max() <= 1e-5, key
+    assert np.abs(_np(be.swiglu(_t(g["swiglu_g"]), _t(g["swiglu_u"]))) - g["swiglu_y"]).max() <= 1e-5
+    assert np.abs(_np(be.geglu(_t(g["geglu_x"]))) - g["geglu_y"]).max() <= 1e-5
+    for causal, key in ((False, "softmax_y"), (True, "softmax_y_causal")):
+        x = _t(g["softmax_x"])
+        be.softmax_rows_(x, 0.37, causal)
+        assert np.abs(_np(x) - g[key]).max() <= 1e-6, key
+    assert np.abs(_np(be.group_norm(_t(g["gn_x"]), 32, _t(g["gn_g"]), _t(g["gn_b"]), 1e-6)) - g["gn_y"]).max() <= 1e-4
+    x = _t(g["rows_x"])
+    be.mul_rows_(x, _t(g["rows_v"]))
+    assert np.abs(_np(x) - g["mul_rows"]).max() <= 1e-6
+    x = _t(g["rows_x"])
+    be.add_rows_scaled_(x, _t(g["rows_y"]), _t(g["rows_v"]))
+    assert np.abs(_np(x) - g["add_rows_scaled"]).max() <= 1e-6
+
+
+def test_golden_conv2d(sdb):
+    for f in sorted(glob.glob(os.path.join(GOLDEN, "conv2d_*.npz"))):
+        g = np.load(f)
+        stride, pad = (int(v) for v in g["dims"])
+        got = _np(sdb.backend.conv2d(_t(g["x"]), _t(g["w"]), _t(g["b"]), stride, pad))
+        assert rel_fro(got, g["y"]) <= 2e-3, f
+
+
+def test_conv2d_sd15_shape(sdb, orc):
+    """BASELINE config 2 conv: 3x3, 320 -> 320 on a 64x64 latent (GEMM 320 x 4096 x 2880)."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((1, 320, 64, 64)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((320, 320, 3, 3))).astype(np.float32)
+    b = (0.02 * rng.standard_normal(320)).astype(np.float32)
+    want = orc.conv2d(x, w, b, 1, 1)
+    got = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 1, 1))
+    assert rel_fro(got, want) <= 2e-3
+
+
+def test_elementwise_and_layout(sdb):
+    import torch
+
+    rng = np.random.default_rng(8)
+    a = rng.standard_normal(1000).astype(np.float32)
+    for name, fn in (("silu", lambda v: v / (1 + np.exp(-v))), ("tanh", np.tanh),
+                     ("quick_gelu", lambda v: v / (1 + np.exp(-1.702 * v)))):
+        x = _t(a)
+        sdb.backend.unary_(name, x)
+        assert np.abs(_np(x) - fn(a.astype(np.float64))).max() <= 1e-5, name
+    L = sdb.lib()
+    img = rng.standard_normal((2, 3, 4, 5)).astype(np.float32)
+    x = _t(img)
+    y = torch.empty((2, 20, 3), device="cuda")
+    sdb.check(L.sdb200_nchw_to_nlc(x.data_ptr(), y.data_ptr(), 2, 3, 20))
+    assert np.array_equal(_np(y), img.reshape(2, 3, 20).transpose(0, 2, 1))
+    z = torch.empty_like(x)
+    sdb.check(L.sdb200_nlc_to_nchw(y.data_ptr(), z.data_ptr(), 2, 3, 20))
+    assert np.array_equal(_np(z), img)
+    up = torch.empty((2, 3, 8, 10), device="cuda")
+    sdb.check(L.sdb200_upsample_nearest2x(x.data_ptr(), up.data_ptr(), 6, 4, 5))
+    assert np.array_equal(_np(up), img.repeat(2, axis=2).repeat(2, axis=3))
+    lat = rng.standard_normal((16, 6, 8)).astype(np.float32)
+    lt = _t(lat)
+    tok = torch.empty((12, 64), device="cuda")
+    sdb.check(L.sdb200_patchify(lt.data_ptr(), tok.data_ptr(), 16, 6, 8, 2))
+    want = lat.reshape(16, 3, 2, 4, 2).transpose(1, 3, 2, 4, 0).reshape(12, 64)
+    assert np.array_equal(_np(tok), want)
+    back = torch.empty_like(lt)
+    sdb.check(L.sdb200_unpatchify(tok.data_ptr(), back.data_ptr(), 16, 6, 8, 2))
+    assert np.array_equal(_np(back), lat)
