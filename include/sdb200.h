@@ -122,6 +122,18 @@ int sdb200_set_gemm_tile(int bn);
 int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                      int heads, int kv_heads, int64_t d, int causal);
 
+/* Extension of backend_cuda.h:58-59 for producers that already emit fp16 operands:
+ * q [N, Sq, heads, dp], k/v [N, Skv, kv_heads, dp] fp16 (dp = 64 for d <= 64, else 128,
+ * zero padded beyond d); out [N, Sq, heads*d] fp32, or bf16 when out_bf16 != 0. */
+int sdb200_attention_f16(const void* q, const void* k, const void* v, void* out, int out_bf16, int64_t N, int64_t Sq,
+                         int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp, int causal);
+/* fp32 x [rows, heads*d] -> fp16 y [rows, heads, dp] (zero padded, |x| > 65504 saturates). */
+int sdb200_pack_heads_f16(const float* x, void* y, int64_t rows, int heads, int64_t d, int64_t dp);
+/* Extension (no reference counterpart): 0 = tensor-core attention (fp16 operands,
+ * fp32 accumulation and softmax; head dims <= 128), 1 = exact fp32 streaming kernel.
+ * Applies to later sdb200_attention calls of this process. */
+int sdb200_set_attention_path(int path);
+
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
 /* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */
 int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,

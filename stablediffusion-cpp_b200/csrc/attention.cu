@@ -6,8 +6,9 @@
 // This file holds the exact-fp32 streaming kernel (online softmax, no score matrix in
 // memory): K/V tiles of 32 keys are staged in shared memory and shared by the query
 // rows of a block; each warp owns one query row and keeps its running max, sum and
-// output accumulator in registers. It serves every head dim up to 256 and is the path
-// for shapes the tensor-core kernel (attention_tc.cu) does not take.
+// output accumulator in registers. It serves head dims above 128, which the
+// tensor-core kernel (attention_tc.cu) does not take, and is the exact reference the
+// tensor-core path can be compared with on the device.
 #include <algorithm>
 #include <cmath>
 
@@ -120,11 +121,6 @@ void launch_attention_simt(const float* q, const float* k, const float* v, float
     case 7: return launch_simt<7>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
     default: return launch_simt<8>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
   }
-}
-
-void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
-                      int heads, int kv_heads, int64_t d, bool causal) {
-  launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
 }
 
 }  // namespace sdb

@@ -1,0 +1,229 @@
+// dit_ops.cu - the memory-bound glue of one Z-Image DiT block, fused around the
+// tensor-core GEMMs so activations cross HBM as few times as possible. Each kernel
+// names the chain of reference ops it replaces (zimage.cpp:90-136 run_block, built on
+// tensor.cpp's rms_norm / mul_rows_ / rms_norm_heads_ / rope_ / add_rows_scaled_).
+//
+//   k_rms_mod_bf16       h = bf16( rms_norm(x, gamma) * scale )   (GEMM A operand)
+//   k_post_norm_residual x += gate * rms_norm(a, gamma2)           (or x += rms_norm(a))
+//   k_qk_norm_rope_pack  per (token, head): q, k RMS-normalised, rotated (interleaved
+//                        RoPE) and packed with v to fp16 [S, heads, 128] for attention
+//   k_adaln_split        mod[4D] -> (1 + scale_msa, tanh gate_msa, 1 + scale_mlp, tanh gate_mlp)
+//   k_timestep_embed     the 256-d sinusoid of t * t_scale (zimage.cpp:151-157)
+//   k_layer_norm_mod     y = layer_norm(x, eps) * scale (final layer, zimage.cpp:221-223)
+//
+// Row kernels run one CTA per token row with 256 threads and float4 loads (D = 3840 =
+// 256 x 15, so each thread owns 15 values = 3.75 float4; a scalar tail covers any D).
+// Reductions are fp32 warp-shuffle trees.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace sdb {
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float block_sum256(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float t = lane < (kRowThreads / 32) ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
+// h[r, :] = bf16(x[r, :] * rstd * gamma * scale); scale may be null (unmodulated
+// blocks). Reference: rms_norm (tensor.cpp:660-679) then mul_rows_ (:889-901), then
+// the A-operand rounding of gemm_nt_bf16 (backend_cuda.cu:466-467).
+__global__ void __launch_bounds__(kRowThreads) k_rms_mod_bf16(const float* __restrict__ x, uint16_t* __restrict__ h,
+                                                              int D, const float* __restrict__ gamma,
+                                                              const float* __restrict__ scale, float eps) {
+  __shared__ float red[32];
+  const float* p = x + (int64_t)blockIdx.x * D;
+  uint16_t* q = h + (int64_t)blockIdx.x * D;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) ss += p[i] * p[i];
+  const float rstd = rsqrtf(block_sum256(ss, red) / (float)D + eps);
+  for (int i = threadIdx.x * 2; i < D; i += kRowThreads * 2) {
+    float a = p[i] * rstd * (gamma ? gamma[i] : 1.0f);
+    if (scale) a *= scale[i];
+    if (i + 1 < D) {
+      float b = p[i + 1] * rstd * (gamma ? gamma[i + 1] : 1.0f);
+      if (scale) b *= scale[i + 1];
+      *reinterpret_cast<uint32_t*>(q + i) = pack_bf16x2(a, b);
+    } else {
+      q[i] = f32_to_bf16_rne(a);
+    }
+  }
+}
+
+// x[r, :] += g * (a[r, :] * rstd(a[r, :]) * gamma); g null means 1 (plain residual).
+// Reference: rms_norm (attn_norm2 / ffn_norm2) then add_rows_scaled_ or add_
+// (zimage.cpp:122-126, :131-135).
+__global__ void __launch_bounds__(kRowThreads) k_post_norm_residual(float* __restrict__ x, const float* __restrict__ a,
+                                                                    int D, const float* __restrict__ gamma,
+                                                                    const float* __restrict__ g, float eps) {
+  __shared__ float red[32];
+  const float* p = a + (int64_t)blockIdx.x * D;
+  float* y = x + (int64_t)blockIdx.x * D;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) ss += p[i] * p[i];
+  const float rstd = rsqrtf(block_sum256(ss, red) / (float)D + eps);
+  for (int i = threadIdx.x; i < D; i += kRowThreads) {
+    const float v = p[i] * rstd * (gamma ? gamma[i] : 1.0f);
+    y[i] += g ? g[i] * v : v;
+  }
+}
+
+// One warp per (token, head): q and k (columns h*128.. of the [S, 3*H*128] QKV output)
+// are RMS-normalised over the head (eps 1e-5, gammas norm_q / norm_k), rotated by the
+// interleaved RoPE tables [S, 128] and written as fp16 to [S, H, 128]; v is copied to
+// fp16. Reference: rms_norm_heads_ + rope_(interleaved) (zimage.cpp:117-120).
+__global__ void k_qk_norm_rope_pack(const float* __restrict__ qkv, int S, int H, const float* __restrict__ gq,
+                                    const float* __restrict__ gk, const float* __restrict__ cs,
+                                    const float* __restrict__ sn, float eps, __half* __restrict__ q16,
+                                    __half* __restrict__ k16, __half* __restrict__ v16) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= (int64_t)S * H) return;
+  const int s = (int)(w / H), h = (int)(w % H);
+  const int D = H * 128;
+  const float* row = qkv + (int64_t)s * 3 * D + h * 128;
+  const int c = lane * 4;  // this lane's 4 consecutive dims = 2 rotary pairs
+  const float4 cv = *reinterpret_cast<const float4*>(cs + (int64_t)s * 128 + c);
+  const float4 sv = *reinterpret_cast<const float4*>(sn + (int64_t)s * 128 + c);
+  const int64_t o = w * 128 + c;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const float* src = row + which * D;
+    const float* gam = which == 0 ? gq : gk;
+    float4 v = *reinterpret_cast<const float4*>(src + c);
+    const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    const float rstd = rsqrtf(ss / 128.0f + eps);
+    if (gam) {
+      const float4 gv = *reinterpret_cast<const float4*>(gam + c);
+      v.x = v.x * rstd * gv.x;
+      v.y = v.y * rstd * gv.y;
+      v.z = v.z * rstd * gv.z;
+      v.w = v.w * rstd * gv.w;
+    } else {
+      v.x *= rstd;
+      v.y *= rstd;
+      v.z *= rstd;
+      v.w *= rstd;
+    }
+    // interleaved pairs (c, c+1) and (c+2, c+3); the tables repeat each angle twice
+    const float r0 = v.x * cv.x - v.y * sv.x, r1 = v.y * cv.x + v.x * sv.x;
+    const float r2 = v.z * cv.z - v.w * sv.z, r3 = v.w * cv.z + v.z * sv.z;
+    __half2* dst = reinterpret_cast<__half2*>((which == 0 ? q16 : k16) + o);
+    dst[0] = __floats2half2_rn(r0, r1);
+    dst[1] = __floats2half2_rn(r2, r3);
+  }
+  const float4 vv = *reinterpret_cast<const float4*>(row + 2 * D + c);
+  __half2* dv = reinterpret_cast<__half2*>(v16 + o);
+  dv[0] = __floats2half2_rn(vv.x, vv.y);
+  dv[1] = __floats2half2_rn(vv.z, vv.w);
+}
+
+// mod [4D] = scale_msa | gate_msa | scale_mlp | gate_mlp -> 1 + s, tanh(g) in place
+// (zimage.cpp:97-112: affine_(1, 1) and tanh_).
+__global__ void k_adaln_split(float* __restrict__ mod, int D) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 4 * D; i += gridDim.x * blockDim.x) {
+    const int part = i / D;
+    const float v = mod[i];
+    mod[i] = (part == 0 || part == 2) ? v * 1.0f + 1.0f : tanhf(v);
+  }
+}
+
+// freq[i] = cos(tt * f_i), freq[half + i] = sin(tt * f_i), f_i = exp(-ln(10000) i / half)
+// (zimage.cpp:151-157).
+__global__ void k_timestep_embed(float* __restrict__ out, int F, float tt) {
+  const int half = F / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = expf(-logf(10000.0f) * (float)i / (float)half);
+    out[i] = cosf(tt * f);
+    out[half + i] = sinf(tt * f);
+  }
+}
+
+// y = layer_norm(x) (no affine) * scale, two-pass mean / variance
+// (tensor.cpp:628-658 then mul_rows_; zimage.cpp:221-223).
+__global__ void __launch_bounds__(kRowThreads) k_layer_norm_mod(const float* __restrict__ x, float* __restrict__ y,
+                                                                int D, const float* __restrict__ scale, float eps) {
+  __shared__ float red[32];
+  const float* p = x + (int64_t)blockIdx.x * D;
+  float* q = y + (int64_t)blockIdx.x * D;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) s += p[i];
+  const float mean = block_sum256(s, red) / (float)D;
+  float v = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) {
+    const float d = p[i] - mean;
+    v += d * d;
+  }
+  const float rstd = rsqrtf(block_sum256(v, red) / (float)D + eps);
+  for (int i = threadIdx.x; i < D; i += kRowThreads) q[i] = (p[i] - mean) * rstd * (scale ? scale[i] : 1.0f);
+}
+
+// Copies `src` [1, D] into rows [r0, r1) of y [*, D] (pad tokens, zimage.cpp:31-36).
+__global__ void k_fill_rows(float* __restrict__ y, const float* __restrict__ src, int64_t r0, int64_t r1, int D) {
+  const int64_t n = (r1 - r0) * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[r0 * D + i] = src[i % D];
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------
+void dit_rms_mod_bf16(const float* x, uint16_t* h, int64_t rows, int D, const float* gamma, const float* scale,
+                      float eps) {
+  if (rows <= 0) return;
+  k_rms_mod_bf16<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, h, D, gamma, scale, eps);
+  check_launch("rms_mod_bf16");
+}
+void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const float* gamma, const float* g,
+                            float eps) {
+  if (rows <= 0) return;
+  k_post_norm_residual<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, a, D, gamma, g, eps);
+  check_launch("post_norm_residual");
+}
+void dit_qk_norm_rope_pack(const float* qkv, int S, int H, const float* gq, const float* gk, const float* cs,
+                           const float* sn, float eps, void* q16, void* k16, void* v16) {
+  const int64_t warps = (int64_t)S * H;
+  if (warps <= 0) return;
+  const int wpb = 8;
+  k_qk_norm_rope_pack<<<(unsigned)((warps + wpb - 1) / wpb), wpb * 32, 0, ctx().stream>>>(
+      qkv, S, H, gq, gk, cs, sn, eps, (__half*)q16, (__half*)k16, (__half*)v16);
+  check_launch("qk_norm_rope_pack");
+}
+void dit_adaln_split(float* mod, int D) {
+  k_adaln_split<<<(unsigned)((4 * D + 255) / 256), 256, 0, ctx().stream>>>(mod, D);
+  check_launch("adaln_split");
+}
+void dit_timestep_embed(float* out, int F, float tt) {
+  k_timestep_embed<<<1, 128, 0, ctx().stream>>>(out, F, tt);
+  check_launch("timestep_embed");
+}
+void dit_layer_norm_mod(const float* x, float* y, int64_t rows, int D, const float* scale, float eps) {
+  if (rows <= 0) return;
+  k_layer_norm_mod<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, y, D, scale, eps);
+  check_launch("layer_norm_mod");
+}
+void dit_fill_rows(float* y, const float* src, int64_t r0, int64_t r1, int D) {
+  if (r1 <= r0) return;
+  const int64_t n = (r1 - r0) * D;
+  k_fill_rows<<<(unsigned)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, ctx().stream>>>(y, src, r0, r1, D);
+  check_launch("fill_rows");
+}
+
+}  // namespace sdb

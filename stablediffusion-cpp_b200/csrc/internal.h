@@ -102,9 +102,15 @@ void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* 
 // Attention (attention.cu).
 void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                       int heads, int kv_heads, int64_t d, bool causal);
-// Attention on bf16 operands already laid out [N, heads, S, dp] (dp = padded head dim).
-void launch_attention_bf16(const uint16_t* q, const uint16_t* k, const uint16_t* v, float* out, int64_t out_ld,
-                           int64_t N, int64_t Sq, int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp,
-                           bool causal, float scale, bool out_bf16);
+// Tensor-core attention on fp16 operands laid out [N, S, heads, dp] (dp = 64 or 128,
+// zero padded); out rows are out_row elements apart, samples out_batch apart; out is
+// fp32 or bf16.
+void launch_attention_f16(const void* q, const void* k, const void* v, void* out, long long out_row,
+                          long long out_batch, bool out_bf16, int64_t N, int64_t Sq, int64_t Skv, int heads,
+                          int kv_heads, int64_t d, int64_t dp, bool causal);
+// fp32 [rows, H*d] -> fp16 [rows, H, dp], zero padded.
+void launch_pack_heads_f16(const float* x, void* y, int64_t rows, int H, int64_t d, int64_t dp);
+// Selects the tensor-core attention (true, default) or the exact fp32 kernel.
+void set_attention_tc(bool on);
 
 }  // namespace sdb

@@ -253,6 +253,13 @@ int sdb200_set_gemm_tile(int bn) {
   })
 }
 
+int sdb200_set_attention_path(int path) {
+  SDB_GUARD({
+    require(path == 0 || path == 1, "set_attention_path", "path must be 0 (tensor cores) or 1 (exact fp32)");
+    sdb::set_attention_tc(path == 0);
+  })
+}
+
 int sdb200_gemm_nt_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                        float* C, int64_t ldc, const float* bias, int accumulate) {
   SDB_GUARD(gemm_nt_f32_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
@@ -285,6 +292,33 @@ int sdb200_attention(const float* q, const float* k, const float* v, float* out,
     require_ptr(v, op, "v");
     require_ptr(out, op, "out");
     launch_attention(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal != 0);
+  })
+}
+
+int sdb200_attention_f16(const void* q, const void* k, const void* v, void* out, int out_bf16, int64_t N, int64_t Sq,
+                         int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp, int causal) {
+  SDB_GUARD({
+    const char* op = "attention_f16";
+    require(N >= 0 && Sq >= 0 && Skv > 0 && d > 0, op, "bad shape");
+    require(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, op, "heads must be a multiple of kv_heads");
+    require((dp == 64 && d <= 64) || (dp == 128 && d <= 128), op, "dp must be 64 (d <= 64) or 128 (d <= 128)");
+    require_ptr(q, op, "q");
+    require_ptr(k, op, "k");
+    require_ptr(v, op, "v");
+    require_ptr(out, op, "out");
+    require(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0, op, "q/k/v must be 16-byte aligned");
+    if (N == 0 || Sq == 0) return kOk;
+    launch_attention_f16(q, k, v, out, (long long)heads * d, (long long)Sq * heads * d, out_bf16 != 0, N, Sq, Skv,
+                         heads, kv_heads, d, dp, causal != 0);
+  })
+}
+
+int sdb200_pack_heads_f16(const float* x, void* y, int64_t rows, int heads, int64_t d, int64_t dp) {
+  SDB_GUARD({
+    require(dp >= d && heads > 0 && rows >= 0, "pack_heads_f16", "bad shape");
+    require_ptr(x, "pack_heads_f16", "x");
+    require_ptr(y, "pack_heads_f16", "y");
+    launch_pack_heads_f16(x, y, rows, heads, d, dp);
   })
 }
 

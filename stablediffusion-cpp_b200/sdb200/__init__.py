@@ -66,6 +66,9 @@ _SIGS = {
     "sdb200_gemm_nt_bf16": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16a": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_bf16_epilogue": ([_i64, _i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i, _v, _i], _i),
+    "sdb200_set_attention_path": ([_i], _i),
+    "sdb200_attention_f16": ([_v, _v, _v, _v, _i, _i64, _i64, _i64, _i, _i, _i64, _i64, _i], _i),
+    "sdb200_pack_heads_f16": ([_v, _v, _i64, _i, _i64, _i64], _i),
     "sdb200_attention": ([_v, _v, _v, _v, _i64, _i64, _i64, _i, _i, _i64, _i], _i),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
     "sdb200_group_norm": ([_v, _v, _i64, _i64, _i64, _i, _v, _v, _f], _i),

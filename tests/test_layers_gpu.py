@@ -30,8 +30,18 @@ def _np(t):
     return t.cpu().numpy()
 
 
-def test_golden_attention(sdb):
-    """MHA, causal, GQA 4/2 and 8/2 (Qwen3-like), head dims 4..128, Skv != Sq."""
+@pytest.fixture
+def attention_path(sdb):
+    """Selects the attention kernel for one test and restores the default after."""
+    def use(path):
+        sdb.check(sdb.lib().sdb200_set_attention_path(path))
+    yield use
+    sdb.check(sdb.lib().sdb200_set_attention_path(0))
+
+
+def test_golden_attention_exact_path(sdb, attention_path):
+    """fp32 streaming kernel: the reference's own GPU tolerance (test_ops.cpp:439-451, 1e-4)."""
+    attention_path(1)
     for f in sorted(glob.glob(os.path.join(GOLDEN, "attention_*.npz"))):
         g = np.load(f)
         N, Sq, Skv, H, KVH, d, causal = (int(v) for v in g["dims"])
@@ -39,16 +49,45 @@ def test_golden_attention(sdb):
         assert np.abs(_np(o) - g["out"]).max() <= 1e-4, f
 
 
-def test_attention_dit_shape(sdb, orc):
-    """One Z-Image head group at reduced length: 30 heads x d128, 640 tokens."""
-    rng = np.random.default_rng(3)
-    S, H, d = 640, 30, 128
-    q = rng.standard_normal((1, S, H * d)).astype(np.float32)
-    k = rng.standard_normal((1, S, H * d)).astype(np.float32)
-    v = rng.standard_normal((1, S, H * d)).astype(np.float32)
-    want = orc.attention(q, k, v, H, H, False)
-    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), H))
+def test_golden_attention_tensor_cores(sdb, attention_path):
+    """tcgen05 kernel (fp16 operands, fp32 softmax/accumulate): relative Frobenius <= 2e-3,
+    the per-contraction parity gate. Covers MHA, causal, GQA 4/2 and 8/2, head dims 4..128
+    (padded to 64/128), Skv != Sq and ragged tiles."""
+    attention_path(0)
+    for f in sorted(glob.glob(os.path.join(GOLDEN, "attention_*.npz"))):
+        g = np.load(f)
+        N, Sq, Skv, H, KVH, d, causal = (int(v) for v in g["dims"])
+        o = sdb.backend.attention(_t(g["q"]), _t(g["k"]), _t(g["v"]), H, bool(causal), KVH)
+        assert rel_fro(_np(o), g["out"]) <= 2e-3, f
+
+
+@pytest.mark.parametrize("N,Sq,Skv,H,KVH,d,causal", [
+    (1, 4224, 4224, 4, 4, 128, False),   # Z-Image joint sequence at 1024^2 (4 of 30 heads)
+    (1, 640, 640, 30, 30, 128, False),   # all 30 heads, shorter sequence
+    (2, 300, 300, 32, 8, 128, True),     # Qwen3-like GQA 32/8, causal
+    (1, 1024, 77, 8, 8, 40, False),      # SD1.5 cross-attention (d=40 padded to 64)
+    (2, 1000, 1000, 8, 8, 40, False),    # SD1.5 self-attention, ragged tiles
+    (1, 129, 700, 2, 1, 64, True),       # Skv > Sq, causal, 2/1 GQA
+])
+def test_attention_tensor_cores_vs_oracle(sdb, orc, attention_path, N, Sq, Skv, H, KVH, d, causal):
+    attention_path(0)
+    rng = np.random.default_rng(Sq + Skv + H)
+    q = rng.standard_normal((N, Sq, H * d)).astype(np.float32)
+    k = rng.standard_normal((N, Skv, KVH * d)).astype(np.float32)
+    v = rng.standard_normal((N, Skv, KVH * d)).astype(np.float32)
+    want = orc.attention(q, k, v, H, KVH, causal)
+    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), H, causal, KVH))
+    assert np.isfinite(got).all()
     assert rel_fro(got, want) <= 2e-3
+
+
+def test_attention_d256_uses_exact_kernel(sdb, orc):
+    rng = np.random.default_rng(12)
+    q = rng.standard_normal((1, 40, 2 * 256)).astype(np.float32)
+    k = rng.standard_normal((1, 50, 2 * 256)).astype(np.float32)
+    v = rng.standard_normal((1, 50, 2 * 256)).astype(np.float32)
+    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), 2))
+    assert np.abs(got - orc.attention(q, k, v, 2, 2, False)).max() <= 1e-4
 
 
 def test_golden_layers(sdb):
