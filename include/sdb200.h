@@ -134,6 +134,23 @@ int sdb200_pack_heads_f16(const float* x, void* y, int64_t rows, int heads, int6
  * Applies to later sdb200_attention calls of this process. */
 int sdb200_set_attention_path(int path);
 
+/* ---- Z-Image DiT forward (zimage.h:56 ZImageTransformer::forward) ------------------
+ * The whole transformer on the device: create with the Config values of zimage.h:40-47,
+ * register every weight (device pointer, dtype, shape) under its checkpoint name
+ * (zimage.cpp:38-67), finalize (builds the fused QKV / interleaved w1-w3 weights the
+ * model owns; the caller keeps the registered buffers alive), then call forward. x is
+ * [B, C, H, W] fp32, cap [B, L, capdim] fp32, out [B, C, H, W] fp32, all on the device;
+ * the B images share the timestep t (the reference forward is batch 1, zimage.cpp:140).
+ * Block linears must be bf16; head dim must be 128. */
+void* sdb200_zimage_create(int heads, int patch, float norm_eps, float rope_theta, float t_scale, int ax0, int ax1,
+                           int ax2);
+int sdb200_zimage_set_weight(void* model, const char* name, const void* dev_ptr, int is_bf16, const int64_t* shape,
+                             int ndim);
+int sdb200_zimage_finalize(void* model);
+int sdb200_zimage_forward(void* model, const float* x, int64_t B, int64_t C, int64_t H, int64_t W, float t,
+                          const float* cap, int64_t L, int64_t capdim, float* out);
+void sdb200_zimage_destroy(void* model);
+
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
 /* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */
 int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,

@@ -182,7 +182,35 @@ __global__ void k_fill_rows(float* __restrict__ y, const float* __restrict__ src
     y[r0 * D + i] = src[i % D];
 }
 
+// out rows [32j, 32j+16) = a rows [16j, 16j+16), out rows [32j+16, 32j+32) = b rows
+// [16j, 16j+16): the gate/up (or value/gate) interleave the fused gated epilogue of
+// the GEMM reads (gemm_tc.cu). Works for 2-byte and 4-byte elements (weights, biases).
+template <typename T>
+__global__ void k_interleave_rows16(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ out,
+                                    int64_t rows, int64_t cols) {
+  const int64_t n = 2 * rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int64_t blk = r / 32, w = r % 32;
+    const int64_t src = blk * 16 + (w & 15);
+    out[i] = (w < 16 ? a : b)[src * cols + c];
+  }
+}
+
 }  // namespace
+
+void dit_interleave_rows16(const void* a, const void* b, void* out, int64_t rows, int64_t cols, int esize) {
+  const int64_t n = 2 * rows * cols;
+  if (n <= 0) return;
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)ctx().num_sms * 16);
+  if (esize == 2)
+    k_interleave_rows16<uint16_t><<<blocks, 256, 0, ctx().stream>>>((const uint16_t*)a, (const uint16_t*)b,
+                                                                     (uint16_t*)out, rows, cols);
+  else
+    k_interleave_rows16<float><<<blocks, 256, 0, ctx().stream>>>((const float*)a, (const float*)b, (float*)out, rows,
+                                                                 cols);
+  check_launch("interleave_rows16");
+}
 
 // ---------------------------------------------------------------------------------
 void dit_rms_mod_bf16(const float* x, uint16_t* h, int64_t rows, int D, const float* gamma, const float* scale,

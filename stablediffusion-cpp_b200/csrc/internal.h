@@ -99,6 +99,58 @@ void launch_copy2d(const void* src, int64_t ld, void* dst, int64_t ldo, int64_t 
 // C[m, n] = bias[n] (or += when accumulate), used when K == 0.
 void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, bool accumulate);
 
+// Layer ops (layers.cu); arguments already validated by the caller.
+void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
+void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float);
+void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const float*, float, bool);
+void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
+void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);
+void op_softmax_rows(float*, int64_t, int64_t, float, bool, int64_t);
+void op_geglu(const float*, float*, int64_t, int64_t);
+void op_swiglu(const float*, const float*, float*, int64_t);
+void op_unary(float*, int64_t, int);  // 0 silu, 1 gelu (erf), 2 quick_gelu, 3 tanh
+void op_add(float*, const float*, int64_t);
+void op_affine(float*, float, float, int64_t);
+void op_mul_rows(float*, const float*, int64_t, int64_t);
+void op_add_rows_scaled(float*, const float*, const float*, int64_t, int64_t);
+void op_add_channel_bias(float*, const float*, int64_t, int64_t, int64_t);
+void op_add_bias_rows(float*, int64_t, int64_t, int64_t, const float*);
+void op_upsample2x(const float*, float*, int64_t, int64_t, int64_t);
+void op_concat_channels(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t);
+void op_nchw_to_nlc(const float*, float*, int64_t, int64_t, int64_t);
+void op_nlc_to_nchw(const float*, float*, int64_t, int64_t, int64_t);
+void op_patchify(const float*, float*, int64_t, int64_t, int64_t, int);
+void op_unpatchify(const float*, float*, int64_t, int64_t, int64_t, int);
+void op_im2col(const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int, int, int64_t, int64_t,
+               int64_t, int64_t);
+void set_last_error(const std::string& s);
+
+// Caching allocator (runtime.cu).
+void* pool_malloc(size_t bytes);
+void pool_free(void* p);
+
+// GEMM front-ends with argument checks (ops_api.cu).
+void gemm_nt_bf16_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                       float* C, int64_t ldc, const float* bias, bool acc);
+void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                      float* C, int64_t ldc, const float* bias, bool acc);
+void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16,
+                             const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, bool y_bf16, const float* bias,
+                             int epi);
+
+// DiT glue kernels (dit_ops.cu).
+void dit_rms_mod_bf16(const float* x, uint16_t* h, int64_t rows, int D, const float* gamma, const float* scale,
+                      float eps);
+void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const float* gamma, const float* g,
+                            float eps);
+void dit_qk_norm_rope_pack(const float* qkv, int S, int H, const float* gq, const float* gk, const float* cs,
+                           const float* sn, float eps, void* q16, void* k16, void* v16);
+void dit_adaln_split(float* mod, int D);
+void dit_timestep_embed(float* out, int F, float tt);
+void dit_layer_norm_mod(const float* x, float* y, int64_t rows, int D, const float* scale, float eps);
+void dit_fill_rows(float* y, const float* src, int64_t r0, int64_t r1, int D);
+void dit_interleave_rows16(const void* a, const void* b, void* out, int64_t rows, int64_t cols, int esize);
+
 // Attention (attention.cu).
 void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                       int heads, int kv_heads, int64_t d, bool causal);

@@ -16,30 +16,6 @@
 #include "sdb200.h"
 
 namespace sdb {
-void set_last_error(const std::string& s);
-void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
-void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float);
-void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const float*, float, bool);
-void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
-void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);
-void op_softmax_rows(float*, int64_t, int64_t, float, bool, int64_t);
-void op_geglu(const float*, float*, int64_t, int64_t);
-void op_swiglu(const float*, const float*, float*, int64_t);
-void op_unary(float*, int64_t, int);
-void op_add(float*, const float*, int64_t);
-void op_affine(float*, float, float, int64_t);
-void op_mul_rows(float*, const float*, int64_t, int64_t);
-void op_add_rows_scaled(float*, const float*, const float*, int64_t, int64_t);
-void op_add_channel_bias(float*, const float*, int64_t, int64_t, int64_t);
-void op_add_bias_rows(float*, int64_t, int64_t, int64_t, const float*);
-void op_upsample2x(const float*, float*, int64_t, int64_t, int64_t);
-void op_concat_channels(const float*, const float*, float*, int64_t, int64_t, int64_t, int64_t);
-void op_nchw_to_nlc(const float*, float*, int64_t, int64_t, int64_t);
-void op_nlc_to_nchw(const float*, float*, int64_t, int64_t, int64_t);
-void op_patchify(const float*, float*, int64_t, int64_t, int64_t, int);
-void op_unpatchify(const float*, float*, int64_t, int64_t, int64_t, int);
-void op_im2col(const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int, int, int64_t, int64_t,
-               int64_t, int64_t);
 
 namespace {
 
@@ -202,8 +178,6 @@ void conv2d_impl(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, c
   const int64_t Kp = round_up(K, 4);
   const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(HW, ((int64_t)1 << 26) / Kp));
   // cols live in pool memory so that the GEMM's own workspace stays free.
-  void* pool_malloc(size_t);
-  void pool_free(void*);
   float* cols = static_cast<float*>(pool_malloc((size_t)(chunk * Kp) * 4));
   try {
     for (int64_t n = 0; n < N; ++n) {

@@ -1,0 +1,469 @@
+// zimage.cu - the Z-Image single-stream DiT forward (reference: src/zimage.{h,cpp},
+// ZImageTransformer::forward / run_block) on the B200 kernels, every activation kept
+// on the device from the latent in to the prediction out.
+//
+// Per block (zimage.cpp:90-136), with the reference op each step replaces:
+//   mod  = adaLN(t_emb)               GEMV, M=1 (bf16 W)        -> k_gemm_skinny
+//          1 + s, tanh(g)             affine_/tanh_             -> k_adaln_split
+//   h    = bf16(rms_norm(x)*scale)    rms_norm + mul_rows_      -> k_rms_mod_bf16
+//   qkv  = h Wqkv^T                   to_q / to_k / to_v (3 GEMMs) -> one tcgen05 GEMM, N = 3D
+//   q,k,v -> fp16 heads               rms_norm_heads_ + rope_   -> k_qk_norm_rope_pack
+//   o    = attention(q,k,v)           attention                  -> k_attention_tc (bf16 out)
+//   a    = o Wout^T                   to_out                     -> tcgen05 GEMM
+//   x   += g_msa * rms_norm(a)        rms_norm + add_rows_scaled_ -> k_post_norm_residual
+//   h    = bf16(rms_norm(x)*scale)    (as above)
+//   f    = silu(h W1^T) * (h W3^T)    w1, w3, swiglu             -> one GEMM, SwiGLU epilogue
+//   a    = f W2^T                     w2                         -> tcgen05 GEMM
+//   x   += g_mlp * rms_norm(a)        (as above)
+// The forward takes a batch of B images that share the timestep (a sampler step):
+// row-wise ops and GEMMs run over all B*S rows at once (larger GEMM M), attention over
+// N = B samples. The reference forward is batch-1; for B = 1 the math is identical.
+//
+// Weights are the caller's device buffers under the checkpoint names
+// (zimage.cpp:38-67). Block linears must be bf16 (the loader keeps tensors of >= 2^20
+// elements in bf16, safetensors.cpp:119); small layers (x_embed, t_mlp, final) may be
+// fp32 or bf16. finalize() builds the fused QKV and interleaved w1/w3 weights it owns.
+#include <array>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "internal.h"
+#include "sdb200.h"
+
+namespace sdb {
+namespace {
+
+struct WRef {
+  const void* p = nullptr;
+  bool bf16 = false;
+  std::vector<int64_t> shape;
+  int64_t dim(int i) const { return shape[i < 0 ? i + (int)shape.size() : i]; }
+};
+
+// Device buffer owned by the model (pool allocator).
+struct DBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+  DBuf(DBuf&& o) noexcept : p(o.p), bytes(o.bytes) {
+    o.p = nullptr;
+    o.bytes = 0;
+  }
+  DBuf& operator=(DBuf&& o) noexcept {
+    if (this != &o) {
+      reset();
+      p = o.p;
+      bytes = o.bytes;
+      o.p = nullptr;
+      o.bytes = 0;
+    }
+    return *this;
+  }
+  ~DBuf() { reset(); }
+  void reset() {
+    if (p) {
+      try {
+        pool_free(p);
+      } catch (...) {
+      }
+    }
+    p = nullptr;
+    bytes = 0;
+  }
+  void ensure(size_t b) {
+    if (b <= bytes) return;
+    reset();
+    p = pool_malloc(b);
+    bytes = b;
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+struct Block {
+  const float *attn_norm1 = nullptr, *attn_norm2 = nullptr, *ffn_norm1 = nullptr, *ffn_norm2 = nullptr;
+  const float *norm_q = nullptr, *norm_k = nullptr;
+  DBuf wqkv, bqkv, w13, b13;  // fused, owned
+  bool has_bqkv = false, has_b13 = false;
+  const uint16_t* wout = nullptr;
+  const float* bout = nullptr;
+  const uint16_t* w2 = nullptr;
+  const float* b2 = nullptr;
+  const uint16_t* adaln = nullptr;  // [4D, tdim] or null (context refiner)
+  const float* adaln_b = nullptr;
+  int64_t F = 0;
+};
+
+// Generic linear on fp32 activations: bf16 or fp32 weights (tensor.cpp:481-501).
+void linear(const float* x, int64_t rows, int64_t in, const WRef& W, const WRef* b, float* y) {
+  const int64_t out = W.dim(0);
+  if (W.dim(1) != in) fail(kErrInvalidArg, "zimage: linear input width mismatch");
+  const float* bias = b ? static_cast<const float*>(b->p) : nullptr;
+  if (W.bf16)
+    gemm_nt_bf16_impl(rows, out, in, x, in, static_cast<const uint16_t*>(W.p), in, y, out, bias, false);
+  else
+    gemm_nt_f32_impl(rows, out, in, x, in, static_cast<const float*>(W.p), in, y, out, bias, false);
+}
+
+}  // namespace
+
+class ZImage {
+ public:
+  int heads, patch;
+  float norm_eps, rope_theta, t_scale;
+  int axes[3];
+  std::unordered_map<std::string, WRef> w;
+  bool finalized = false;
+  int64_t D = 0, head_dim = 0, in_ch = 0, tdim = 0;
+  std::vector<Block> noise, context, layers;
+
+  ZImage(int h, int p, float eps, float theta, float ts, int a0, int a1, int a2)
+      : heads(h), patch(p), norm_eps(eps), rope_theta(theta), t_scale(ts), axes{a0, a1, a2} {}
+
+  const WRef& get(const std::string& n) const {
+    auto it = w.find(n);
+    if (it == w.end()) fail(kErrInvalidArg, "zimage: missing weight: " + n);
+    return it->second;
+  }
+  const WRef* try_get(const std::string& n) const {
+    auto it = w.find(n);
+    return it == w.end() ? nullptr : &it->second;
+  }
+  const float* f32(const std::string& n) const {
+    const WRef& r = get(n);
+    if (r.bf16) fail(kErrInvalidArg, "zimage: " + n + " must be fp32");
+    return static_cast<const float*>(r.p);
+  }
+  const uint16_t* bf16w(const std::string& n) const {
+    const WRef& r = get(n);
+    if (!r.bf16) fail(kErrInvalidArg, "zimage: " + n + " must be bf16 (block linears run on the bf16 path)");
+    return static_cast<const uint16_t*>(r.p);
+  }
+
+  Block load_block(const std::string& p, bool modulated) {
+    Block b;
+    b.attn_norm1 = f32(p + ".attention_norm1.weight");
+    b.attn_norm2 = f32(p + ".attention_norm2.weight");
+    b.ffn_norm1 = f32(p + ".ffn_norm1.weight");
+    b.ffn_norm2 = f32(p + ".ffn_norm2.weight");
+    b.norm_q = f32(p + ".attention.norm_q.weight");
+    b.norm_k = f32(p + ".attention.norm_k.weight");
+    const uint16_t* wq = bf16w(p + ".attention.to_q.weight");
+    const uint16_t* wk = bf16w(p + ".attention.to_k.weight");
+    const uint16_t* wv = bf16w(p + ".attention.to_v.weight");
+    const size_t mat = (size_t)(D * D) * 2;
+    b.wqkv.ensure(3 * mat);
+    cudaStream_t s = ctx().stream;
+    check_cuda(cudaMemcpyAsync(b.wqkv.as<uint8_t>(), wq, mat, cudaMemcpyDeviceToDevice, s), "zimage wqkv");
+    check_cuda(cudaMemcpyAsync(b.wqkv.as<uint8_t>() + mat, wk, mat, cudaMemcpyDeviceToDevice, s), "zimage wqkv");
+    check_cuda(cudaMemcpyAsync(b.wqkv.as<uint8_t>() + 2 * mat, wv, mat, cudaMemcpyDeviceToDevice, s), "zimage wqkv");
+    const WRef* bq = try_get(p + ".attention.to_q.bias");
+    const WRef* bk = try_get(p + ".attention.to_k.bias");
+    const WRef* bv = try_get(p + ".attention.to_v.bias");
+    if (bq || bk || bv) {
+      b.has_bqkv = true;
+      b.bqkv.ensure((size_t)(3 * D) * 4);
+      check_cuda(cudaMemsetAsync(b.bqkv.p, 0, (size_t)(3 * D) * 4, s), "zimage bqkv");
+      const WRef* bb[3] = {bq, bk, bv};
+      for (int i = 0; i < 3; ++i)
+        if (bb[i])
+          check_cuda(cudaMemcpyAsync(b.bqkv.as<float>() + i * D, bb[i]->p, (size_t)D * 4, cudaMemcpyDeviceToDevice, s),
+                     "zimage bqkv");
+    }
+    b.wout = bf16w(p + ".attention.to_out.0.weight");
+    const WRef* bo = try_get(p + ".attention.to_out.0.bias");
+    b.bout = bo ? static_cast<const float*>(bo->p) : nullptr;
+    const WRef& w1 = get(p + ".feed_forward.w1.weight");
+    b.F = w1.dim(0);
+    if (b.F % 16) fail(kErrInvalidArg, "zimage: FFN width must be a multiple of 16");
+    b.w13.ensure((size_t)(2 * b.F * D) * 2);
+    dit_interleave_rows16(bf16w(p + ".feed_forward.w1.weight"), bf16w(p + ".feed_forward.w3.weight"), b.w13.p, b.F, D,
+                          2);
+    const WRef* b1 = try_get(p + ".feed_forward.w1.bias");
+    const WRef* b3 = try_get(p + ".feed_forward.w3.bias");
+    if (b1 || b3) {
+      if (!b1 || !b3) fail(kErrUnsupported, "zimage: w1/w3 must both have biases or neither");
+      b.has_b13 = true;
+      b.b13.ensure((size_t)(2 * b.F) * 4);
+      dit_interleave_rows16(b1->p, b3->p, b.b13.p, b.F, 1, 4);
+    }
+    b.w2 = bf16w(p + ".feed_forward.w2.weight");
+    const WRef* b2 = try_get(p + ".feed_forward.w2.bias");
+    b.b2 = b2 ? static_cast<const float*>(b2->p) : nullptr;
+    if (modulated) {
+      b.adaln = bf16w(p + ".adaLN_modulation.0.weight");
+      const WRef* ab = try_get(p + ".adaLN_modulation.0.bias");
+      b.adaln_b = ab ? static_cast<const float*>(ab->p) : nullptr;
+      if (get(p + ".adaLN_modulation.0.weight").dim(0) != 4 * D) fail(kErrInvalidArg, "zimage: adaLN width != 4*dim");
+    }
+    return b;
+  }
+
+  void finalize() {
+    const WRef& xe = get("all_x_embedder.2-1.weight");
+    D = xe.dim(0);
+    if (D % heads) fail(kErrInvalidArg, "zimage: dim not divisible by heads");
+    head_dim = D / heads;
+    if (head_dim != 128) fail(kErrUnsupported, "zimage: head dim must be 128 (Z-Image)");
+    if (axes[0] + axes[1] + axes[2] != head_dim) fail(kErrInvalidArg, "zimage: axes_dims must sum to the head dim");
+    in_ch = xe.dim(1) / (patch * patch);
+    tdim = get("t_embedder.mlp.0.weight").dim(1);
+    for (int i = 0; has("noise_refiner." + std::to_string(i) + ".attention_norm1.weight"); ++i)
+      noise.push_back(load_block("noise_refiner." + std::to_string(i), true));
+    for (int i = 0; has("context_refiner." + std::to_string(i) + ".attention_norm1.weight"); ++i)
+      context.push_back(load_block("context_refiner." + std::to_string(i), false));
+    for (int i = 0; has("layers." + std::to_string(i) + ".attention_norm1.weight"); ++i)
+      layers.push_back(load_block("layers." + std::to_string(i), true));
+    if (layers.empty()) fail(kErrInvalidArg, "zimage: no transformer layers found");
+    finalized = true;
+  }
+  bool has(const std::string& n) const { return w.count(n) != 0; }
+
+  // ---- activations (grown on demand) ----------------------------------------------
+  DBuf tok, img, cap, uni, h, qkv, q16, k16, v16, ao, a, g, mod, temb, thid, adaln, fscale, capn, outtok, fin;
+  std::map<std::array<int64_t, 3>, std::unique_ptr<DBuf[]>> tables;  // (Ht, Wt, n_cap_pad) -> cos/sin sets
+
+  // Rotary tables for (axis0, h, w) positions, interleaved layout (zimage.cpp:71-88):
+  // freq = theta^(-2k/d_a) in double, angle = (float)(pos * freq), cos/sin in float.
+  void rope_tables(const std::vector<std::array<int, 3>>& pos, std::vector<float>& cs, std::vector<float>& sn) const {
+    const int64_t S = (int64_t)pos.size(), d = head_dim;
+    cs.assign((size_t)(S * d), 0.0f);
+    sn.assign((size_t)(S * d), 0.0f);
+    for (int64_t s = 0; s < S; ++s) {
+      int64_t off = 0;
+      for (int a = 0; a < 3; ++a) {
+        const int da = axes[a];
+        for (int k = 0; k < da / 2; ++k) {
+          const double freq = 1.0 / std::pow((double)rope_theta, (double)(2 * k) / (double)da);
+          const float ang = (float)((double)pos[s][a] * freq);
+          const float c = std::cos(ang), si = std::sin(ang);
+          cs[s * d + off + 2 * k] = cs[s * d + off + 2 * k + 1] = c;
+          sn[s * d + off + 2 * k] = sn[s * d + off + 2 * k + 1] = si;
+        }
+        off += da;
+      }
+    }
+  }
+
+  // Returns [img cos, img sin, cap cos, cap sin, uni cos, uni sin] on the device.
+  DBuf* get_tables(int64_t Ht, int64_t Wt, int64_t n_img_pad, int64_t n_cap_pad) {
+    auto key = std::array<int64_t, 3>{Ht, Wt, n_cap_pad};
+    auto it = tables.find(key);
+    if (it != tables.end()) return it->second.get();
+    std::vector<std::array<int, 3>> cap_pos(n_cap_pad), img_pos(n_img_pad, {0, 0, 0});
+    for (int64_t i = 0; i < n_cap_pad; ++i) cap_pos[i] = {(int)(1 + i), 0, 0};
+    for (int64_t hh = 0; hh < Ht; ++hh)
+      for (int64_t ww = 0; ww < Wt; ++ww) img_pos[hh * Wt + ww] = {(int)(n_cap_pad + 1), (int)hh, (int)ww};
+    std::vector<std::array<int, 3>> uni_pos = img_pos;
+    uni_pos.insert(uni_pos.end(), cap_pos.begin(), cap_pos.end());
+    std::unique_ptr<DBuf[]> t(new DBuf[6]);
+    const std::vector<std::array<int, 3>>* sets[3] = {&img_pos, &cap_pos, &uni_pos};
+    for (int i = 0; i < 3; ++i) {
+      std::vector<float> c, s;
+      rope_tables(*sets[i], c, s);
+      const size_t bytes = c.size() * 4;
+      t[2 * i].ensure(bytes);
+      t[2 * i + 1].ensure(bytes);
+      check_cuda(cudaMemcpy(t[2 * i].p, c.data(), bytes, cudaMemcpyHostToDevice), "zimage tables");
+      check_cuda(cudaMemcpy(t[2 * i + 1].p, s.data(), bytes, cudaMemcpyHostToDevice), "zimage tables");
+    }
+    DBuf* raw = t.get();
+    tables[key] = std::move(t);
+    return raw;
+  }
+
+  // One block on x [B*S, D] (B sequences of S rows), rotary tables [S, 128].
+  void run_block(const Block& b, float* x, int64_t B, int64_t S, const float* cs, const float* sn, bool modulated) {
+    const int64_t R = B * S;
+    const float *scale_msa = nullptr, *gate_msa = nullptr, *scale_mlp = nullptr, *gate_mlp = nullptr;
+    if (modulated) {
+      gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, b.adaln, tdim, mod.as<float>(), 4 * D, b.adaln_b,
+                        false);
+      dit_adaln_split(mod.as<float>(), (int)D);
+      scale_msa = mod.as<float>();
+      gate_msa = scale_msa + D;
+      scale_mlp = scale_msa + 2 * D;
+      gate_mlp = scale_msa + 3 * D;
+    }
+    // attention
+    dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.attn_norm1, scale_msa, norm_eps);
+    gemm_bf16_epilogue_impl(R, 3 * D, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * D, false,
+                            b.has_bqkv ? b.bqkv.as<float>() : nullptr, 0);
+    for (int64_t n = 0; n < B; ++n)
+      dit_qk_norm_rope_pack(qkv.as<float>() + n * S * 3 * D, (int)S, heads, b.norm_q, b.norm_k, cs, sn, 1e-5f,
+                            q16.as<uint8_t>() + n * S * D * 2, k16.as<uint8_t>() + n * S * D * 2,
+                            v16.as<uint8_t>() + n * S * D * 2);
+    launch_attention_f16(q16.p, k16.p, v16.p, ao.p, D, S * D, true, B, S, S, heads, heads, head_dim, 128, false);
+    gemm_bf16_epilogue_impl(R, D, D, ao.p, D, true, b.wout, D, a.p, D, false, b.bout, 0);
+    dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.attn_norm2, gate_msa, norm_eps);
+    // feed-forward
+    dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.ffn_norm1, scale_mlp, norm_eps);
+    gemm_bf16_epilogue_impl(R, 2 * b.F, D, h.p, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
+                            b.has_b13 ? b.b13.as<float>() : nullptr, 1);
+    gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0);
+    dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.ffn_norm2, gate_mlp, norm_eps);
+  }
+
+  static int64_t pad_to(int64_t n) { return (n + 31) / 32 * 32; }
+
+  // x [B, C, H, W], cap [B, L, capdim] -> out [B, C, H, W] (zimage.cpp:138-228).
+  void forward(const float* x_in, int64_t B, int64_t C, int64_t H, int64_t W, float t, const float* cap_in, int64_t L,
+               int64_t capdim, float* out) {
+    if (!finalized) fail(kErrInvalidArg, "zimage: finalize() not called");
+    const int64_t p = patch;
+    if (C != in_ch || H % p || W % p || B < 1) fail(kErrInvalidArg, "zimage: bad latent shape");
+    const int64_t Ht = H / p, Wt = W / p, n_img = Ht * Wt, n_img_pad = pad_to(n_img);
+    const int64_t n_cap_pad = pad_to(L), S = n_img_pad + n_cap_pad;
+    const int64_t F = layers[0].F;
+    cudaStream_t st = ctx().stream;
+    DBuf* tb = get_tables(Ht, Wt, n_img_pad, n_cap_pad);
+    // activations
+    const int64_t Rmax = B * S;
+    tok.ensure((size_t)(B * n_img * p * p * C) * 4);
+    img.ensure((size_t)(B * n_img_pad * D) * 4);
+    cap.ensure((size_t)(B * n_cap_pad * D) * 4);
+    uni.ensure((size_t)(Rmax * D) * 4);
+    h.ensure((size_t)(Rmax * D) * 2);
+    qkv.ensure((size_t)(Rmax * 3 * D) * 4);
+    q16.ensure((size_t)(Rmax * D) * 2);
+    k16.ensure((size_t)(Rmax * D) * 2);
+    v16.ensure((size_t)(Rmax * D) * 2);
+    ao.ensure((size_t)(Rmax * D) * 2);
+    a.ensure((size_t)(Rmax * D) * 4);
+    g.ensure((size_t)(Rmax * F) * 2);
+    mod.ensure((size_t)(4 * D) * 4);
+    const WRef& t0 = get("t_embedder.mlp.0.weight");
+    temb.ensure((size_t)tdim * 4);
+    thid.ensure((size_t)t0.dim(0) * 4);
+    adaln.ensure((size_t)tdim * 4);
+    fscale.ensure((size_t)D * 4);
+    capn.ensure((size_t)(B * L * capdim) * 4);
+    outtok.ensure((size_t)(B * n_img * p * p * C) * 4);
+    fin.ensure((size_t)(B * n_img * D) * 4);
+
+    // 1. timestep embedding -> adaln [1, tdim]
+    dit_timestep_embed(temb.as<float>(), (int)tdim, t * t_scale);
+    linear(temb.as<float>(), 1, tdim, t0, try_get("t_embedder.mlp.0.bias"), thid.as<float>());
+    op_unary(thid.as<float>(), t0.dim(0), 0);  // silu
+    linear(thid.as<float>(), 1, t0.dim(0), get("t_embedder.mlp.2.weight"), try_get("t_embedder.mlp.2.bias"),
+           adaln.as<float>());
+    // 2. image tokens: patchify, embed, pad
+    const int64_t tokw = p * p * C;
+    for (int64_t n = 0; n < B; ++n) {
+      op_patchify(x_in + n * C * H * W, tok.as<float>() + n * n_img * tokw, C, H, W, (int)p);
+      linear(tok.as<float>() + n * n_img * tokw, n_img, tokw, get("all_x_embedder.2-1.weight"),
+             try_get("all_x_embedder.2-1.bias"), img.as<float>() + n * n_img_pad * D);
+      dit_fill_rows(img.as<float>() + n * n_img_pad * D, f32("x_pad_token"), n_img, n_img_pad, (int)D);
+    }
+    // 3. text tokens: RMSNorm, embed, pad
+    op_row_norm(cap_in, capn.as<float>(), B * L, capdim, f32("cap_embedder.0.weight"), nullptr, norm_eps, true);
+    for (int64_t n = 0; n < B; ++n) {
+      linear(capn.as<float>() + n * L * capdim, L, capdim, get("cap_embedder.1.weight"), try_get("cap_embedder.1.bias"),
+             cap.as<float>() + n * n_cap_pad * D);
+      dit_fill_rows(cap.as<float>() + n * n_cap_pad * D, f32("cap_pad_token"), L, n_cap_pad, (int)D);
+    }
+    // refiners
+    for (const Block& b : noise)
+      run_block(b, img.as<float>(), B, n_img_pad, tb[0].as<float>(), tb[1].as<float>(), true);
+    for (const Block& b : context)
+      run_block(b, cap.as<float>(), B, n_cap_pad, tb[2].as<float>(), tb[3].as<float>(), false);
+    // 4. unified [image, text] per sample, main stack
+    for (int64_t n = 0; n < B; ++n) {
+      check_cuda(cudaMemcpyAsync(uni.as<float>() + n * S * D, img.as<float>() + n * n_img_pad * D,
+                                 (size_t)(n_img_pad * D) * 4, cudaMemcpyDeviceToDevice, st),
+                 "zimage concat");
+      check_cuda(cudaMemcpyAsync(uni.as<float>() + (n * S + n_img_pad) * D, cap.as<float>() + n * n_cap_pad * D,
+                                 (size_t)(n_cap_pad * D) * 4, cudaMemcpyDeviceToDevice, st),
+                 "zimage concat");
+    }
+    for (const Block& b : layers) run_block(b, uni.as<float>(), B, S, tb[4].as<float>(), tb[5].as<float>(), true);
+    // 5. final layer on the image tokens: LayerNorm * (1 + adaLN(silu(t_emb))), linear, unpatchify
+    {
+      check_cuda(cudaMemcpyAsync(temb.p, adaln.p, (size_t)tdim * 4, cudaMemcpyDeviceToDevice, st), "zimage final");
+      op_unary(temb.as<float>(), tdim, 0);  // silu(adaln) (the reference silus a copy)
+      linear(temb.as<float>(), 1, tdim, get("all_final_layer.2-1.adaLN_modulation.1.weight"),
+             try_get("all_final_layer.2-1.adaLN_modulation.1.bias"), fscale.as<float>());
+      op_affine(fscale.as<float>(), 1.0f, 1.0f, D);
+    }
+    for (int64_t n = 0; n < B; ++n) {
+      dit_layer_norm_mod(uni.as<float>() + n * S * D, fin.as<float>() + n * n_img * D, n_img, (int)D,
+                         fscale.as<float>(), 1e-6f);
+    }
+    linear(fin.as<float>(), B * n_img, D, get("all_final_layer.2-1.linear.weight"),
+           try_get("all_final_layer.2-1.linear.bias"), outtok.as<float>());
+    for (int64_t n = 0; n < B; ++n)
+      op_unpatchify(outtok.as<float>() + n * n_img * tokw, out + n * C * H * W, C, H, W, (int)p);
+  }
+};
+
+}  // namespace sdb
+
+// ===================================================================================
+using sdb::ZImage;
+
+#define SDB_GUARD(body)                 \
+  try {                                 \
+    body;                               \
+    return sdb::kOk;                    \
+  } catch (const sdb::Error& e) {       \
+    sdb::set_last_error(e.msg);         \
+    return e.code;                      \
+  } catch (const std::exception& e) {   \
+    sdb::set_last_error(e.what());      \
+    return sdb::kErrCuda;               \
+  }
+
+extern "C" {
+
+void* sdb200_zimage_create(int heads, int patch, float norm_eps, float rope_theta, float t_scale, int ax0, int ax1,
+                           int ax2) {
+  try {
+    if (heads <= 0 || patch <= 0) sdb::fail(sdb::kErrInvalidArg, "zimage_create: bad config");
+    return new ZImage(heads, patch, norm_eps, rope_theta, t_scale, ax0, ax1, ax2);
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return nullptr;
+  }
+}
+
+int sdb200_zimage_set_weight(void* m, const char* name, const void* dev_ptr, int is_bf16, const int64_t* shape,
+                             int ndim) {
+  SDB_GUARD({
+    if (!m || !name || !dev_ptr || !shape || ndim <= 0) sdb::fail(sdb::kErrInvalidArg, "zimage_set_weight: bad args");
+    ZImage* z = static_cast<ZImage*>(m);
+    if (z->finalized) sdb::fail(sdb::kErrInvalidArg, "zimage_set_weight: model already finalized");
+    sdb::WRef r;
+    r.p = dev_ptr;
+    r.bf16 = is_bf16 != 0;
+    r.shape.assign(shape, shape + ndim);
+    z->w[name] = r;
+  })
+}
+
+int sdb200_zimage_finalize(void* m) {
+  SDB_GUARD({
+    if (!m) sdb::fail(sdb::kErrInvalidArg, "zimage_finalize: null model");
+    static_cast<ZImage*>(m)->finalize();
+  })
+}
+
+int sdb200_zimage_forward(void* m, const float* x, int64_t B, int64_t C, int64_t H, int64_t W, float t,
+                          const float* cap, int64_t L, int64_t capdim, float* out) {
+  SDB_GUARD({
+    if (!m || !x || !cap || !out) sdb::fail(sdb::kErrInvalidArg, "zimage_forward: null pointer");
+    static_cast<ZImage*>(m)->forward(x, B, C, H, W, t, cap, L, capdim, out);
+  })
+}
+
+void sdb200_zimage_destroy(void* m) { delete static_cast<ZImage*>(m); }
+
+}  // extern "C"

@@ -70,6 +70,11 @@ _SIGS = {
     "sdb200_attention_f16": ([_v, _v, _v, _v, _i, _i64, _i64, _i64, _i, _i, _i64, _i64, _i], _i),
     "sdb200_pack_heads_f16": ([_v, _v, _i64, _i, _i64, _i64], _i),
     "sdb200_attention": ([_v, _v, _v, _v, _i64, _i64, _i64, _i, _i, _i64, _i], _i),
+    "sdb200_zimage_create": ([_i, _i, _f, _f, _f, _i, _i, _i], _v),
+    "sdb200_zimage_set_weight": ([_v, C.c_char_p, _v, _i, C.POINTER(_i64), _i], _i),
+    "sdb200_zimage_finalize": ([_v], _i),
+    "sdb200_zimage_forward": ([_v, _v, _i64, _i64, _i64, _i64, _f, _v, _i64, _i64, _v], _i),
+    "sdb200_zimage_destroy": ([_v], None),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
     "sdb200_group_norm": ([_v, _v, _i64, _i64, _i64, _i, _v, _v, _f], _i),
     "sdb200_layer_norm": ([_v, _v, _i64, _i64, _v, _v, _f], _i),

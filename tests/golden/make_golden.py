@@ -129,6 +129,20 @@ def main():
         pad = (k - 1) // 2
         y = ref.conv2d(x, w, b, stride, pad)
         np.savez(os.path.join(HERE, f"conv2d_{i}.npz"), x=x, w=w, b=b, y=y, dims=np.array([stride, pad]))
+    # Z-Image transformer (zimage.cpp:138-228), small seeded config; the weights are
+    # regenerated from the seed by the tests (sdb200.zimage.random_weights_numpy)
+    from sdb200.zimage import ZConfig, random_weights_numpy
+
+    for name, cfg, B_lat, L, t in [
+        ("zimage_small", ZConfig(dim=256, heads=2, ffn=512, t_dim=256, t_hidden=512, cap_dim=128, layers=2,
+                                 noise_refiners=1, context_refiners=1), (1, 16, 16, 16), 20, 0.6),
+    ]:
+        w, bf = random_weights_numpy(cfg, 0)
+        zr = np.random.default_rng(1)
+        x = zr.standard_normal(B_lat).astype(np.float32)
+        cap = zr.standard_normal((1, L, cfg.cap_dim)).astype(np.float32)
+        model = ref.zimage(w, bf, heads=cfg.heads)
+        np.savez(os.path.join(HERE, f"{name}.npz"), x=x, cap=cap, t=np.float32(t), out=model(x, t, cap))
     print("golden vectors written to", HERE)
 
 
