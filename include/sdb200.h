@@ -98,6 +98,19 @@ int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
                          int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
 
+/* No counterpart in the reference. The gemm_nt_bf16 contraction above, same kernels and
+ * results, for callers that cannot allocate device memory: code inside someone else's
+ * CUDA-graph capture, hosts whose framework owns every device allocation, loops where
+ * a synchronising cudaMalloc/cudaFree would stall. sdb200_gemm_nt_bf16 may grow a
+ * workspace and create a device context (both cudaMalloc); this entry point calls no
+ * allocator. A's bf16 copy goes to a fixed 32 MiB device array held by every GPU that
+ * loads the library: M * round_up(K, 8) <= 16,777,216, and B must be 16-byte aligned
+ * with ldb % 8 == 0, else SDB200_ERR_INVALID_ARG. The first call on a device resolves
+ * the array's address (cudaGetSymbolAddress): make it before any stream capture. All
+ * calls share the array; calls that overlap on the GPU race on it. */
+int sdb200_gemm_nt_bf16_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
+                                int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
+
 /* Fused-epilogue GEMM (extension; the reference runs these as separate kernels after
  * the GEMM: swiglu backend_cuda.h:61, geglu :60, bias backend_cuda.cu:239-241).
  *   epi 0: Y = A B^T + bias (fp32 or bf16 Y)

@@ -390,6 +390,39 @@ void launch_bn(const GemmCall& g, const GemmParams& p, int num_sms) {
   check_launch("gemm_tc");
 }
 
+// Same launch with the device facts passed in instead of read from the device
+// context, for callers that must not create one (the context allocates its error word).
+template <int BN, bool TF32>
+void launch_bn_explicit(const GemmCall& g, const GemmParams& p, int num_sms, cudaStream_t stream, int dev) {
+  using C_ = Cfg<BN>;
+  const int esz = TF32 ? 4 : 2;
+  const uint32_t bk = 128 / esz;
+  CUtensorMap ta, tb;
+  const CUtensorMapDataType dt = TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.M};
+    const uint64_t strides[1] = {(uint64_t)g.lda * esz};
+    const uint32_t box[2] = {bk, (uint32_t)kBM};
+    encode_tmap(&ta, dt, 2, g.A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.N};
+    const uint64_t strides[1] = {(uint64_t)g.ldb * esz};
+    const uint32_t box[2] = {bk, (uint32_t)BN};
+    encode_tmap(&tb, dt, 2, g.B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  auto kern = k_gemm_tc<BN, TF32>;
+  static bool attr_set[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM),
+               "cudaFuncSetAttribute(gemm)");
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(p.num_tiles, num_sms);
+  kern<<<grid, kThreads, C_::SMEM, stream>>>(ta, tb, p);
+  check_launch("gemm_tc");
+}
+
 int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
   (void)epi;  // every candidate BN is a multiple of the 32-column gated chunk
   const int cands[4] = {256, 192, 128, 64};
@@ -451,6 +484,34 @@ void launch_gemm_tc(const GemmCall& g) {
       case 128: launch_bn<128, false>(g, p, c.num_sms); break;
       default: launch_bn<64, false>(g, p, c.num_sms); break;
     }
+  }
+}
+
+// bf16 GEMM launch on an explicit device / stream / error word (no device context).
+void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream, int* err_word, int dev) {
+  GemmParams p{};
+  p.M = (int)g.M;
+  p.N = (int)g.N;
+  p.K = (int)g.K;
+  const int bn = g.bn ? g.bn : choose_bn(g.M, g.N, num_sms, g.epi);
+  p.m_tiles = (int)((g.M + kBM - 1) / kBM);
+  p.n_tiles = (int)((g.N + bn - 1) / bn);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = (int)((g.K + 63) / 64);
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.bias = g.bias;
+  p.accumulate = g.accumulate ? 1 : 0;
+  p.epi = (int)g.epi;
+  p.out_bf16 = g.out_bf16 ? 1 : 0;
+  const int oesz = g.out_bf16 ? 2 : 4;
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * oesz) % 16 == 0);
+  p.err = err_word;
+  switch (bn) {
+    case 256: launch_bn_explicit<256, false>(g, p, num_sms, stream, dev); break;
+    case 192: launch_bn_explicit<192, false>(g, p, num_sms, stream, dev); break;
+    case 128: launch_bn_explicit<128, false>(g, p, num_sms, stream, dev); break;
+    default: launch_bn_explicit<64, false>(g, p, num_sms, stream, dev); break;
   }
 }
 

@@ -50,6 +50,8 @@ struct DeviceContext {
 
 // Context of the calling thread's current device (created on first use).
 DeviceContext& ctx();
+// The context of device `dev` if one was already created, else null (never creates).
+DeviceContext* ctx_if_created(int dev);
 // Returns a workspace pointer of at least `bytes` bytes (256-byte aligned).
 void* workspace(size_t bytes);
 // Encodes a 2-D/3-D tiled tensor map through the driver entry point.
@@ -88,6 +90,8 @@ struct GemmCall {
 void launch_gemm_tc(const GemmCall& g);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
 void set_gemm_tile(int bn);
+// bf16 tcgen05 GEMM on an explicit device / stream / error word; no device context.
+void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream, int* err_word, int dev);
 // Small-M (M <= 16) GEMM through a memory-bound SIMT kernel (weights streamed once).
 void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
                         bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate);

@@ -71,6 +71,11 @@ DeviceContext& ctx() {
   return c;
 }
 
+DeviceContext* ctx_if_created(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  return g_ctx[dev].device >= 0 ? &g_ctx[dev] : nullptr;
+}
+
 void* workspace(size_t bytes) {
   DeviceContext& c = ctx();
   if (bytes <= c.ws_bytes) return c.ws;

@@ -64,6 +64,7 @@ _SIGS = {
     "sdb200_set_gemm_tile": ([_i], _i),
     "sdb200_gemm_nt_f32": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
+    "sdb200_gemm_nt_bf16_noalloc": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16a": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_bf16_epilogue": ([_i64, _i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i, _v, _i], _i),
     "sdb200_set_attention_path": ([_i], _i),
