@@ -1,31 +1,36 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gemm]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload dit|gemm]
 
-Workload `gemm`: the Z-Image fused-QKV projection
-Y[4096, 11520] = X[4096, 3840] (fp32) * W[11520, 3840]^T (bf16) + b, fp32 accumulate,
-through sdb200_gemm_nt_bf16 (the drop-in for the reference's gemm_nt_bf16). One step =
-one such GEMM on each GPU. The GPUs run independent replicas (no collective: one GEMM
-does not shard across devices), so the value is the sum over GPUs ("scaling": "weak").
+Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
+random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
+width 2560 ~N(0,1)), one denoising step = one transformer forward over a global batch of
+8 images. The 8 images are split across the N ranks (8/N per GPU, weights replicated,
+no collective: image forwards are independent), so total work is fixed: "scaling":
+"strong". Metric: ms per denoising step for the whole batch (lower is better), max over
+ranks of CUDA-event time.
+
+Workload `gemm`: Y[4096,11520] = X[4096,3840] W[11520,3840]^T + b,
+one GEMM per GPU per step (replicas), TFLOP/s.
 
 Printed on rank 0 as one JSON line:
-  value      TFLOP/s of the whole job, inputs resident in HBM (2*M*N*K per step)
-  e2e        the same metric through the C ABI with pinned HOST buffers: H2D of X and
-             D2H of Y inside the timed region (W is resident, as the reference keeps
-             weights on the device after Weights::to_device)
-  roofline   the tensor-core GEMM kernel alone (A pre-packed to bf16), timed with CUDA
-             events on the library's stream, against MEASURED_PEAKS.json bf16 burst peak
-  cpu_baseline  the reference's own CPU gemm_nt_bf16 (oracle/_ref, compiled from its
-             sources) on this host's cores, rank 0 at N=1 only
-The inputs (340 MB per step: X 63 MB, W 88 MB, Y 189 MB) exceed the 126 MB L2, so no
-explicit flush is needed between timed iterations.
-
---impl reference runs the reference's CPU implementation of the same GEMM (rank 0
-only) and prints the same line with "impl": "reference".
+  value / ms_per_step  inputs resident in HBM
+  e2e          the same metric through the C ABI with pinned HOST buffers: H2D of the
+               step's latents and text states, D2H of the prediction, inside the timed
+               region (weights resident, as after Weights::to_device)
+  roofline     the dominant kernel (the tcgen05 GEMM) timed live with CUDA events on the
+               library's stream across one profiled step: algorithmic FLOPs / kernel time,
+               against MEASURED_PEAKS.json (sustained bf16 peak for a kernel inside a long
+               step; burst for the isolated GEMM workload)
+  cpu_baseline the reference's own CPU forward (oracle/_ref, compiled from its sources) on
+               a bounded sample: one full-width block at 1024^2, scaled by FLOPs to the step
+  gpu_launches kernels this library launched inside the timed region (counted by the library)
+--impl reference times the reference's CPU implementation of the same workload (rank 0).
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -38,9 +43,9 @@ sys.path.insert(0, os.path.join(ROOT, "stablediffusion-cpp_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 METRIC = "bf16 GEMM TFLOP/s (% tcgen05 peak); Z-Image DiT ms/step @1024² at 1/2/4/8 GPUs"
-M_, N_, K_ = 4096, 11520, 3840
-FLOP = 2.0 * M_ * N_ * K_
-
+GLOBAL_BATCH = 8
+LAT_H = LAT_W = 128        # 1024x1024 image / 8 (VAE)
+TEXT_TOKENS = 128
 THROTTLE_BITS = {
     0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
     0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
@@ -53,17 +58,18 @@ def peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d["bf16_tflops"], d["hbm_gbs"], "measured"
-    return 1590.0, 6650.0, "fallback"
+        return {"burst": d["bf16_tflops"], "sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "hbm": d["hbm_gbs"], "kind": "measured"}
+    return {"burst": 1590.0, "sustained": 1400.0, "hbm": 6650.0, "kind": "fallback"}
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gemm_tc_cfg1.md")
+def profile_value(fname, key):
+    """A `key: value` line from a committed ncu summary under profiles/."""
+    p = os.path.join(ROOT, "profiles", fname)
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip())
             except ValueError:
@@ -124,230 +130,380 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
+# ---------------------------------------------------------------------------------------
+# FLOP model of one Z-Image forward (algorithmic: 2*M*N*K per GEMM, 4*S^2*D per attention)
+# ---------------------------------------------------------------------------------------
+def dit_forward_flops(cfg, H=LAT_H, W=LAT_W, L=TEXT_TOKENS):
+    pad = lambda n: (n + 31) // 32 * 32  # noqa: E731
+    D, F, T = cfg.dim, cfg.ffn, cfg.t_dim
+    n_img = (H // cfg.patch) * (W // cfg.patch)
+    s_img, s_cap = pad(n_img), pad(L)
+    s_uni = s_img + s_cap
+    pc = cfg.patch * cfg.patch * cfg.in_channels
+
+    def block(S, modulated):
+        lin = 2.0 * S * (4 * D * D + 3 * D * F)
+        att = 4.0 * S * S * D
+        mod = 2.0 * 4 * D * T if modulated else 0.0
+        return lin, att, mod
+
+    lin = att = small = 0.0
+    for S, n, m in ((s_img, cfg.noise_refiners, True), (s_cap, cfg.context_refiners, False),
+                    (s_uni, cfg.layers, True)):
+        a, b, c = block(S, m)
+        lin += n * a
+        att += n * b
+        small += n * c
+    small += 2.0 * n_img * pc * D + 2.0 * L * cfg.cap_dim * D + 2.0 * n_img * D * pc
+    small += 2.0 * (cfg.t_hidden * T * 2 + D * T)
+    return {"total": lin + att + small, "linear": lin, "attention": att, "small": small}
+
+
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), int(
+        os.environ.get("LOCAL_RANK", "0"))
 
 
-def run_reference(args, world, rank):
-    """The reference's own CPU GEMM (oracle/_ref) on this host's cores: bounded sample
-    of the same workload per step (512 rows of X, i.e. 1/8 of the GEMM)."""
-    if rank != 0:
-        return
+# ---------------------------------------------------------------------------------------
+# Reference CPU path (oracle/_ref: the reference's own tensor.cpp / zimage.cpp)
+# ---------------------------------------------------------------------------------------
+def ref_dit_block_sample():
+    """The reference ZImageTransformer with one full-width layer (no refiners) at 1024^2:
+    returns (callable forward, sample FLOPs, threads, model keep-alive)."""
     import numpy as np
 
     from oracle import RefCPU
+    from sdb200.zimage import ZConfig, random_weights_numpy
 
     ref = RefCPU()
     ref.set_num_threads(0)
-    cores = ref.num_threads()
-    rows = 512
-    rng = np.random.default_rng(0)
-    X = rng.standard_normal((rows, K_), dtype=np.float32)
-    Wh = ref.to_bf16((0.02 * rng.standard_normal((N_, K_), dtype=np.float32)).astype(np.float32))
-    b = (0.01 * rng.standard_normal(N_, dtype=np.float32)).astype(np.float32)
-    for _ in range(args.warmup):
-        ref.gemm_nt_bf16(X, Wh, b)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        ref.gemm_nt_bf16(X, Wh, b)
-    dt = (time.perf_counter() - t0) / args.steps
-    tflops = 2.0 * rows * N_ * K_ / dt / 1e12
-    line = {
-        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 * (M_ / rows),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 x bf16 -> f32",
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights)",
-        "config": {"workload": "cfg1 fused-QKV GEMM 4096x11520x3840 bf16 weights (+bias)",
-                   "parallelism": "reference CPU thread pool", "sample_rows": rows},
-        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
-                         "sample": f"{rows} of 4096 rows of X per step (1/8 of the GEMM), all {N_} columns"},
-        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    cfg = ZConfig(layers=1, noise_refiners=0, context_refiners=0)
+    w, bf = random_weights_numpy(cfg, 11)
+    model = ref.zimage(w, bf, heads=cfg.heads)
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((1, cfg.in_channels, LAT_H, LAT_W)).astype(np.float32)
+    cap = rng.standard_normal((1, TEXT_TOKENS, cfg.cap_dim)).astype(np.float32)
+    return (lambda: model(x, 0.5, cap)), dit_forward_flops(cfg)["total"], ref.num_threads(), model
 
 
-def cpu_baseline_sample():
-    """Reference CPU gemm_nt_bf16 timed on 512 rows (about 2-3 s of CPU work)."""
+def ref_gemm_sample(rows=512):
+    import numpy as np
+
+    from oracle import RefCPU
+    from sdb200.workloads import cfg1_inputs
+
+    ref = RefCPU()
+    ref.set_num_threads(0)
+    X, W, b = cfg1_inputs()
+    Xs = np.ascontiguousarray(X[:rows])
+    Wh = ref.to_bf16(W)
+    return (lambda: ref.gemm_nt_bf16(Xs, Wh, b)), 2.0 * rows * W.shape[0] * W.shape[1], ref.num_threads(), None
+
+
+def cpu_baseline(workload, reps=1):
     try:
-        import numpy as np
-
         from oracle import RefCPU
 
         if not RefCPU.available():
-            return None
-        ref = RefCPU()
-        ref.set_num_threads(0)
-        rows = 512
-        rng = np.random.default_rng(0)
-        X = rng.standard_normal((rows, K_), dtype=np.float32)
-        Wh = ref.to_bf16((0.02 * rng.standard_normal((N_, K_), dtype=np.float32)).astype(np.float32))
-        b = (0.01 * rng.standard_normal(N_, dtype=np.float32)).astype(np.float32)
-        ref.gemm_nt_bf16(X, Wh, b)
-        reps = 3
+            return {"value": None, "unit": None, "cores": None, "kind": "reference",
+                    "sample": "oracle/_ref/libsdref.so not built"}
+        if workload == "dit":
+            from sdb200.zimage import Z_IMAGE
+
+            fn, sample_flop, cores, _keep = ref_dit_block_sample()
+            fn()  # warm-up (thread pool, page-in)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                fn()
+            dt = (time.perf_counter() - t0) / reps
+            step_flop = GLOBAL_BATCH * dit_forward_flops(Z_IMAGE)["total"]
+            return {"value": dt * 1e3 * step_flop / sample_flop, "unit": "ms/step", "cores": cores,
+                    "kind": "reference",
+                    "sample": f"reference ZImageTransformer forward with one full-width block at 1024^2 "
+                              f"({sample_flop / 1e12:.2f} TFLOP, {dt:.2f} s), scaled by FLOPs to a step of "
+                              f"{GLOBAL_BATCH} full 30-layer forwards ({step_flop / 1e12:.0f} TFLOP)"}
+        fn, flop, cores, _ = ref_gemm_sample()
+        fn()
         t0 = time.perf_counter()
-        for _ in range(reps):
-            ref.gemm_nt_bf16(X, Wh, b)
-        dt = (time.perf_counter() - t0) / reps
-        return {"value": 2.0 * rows * N_ * K_ / dt / 1e12, "unit": "TFLOP/s", "cores": ref.num_threads(),
-                "kind": "reference",
-                "sample": f"{rows} of 4096 rows of the cfg1 GEMM, {reps} reps after 1 warm-up, reference "
-                          "gemm_nt_bf16 (tensor.cpp:412) built from its sources"}
-    except Exception as e:  # the baseline is reported, never required
-        return {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference", "sample": f"failed: {e}"}
+        for _ in range(max(reps, 3)):
+            fn()
+        dt = (time.perf_counter() - t0) / max(reps, 3)
+        return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                "sample": "512 of 4096 rows of the cfg1 GEMM, reference gemm_nt_bf16 (tensor.cpp:412)"}
+    except Exception as e:  # reported, never required
+        return {"value": None, "unit": None, "cores": None, "kind": "reference", "sample": f"failed: {e}"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU implementation, rank 0 only."""
+    if rank != 0:
+        return
+    if args.workload == "dit":
+        from sdb200.zimage import Z_IMAGE
+
+        fn, sample_flop, cores, _keep = ref_dit_block_sample()
+        step_flop = GLOBAL_BATCH * dit_forward_flops(Z_IMAGE)["total"]
+        for _ in range(args.warmup):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        ms = dt * 1e3 * step_flop / sample_flop
+        line = {"impl": "reference", "metric": METRIC, "value": ms, "unit": "ms/step", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32 activations x bf16 weights (CPU)",
+                "data": "synthetic (random-init weights, N(0,1) latents and text states)",
+                "config": {"workload": "cfg4: 30-layer Z-Image DiT @1024^2, batch of 8 images, one denoising step",
+                           "parallelism": "reference CPU thread pool"},
+                "cpu_baseline": {"value": ms, "unit": "ms/step", "cores": cores, "kind": "reference",
+                                 "sample": f"one full-width block forward per step ({dt:.2f} s), scaled by FLOPs "
+                                           f"({sample_flop / 1e12:.2f} -> {step_flop / 1e12:.0f} TFLOP)"},
+                "e2e": {"value": ms, "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    else:
+        fn, flop, cores, _ = ref_gemm_sample()
+        for _ in range(args.warmup):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        v = flop / dt / 1e12
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 * 8, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 x bf16 -> f32 (CPU)",
+                "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights)",
+                "config": {"workload": "cfg1 fused-QKV GEMM 4096x11520x3840", "sample_rows": 512},
+                "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                                 "sample": "512 of 4096 rows per step"},
+                "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+def timed_loop(fn, steps, stream, pg, dev):
+    """CUDA-event time of `steps` calls on `stream`, barrier + synchronize on both sides,
+    max over ranks."""
+    import torch
+
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if pg:
+        pg.barrier()
+    t = torch.tensor([ms], device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_dit(args, world, rank, local, pg, dev):
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+    from sdb200.zimage import Z_IMAGE, ZImageB200, random_weights_torch
+
+    L = sdb200.lib()
+    if GLOBAL_BATCH % world:
+        raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} GPUs")
+    B = GLOBAL_BATCH // world
+    cfg = Z_IMAGE
+    model = ZImageB200(random_weights_torch(cfg, 0, dev), cfg)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn((B, cfg.in_channels, LAT_H, LAT_W), generator=g, device=dev)
+    cap = torch.randn((B, TEXT_TOKENS, cfg.cap_dim), generator=g, device=dev)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    step = lambda: model.forward(x, 0.5, cap, out)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    ms_step = ms / args.steps
+    fl = dit_forward_flops(cfg)
+    step_flop = GLOBAL_BATCH * fl["total"]
+
+    # one profiled step: GEMM and attention kernels timed live with CUDA events
+    model.profile(True)
+    step()
+    prof = model.profile_read()
+    model.profile(False)
+    pk = peaks()
+    gemm_tf = prof["gemm_flop"] / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] else None
+    attn_tf = prof["attn_flop"] / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] else None
+
+    # end to end through the C ABI: latents + text states in from pinned host memory,
+    # prediction back out, every step
+    xh = x.cpu().pin_memory()
+    caph = cap.cpu().pin_memory()
+    outh = torch.empty_like(out, device="cpu").pin_memory()
+    xd, capd = torch.empty_like(x), torch.empty_like(cap)
+
+    def e2e_step():
+        sdb200.check(L.sdb200_upload(xd.data_ptr(), xh.data_ptr(), xh.numel() * 4))
+        sdb200.check(L.sdb200_upload(capd.data_ptr(), caph.data_ptr(), caph.numel() * 4))
+        model.forward(xd, 0.5, capd, out)
+        sdb200.check(L.sdb200_download(outh.data_ptr(), out.data_ptr(), outh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev) / args.steps
+    err = be.device_error_word()
+    cpu = cpu_baseline("dit") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 GEMM operands, fp16 attention operands, fp32 accumulate/activations",
+            "data": "synthetic (random-init Z-Image-shaped weights, N(0,1) latents and text states)",
+            "config": {"workload": "cfg4: 30-layer Z-Image DiT (dim 3840, 30 heads, FFN 10240, 2+2 refiners) "
+                                   "@1024^2, 128 text tokens, global batch 8 images per denoising step",
+                       "global_batch": GLOBAL_BATCH, "images_per_gpu": B, "seq_len": 4224,
+                       "parallelism": f"image-parallel x{world} (no collective)",
+                       "l2": "weights 12.3 GB + activations > 126 MB L2 per step, no flush needed"},
+            "images_per_s": GLOBAL_BATCH / (ms_step * 1e-3),
+            "step_tflops": step_flop / (ms_step * 1e-3) / 1e12,
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all GEMMs of one step, rank 0)",
+                         "achieved": gemm_tf, "peak": pk["sustained"], "unit": "TFLOP/s",
+                         "frac": (gemm_tf / pk["sustained"]) if gemm_tf else None,
+                         "peak_kind": f"{pk['kind']} bf16 sustained",
+                         "traffic": profile_value("gemm_tc_cfg1.md", "traffic_bytes_per_launch"),
+                         "traffic_note": "ncu DRAM bytes of the cfg1 GEMM launch (profiles/gemm_tc_cfg1.md)",
+                         "gemm_ms_per_step": prof["gemm_ms"], "gemm_launches_per_step": prof["gemm_launches"],
+                         "attention_tflops": attn_tf, "attention_ms_per_step": prof["attn_ms"],
+                         "forward_ms_profiled": prof["forward_ms"]},
+            "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
+                    "d2h_bytes_per_step": int(outh.numel() * 4)},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "device_error_word": err,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_gemm(args, world, rank, local, pg, dev):
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+    from sdb200.workloads import cfg1_inputs, f32_to_bf16_bits
+
+    L = sdb200.lib()
+    M, N, K = 4096, 11520, 3840
+    FLOP = 2.0 * M * N * K
+    X, W, b = cfg1_inputs()
+    Wbits = f32_to_bf16_bits(W)
+    Xd = torch.from_numpy(X).to(dev)
+    Wd = torch.from_numpy(Wbits.view("int16")).to(dev).view(torch.bfloat16)
+    bd = torch.from_numpy(b).to(dev)
+    Yd = torch.empty((M, N), device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        sdb200.check(L.sdb200_gemm_nt_bf16(M, N, K, Xd.data_ptr(), K, Wd.data_ptr(), K, Yd.data_ptr(), N,
+                                           bd.data_ptr(), 0))
+
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    value = FLOP * args.steps * world / (ms * 1e-3) / 1e12
+    # the tensor-core kernel alone (A pre-packed to bf16)
+    Xbf = Xd.to(torch.bfloat16)
+    kstep = lambda: sdb200.check(L.sdb200_gemm_nt_bf16a(M, N, K, Xbf.data_ptr(), K, Wd.data_ptr(), K,  # noqa: E731
+                                                         Yd.data_ptr(), N, bd.data_ptr(), 0))
+    for _ in range(3):
+        kstep()
+    reps = max(args.steps, 10)
+    kms = timed_loop(kstep, reps, stream, None, dev) / reps
+    pk = peaks()
+    achieved = FLOP / (kms * 1e-3) / 1e12
+    Xh = torch.from_numpy(X).pin_memory()
+    Yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    Xs = torch.empty_like(Xd)
+
+    def e2e_step():
+        sdb200.check(L.sdb200_upload(Xs.data_ptr(), Xh.data_ptr(), Xh.numel() * 4))
+        sdb200.check(L.sdb200_gemm_nt_bf16(M, N, K, Xs.data_ptr(), K, Wd.data_ptr(), K, Yd.data_ptr(), N,
+                                           bd.data_ptr(), 0))
+        sdb200.check(L.sdb200_download(Yh.data_ptr(), Yd.data_ptr(), Yh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
+    e2e_value = FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12
+    err = be.device_error_word()
+    cpu = cpu_baseline("gemm") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 x bf16 -> f32 (A rounded from f32)",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights, N(0,0.01) bias)",
+            "config": {"workload": "cfg1 fused-QKV GEMM Y[4096,11520] = X[4096,3840] W[11520,3840]^T + b",
+                       "global_batch": world, "parallelism": f"replicas x{world} (no collective)",
+                       "l2": "inputs 340 MB/step > 126 MB L2, no flush"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 kind::f16, 128x256 tiles)",
+                         "achieved": achieved, "peak": pk["burst"], "unit": "TFLOP/s", "frac": achieved / pk["burst"],
+                         "peak_kind": f"{pk['kind']} bf16 burst",
+                         "traffic": profile_value("gemm_tc_cfg1.md", "traffic_bytes_per_launch"), "kernel_ms": kms},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(Xh.numel() * 4),
+                    "d2h_bytes_per_step": int(Yh.numel() * 4)},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "device_error_word": err,
+        }
+        print(json.dumps(line), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemm", choices=["gemm"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "gemm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
-
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
-    import numpy as np
     import torch
 
     torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     pg = None
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = dist
-
     import sdb200
     from sdb200 import backend as be
 
     if not sdb200.available():
         raise SystemExit("libsdb200: no usable sm_100 device: " + sdb200.lib().sdb200_last_error().decode())
     be.bind_stream()
-    L = sdb200.lib()
-
-    from sdb200.workloads import cfg1_inputs, f32_to_bf16_bits
-
-    X, W, b = cfg1_inputs()
-    Wbits = f32_to_bf16_bits(W)  # bf16 rounding of the weights, as Tensor::to_bf16 does at load time
-    dev = torch.device("cuda", local)
-    Xd = torch.from_numpy(X).to(dev)
-    Wd = torch.from_numpy(Wbits.view(np.int16)).to(dev).view(torch.bfloat16)
-    bd = torch.from_numpy(b).to(dev)
-    Yd = torch.empty((M_, N_), device=dev)
-    stream = torch.cuda.current_stream()
-
-    def step():
-        sdb200.check(L.sdb200_gemm_nt_bf16(M_, N_, K_, Xd.data_ptr(), K_, Wd.data_ptr(), K_, Yd.data_ptr(), N_,
-                                           bd.data_ptr(), 0))
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    t = torch.tensor([ms], device=dev)
-    if pg:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = FLOP * args.steps * world / (ms_max * 1e-3) / 1e12
-
-    # ---- dominant kernel alone: tcgen05 GEMM with A pre-packed to bf16 ----------
-    Xbf = Xd.to(torch.bfloat16)  # A operand as the pack kernel produces it (RNE)
-    for _ in range(3):
-        sdb200.check(L.sdb200_gemm_nt_bf16a(M_, N_, K_, Xbf.data_ptr(), K_, Wd.data_ptr(), K_, Yd.data_ptr(), N_,
-                                            bd.data_ptr(), 0))
-    torch.cuda.synchronize()
-    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(args.steps, 10)
-    k0.record(stream)
-    for _ in range(reps):
-        sdb200.check(L.sdb200_gemm_nt_bf16a(M_, N_, K_, Xbf.data_ptr(), K_, Wd.data_ptr(), K_, Yd.data_ptr(), N_,
-                                            bd.data_ptr(), 0))
-    k1.record(stream)
-    torch.cuda.synchronize()
-    kms = k0.elapsed_time(k1) / reps
-    peak_tf, _, peak_kind = peaks()
-    achieved = FLOP / (kms * 1e-3) / 1e12
-
-    # ---- end to end through the C ABI with host buffers ---------------------------
-    Xh = torch.from_numpy(X).pin_memory()
-    Yh = torch.empty((M_, N_), dtype=torch.float32).pin_memory()
-    Xs = torch.empty_like(Xd)
-
-    def e2e_step():
-        sdb200.check(L.sdb200_upload(Xs.data_ptr(), Xh.data_ptr(), Xh.numel() * 4))
-        sdb200.check(L.sdb200_gemm_nt_bf16(M_, N_, K_, Xs.data_ptr(), K_, Wd.data_ptr(), K_, Yd.data_ptr(), N_,
-                                           bd.data_ptr(), 0))
-        sdb200.check(L.sdb200_download(Yh.data_ptr(), Yd.data_ptr(), Yh.numel() * 4))
-
-    for _ in range(2):
-        e2e_step()
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    a1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = a0.elapsed_time(a1)
-    t = torch.tensor([e2e_ms], device=dev)
-    if pg:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    e2e_value = FLOP * args.steps * world / (float(t.item()) * 1e-3) / 1e12
-    ok_err = be.device_error_word()
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample()
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16 x bf16 -> f32 (A rounded from f32)",
-            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights, N(0,0.01) bias)",
-            "config": {"workload": "cfg1 fused-QKV GEMM Y[4096,11520] = X[4096,3840] W[11520,3840]^T + b",
-                       "global_batch": world, "parallelism": f"replicas x{world} (no collective)",
-                       "l2": "inputs 340 MB/step > 126 MB L2, no flush"},
-            "gpu_launches": 2 * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc<256,false> (tcgen05 kind::f16, 128x256 tiles)",
-                         "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                         "peak_kind": f"{peak_kind} bf16 burst", "traffic": traffic_from_profile(),
-                         "kernel_ms": kms},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(Xh.numel() * 4),
-                    "d2h_bytes_per_step": int(Yh.numel() * 4)},
-            "cpu_baseline": cpu,
-            "clocks": clk.summary(),
-            "device_error_word": ok_err,
-        }
-        print(json.dumps(line), flush=True)
+    if args.workload == "dit":
+        run_dit(args, world, rank, local, pg, dev)
+    else:
+        run_gemm(args, world, rank, local, pg, dev)
     if pg:
         pg.barrier()
         pg.destroy_process_group()

@@ -46,6 +46,8 @@ extern "C" {
 
 /* ---- library / device ---------------------------------------------------------- */
 int sdb200_version(void);
+/* Number of kernels this library has launched in this process (all devices). */
+unsigned long long sdb200_launch_count(void);
 const char* sdb200_last_error(void);
 /* backend_cuda.h:24 available(): 1 if a B200-class (sm_100) device is usable. */
 int sdb200_available(void);
@@ -163,6 +165,11 @@ int sdb200_zimage_finalize(void* model);
 int sdb200_zimage_forward(void* model, const float* x, int64_t B, int64_t C, int64_t H, int64_t W, float t,
                           const float* cap, int64_t L, int64_t capdim, float* out);
 void sdb200_zimage_destroy(void* model);
+/* Per-kernel timing of later forwards with CUDA events on the stream (enable != 0).
+ * profile_read fills out8 = {GEMM ms, GEMM FLOP, GEMM launches, attention ms, attention
+ * FLOP, attention launches, forward ms, forwards} since the last read, synchronising. */
+int sdb200_zimage_profile(void* model, int enable);
+int sdb200_zimage_profile_read(void* model, double* out8);
 
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
 /* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */

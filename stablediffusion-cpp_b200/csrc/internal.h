@@ -20,8 +20,9 @@ struct Error {
 };
 [[noreturn]] void fail(int code, const std::string& msg);
 void check_cuda(cudaError_t e, const char* what);
-// Checks the launch status of the last kernel (does not synchronise).
+// Checks the launch status of the last kernel (does not synchronise) and counts it.
 void check_launch(const char* what);
+unsigned long long launch_count();
 
 // Status codes of the C ABI.
 enum : int {

@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -41,7 +42,13 @@ void check_cuda(cudaError_t e, const char* what) {
          std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
   }
 }
-void check_launch(const char* what) { check_cuda(cudaGetLastError(), what); }
+// Every kernel launch of the library ends in check_launch, so this counts them.
+static std::atomic<unsigned long long> g_launches{0};
+void check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  check_cuda(cudaGetLastError(), what);
+}
+unsigned long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 static void init_context(DeviceContext& c, int dev) {
   cudaDeviceProp prop;
@@ -220,6 +227,8 @@ extern "C" {
 const char* sdb200_last_error(void) { return g_last_error.c_str(); }
 
 int sdb200_version(void) { return SDB200_ABI_VERSION; }
+
+unsigned long long sdb200_launch_count(void) { return sdb::launch_count(); }
 
 int sdb200_available(void) {
   int n = 0;

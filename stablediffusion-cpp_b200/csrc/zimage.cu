@@ -128,6 +128,55 @@ class ZImage {
 
   ZImage(int h, int p, float eps, float theta, float ts, int a0, int a1, int a2)
       : heads(h), patch(p), norm_eps(eps), rope_theta(theta), t_scale(ts), axes{a0, a1, a2} {}
+  ~ZImage() { prof_clear(); }
+
+  // ---- optional per-kernel timing (CUDA events on the stream) ------------------------
+  // Category 0: tensor-core GEMMs, 1: attention, 2: whole forward. FLOPs are the
+  // algorithmic 2*M*N*K (GEMM) and 4*Sq*Skv*d*heads (attention).
+  bool prof_on = false;
+  struct Mark {
+    cudaEvent_t a, b;
+    int cat;
+    double flop;
+  };
+  std::vector<Mark> marks;
+  template <class Fn>
+  void timed(int cat, double flop, Fn&& fn) {
+    if (!prof_on) return fn();
+    Mark m{nullptr, nullptr, cat, flop};
+    check_cuda(cudaEventCreate(&m.a), "cudaEventCreate");
+    check_cuda(cudaEventCreate(&m.b), "cudaEventCreate");
+    check_cuda(cudaEventRecord(m.a, ctx().stream), "cudaEventRecord");
+    fn();
+    check_cuda(cudaEventRecord(m.b, ctx().stream), "cudaEventRecord");
+    marks.push_back(m);
+  }
+  void prof_clear() {
+    for (Mark& m : marks) {
+      cudaEventDestroy(m.a);
+      cudaEventDestroy(m.b);
+    }
+    marks.clear();
+  }
+  // out[0..8]: gemm ms, gemm flop, gemm launches, attention ms, attention flop,
+  // attention launches, forward ms, forwards. Synchronises; resets the record.
+  void prof_read(double* out) {
+    for (int i = 0; i < 8; ++i) out[i] = 0.0;
+    check_cuda(cudaStreamSynchronize(ctx().stream), "profile sync");
+    for (Mark& m : marks) {
+      float ms = 0.0f;
+      check_cuda(cudaEventElapsedTime(&ms, m.a, m.b), "cudaEventElapsedTime");
+      const int base = m.cat == 0 ? 0 : m.cat == 1 ? 3 : 6;
+      out[base] += ms;
+      if (m.cat < 2) {
+        out[base + 1] += m.flop;
+        out[base + 2] += 1.0;
+      } else {
+        out[7] += 1.0;
+      }
+    }
+    prof_clear();
+  }
 
   const WRef& get(const std::string& n) const {
     auto it = w.find(n);
@@ -296,20 +345,27 @@ class ZImage {
     }
     // attention
     dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.attn_norm1, scale_msa, norm_eps);
-    gemm_bf16_epilogue_impl(R, 3 * D, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * D, false,
-                            b.has_bqkv ? b.bqkv.as<float>() : nullptr, 0);
+    const double gf = 2.0 * (double)R * (double)D;  // 2*M*K, times N per GEMM below
+    timed(0, gf * 3 * D, [&] {
+      gemm_bf16_epilogue_impl(R, 3 * D, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * D, false,
+                              b.has_bqkv ? b.bqkv.as<float>() : nullptr, 0);
+    });
     for (int64_t n = 0; n < B; ++n)
       dit_qk_norm_rope_pack(qkv.as<float>() + n * S * 3 * D, (int)S, heads, b.norm_q, b.norm_k, cs, sn, 1e-5f,
                             q16.as<uint8_t>() + n * S * D * 2, k16.as<uint8_t>() + n * S * D * 2,
                             v16.as<uint8_t>() + n * S * D * 2);
-    launch_attention_f16(q16.p, k16.p, v16.p, ao.p, D, S * D, true, B, S, S, heads, heads, head_dim, 128, false);
-    gemm_bf16_epilogue_impl(R, D, D, ao.p, D, true, b.wout, D, a.p, D, false, b.bout, 0);
+    timed(1, 4.0 * (double)B * S * S * D, [&] {
+      launch_attention_f16(q16.p, k16.p, v16.p, ao.p, D, S * D, true, B, S, S, heads, heads, head_dim, 128, false);
+    });
+    timed(0, gf * D, [&] { gemm_bf16_epilogue_impl(R, D, D, ao.p, D, true, b.wout, D, a.p, D, false, b.bout, 0); });
     dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.attn_norm2, gate_msa, norm_eps);
     // feed-forward
     dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.ffn_norm1, scale_mlp, norm_eps);
-    gemm_bf16_epilogue_impl(R, 2 * b.F, D, h.p, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
-                            b.has_b13 ? b.b13.as<float>() : nullptr, 1);
-    gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0);
+    timed(0, gf * 2 * b.F, [&] {
+      gemm_bf16_epilogue_impl(R, 2 * b.F, D, h.p, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
+                              b.has_b13 ? b.b13.as<float>() : nullptr, 1);
+    });
+    timed(0, gf * b.F, [&] { gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0); });
     dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.ffn_norm2, gate_mlp, norm_eps);
   }
 
@@ -319,6 +375,11 @@ class ZImage {
   void forward(const float* x_in, int64_t B, int64_t C, int64_t H, int64_t W, float t, const float* cap_in, int64_t L,
                int64_t capdim, float* out) {
     if (!finalized) fail(kErrInvalidArg, "zimage: finalize() not called");
+    timed(2, 0.0, [&] { forward_impl(x_in, B, C, H, W, t, cap_in, L, capdim, out); });
+  }
+
+  void forward_impl(const float* x_in, int64_t B, int64_t C, int64_t H, int64_t W, float t, const float* cap_in,
+                    int64_t L, int64_t capdim, float* out) {
     const int64_t p = patch;
     if (C != in_ch || H % p || W % p || B < 1) fail(kErrInvalidArg, "zimage: bad latent shape");
     const int64_t Ht = H / p, Wt = W / p, n_img = Ht * Wt, n_img_pad = pad_to(n_img);
@@ -461,6 +522,22 @@ int sdb200_zimage_forward(void* m, const float* x, int64_t B, int64_t C, int64_t
   SDB_GUARD({
     if (!m || !x || !cap || !out) sdb::fail(sdb::kErrInvalidArg, "zimage_forward: null pointer");
     static_cast<ZImage*>(m)->forward(x, B, C, H, W, t, cap, L, capdim, out);
+  })
+}
+
+int sdb200_zimage_profile(void* m, int enable) {
+  SDB_GUARD({
+    if (!m) sdb::fail(sdb::kErrInvalidArg, "zimage_profile: null model");
+    ZImage* z = static_cast<ZImage*>(m);
+    z->prof_clear();
+    z->prof_on = enable != 0;
+  })
+}
+
+int sdb200_zimage_profile_read(void* m, double* out8) {
+  SDB_GUARD({
+    if (!m || !out8) sdb::fail(sdb::kErrInvalidArg, "zimage_profile_read: null pointer");
+    static_cast<ZImage*>(m)->prof_read(out8);
   })
 }
 

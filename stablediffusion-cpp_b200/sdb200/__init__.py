@@ -45,6 +45,7 @@ _i = C.c_int
 # name -> (argtypes, restype)
 _SIGS = {
     "sdb200_version": ([], _i),
+    "sdb200_launch_count": ([], C.c_ulonglong),
     "sdb200_last_error": ([], C.c_char_p),
     "sdb200_available": ([], _i),
     "sdb200_device_count": ([], _i),
@@ -76,6 +77,8 @@ _SIGS = {
     "sdb200_zimage_finalize": ([_v], _i),
     "sdb200_zimage_forward": ([_v, _v, _i64, _i64, _i64, _i64, _f, _v, _i64, _i64, _v], _i),
     "sdb200_zimage_destroy": ([_v], None),
+    "sdb200_zimage_profile": ([_v, _i], _i),
+    "sdb200_zimage_profile_read": ([_v, C.POINTER(C.c_double)], _i),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
     "sdb200_group_norm": ([_v, _v, _i64, _i64, _i64, _i, _v, _v, _f], _i),
     "sdb200_layer_norm": ([_v, _v, _i64, _i64, _v, _v, _f], _i),

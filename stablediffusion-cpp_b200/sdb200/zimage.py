@@ -154,6 +154,17 @@ class ZImageB200:
                                           cap.shape[2], out.data_ptr()))
         return out
 
+    def profile(self, enable: bool = True):
+        """Times later forwards' GEMM and attention kernels with CUDA events."""
+        check(lib().sdb200_zimage_profile(self._m, int(enable)))
+
+    def profile_read(self) -> dict:
+        out = (C.c_double * 8)()
+        check(lib().sdb200_zimage_profile_read(self._m, out))
+        keys = ("gemm_ms", "gemm_flop", "gemm_launches", "attn_ms", "attn_flop", "attn_launches", "forward_ms",
+                "forwards")
+        return dict(zip(keys, list(out)))
+
     def __del__(self):
         try:
             if self._m:
