@@ -4,12 +4,14 @@
 // (backend_cuda.cu:550-586: two batched SGEMMs around a softmax, the full Sq x Skv
 // matrix in HBM) and the CPU path it is checked against (tensor.cpp:771-810).
 //
-// One CTA owns 128 query rows of one (sample, head); 192 threads in three roles:
-//   warp 0     TMA: Q once, then K/V tiles of 128 keys through a 2-stage ring
-//   warp 1     MMA: S_j = Q K_j^T into one of two TMEM score buffers (ping-pong, so
-//              the next tile's QK^T overlaps this tile's softmax), then
-//              O += P_j V_j into a TMEM accumulator
-//   warps 2-5  softmax: one query row per thread (TMEM lane). Loads S_j, applies the
+// One CTA owns 128 query rows of one (sample, head); 224 threads in four roles:
+//   warp 0     TMA: Q once, then K and V tiles of 128 keys through separate 2-stage
+//              rings (K is freed when QK^T is done, so it runs ahead of the PV chain)
+//   warp 1     QK^T issuer: S_j = Q K_j^T into one of two TMEM score buffers
+//              (ping-pong: the next tile's QK^T overlaps this tile's softmax)
+//   warp 2     PV issuer: O += P_j V_j into a TMEM accumulator as soon as P_j and V_j
+//              are ready; two issuer threads keep one role's wait from blocking the other
+//   warps 3-6  softmax: one query row per thread (TMEM lane). Loads S_j, applies the
 //              scale (in log2 units) and the masks, keeps the running max m and sum l,
 //              writes P_j = 2^(s - m) as fp16 into a swizzled shared-memory tile for
 //              the PV MMA, and at the end normalises O by 1/l and stores it.
@@ -33,7 +35,7 @@ namespace {
 
 constexpr int kBQ = 128;
 constexpr int kBK = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;  // TMA, QK^T issuer, PV issuer, 4 softmax warps
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct AttnParams {
@@ -53,10 +55,17 @@ struct ACfg {
   static constexpr int Q_BYTES = ATOMS * ATOM;
   static constexpr int KV_BYTES = ATOMS * ATOM;  // one K or one V tile
   static constexpr int P_BYTES = 2 * ATOM;       // 128 x 128 fp16
-  static constexpr int SMEM = Q_BYTES + 2 * 2 * KV_BYTES + 2 * P_BYTES + 1024 + 256;
+  static constexpr int SMEM = Q_BYTES + 2 * 2 * KV_BYTES + 2 * P_BYTES + 1024 + 256;  // Q | K[2] | V[2] | P[2]
   static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O
   static constexpr uint32_t O_COL = 256;
 };
+
+// 2^x on the MUFU pipe (PTX ex2.approx.ftz.f32; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -79,14 +88,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sP = sV + 2 * C_::KV_BYTES;     // [2 buffers]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C_::P_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* s_full = bars + 5;     // [2]
-  uint64_t* p_full = bars + 7;     // [2]
-  uint64_t* p_free = bars + 9;     // [2]
-  uint64_t* o_final = bars + 11;
-  uint64_t* drain = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* k_empty = bars + 3;    // [2]
+  uint64_t* v_full = bars + 5;     // [2]
+  uint64_t* v_empty = bars + 7;    // [2]
+  uint64_t* s_full = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;    // [2]
+  uint64_t* p_free = bars + 13;    // [2]
+  uint64_t* o_final = bars + 15;
+  uint64_t* drain = bars + 16;     // [2] one per MMA thread
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,14 +109,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
+      mbar_init(&drain[i], 1);
     }
     mbar_init(o_final, 1);
-    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -125,75 +138,100 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
+    // K_j and V_j have separate 2-stage rings: K_j is released as soon as S_j is
+    // computed, V_j only after PV_j, so K loads run ahead of the PV chain.
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, C_::Q_BYTES);
       for (int a = 0; a < C_::ATOMS; ++a)
         tma_load_3d(sQ + a * C_::ATOM, &tmQ, q_full, h * p.dp + a * 64, q0, n);
-      int issued_last = -1;
+      int k_issued = -1, v_issued = -1;
       bool ok = true;
       for (int j = 0; j < nkv && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, abort_flag, p.err, kErrAttnWait)) {
+        const uint32_t par = ((j >> 1) & 1) ^ 1u;
+        if (!mbar_wait(&k_empty[st], par, abort_flag, p.err, kErrAttnWait)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * C_::KV_BYTES);
-        for (int a = 0; a < C_::ATOMS; ++a) {
-          tma_load_3d(sK + st * C_::KV_BYTES + a * C_::ATOM, &tmK, &kv_full[st], kvh * p.dp + a * 64, j * kBK, n);
-          tma_load_3d(sV + st * C_::KV_BYTES + a * C_::ATOM, &tmV, &kv_full[st], kvh * p.dp + a * 64, j * kBK, n);
+        mbar_arrive_expect_tx(&k_full[st], C_::KV_BYTES);
+        for (int a = 0; a < C_::ATOMS; ++a)
+          tma_load_3d(sK + st * C_::KV_BYTES + a * C_::ATOM, &tmK, &k_full[st], kvh * p.dp + a * 64, j * kBK, n);
+        k_issued = j;
+        if (!mbar_wait(&v_empty[st], par, abort_flag, p.err, kErrAttnWait)) {
+          ok = false;
+          break;
         }
-        issued_last = j;
+        mbar_arrive_expect_tx(&v_full[st], C_::KV_BYTES);
+        for (int a = 0; a < C_::ATOMS; ++a)
+          tma_load_3d(sV + st * C_::KV_BYTES + a * C_::ATOM, &tmV, &v_full[st], kvh * p.dp + a * 64, j * kBK, n);
+        v_issued = j;
       }
       if (!ok) {
         // Aborted: wait (bounded) for the loads this CTA still has in flight.
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
-        for (int j = max(0, issued_last - 1); j <= issued_last; ++j)
-          while (!mbar_try_wait(&kv_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        for (int j = max(0, k_issued - 1); j <= k_issued; ++j)
+          while (!mbar_try_wait(&k_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
+        for (int j = max(0, v_issued - 1); j <= v_issued; ++j)
+          while (!mbar_try_wait(&v_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
           }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer --------------------------------
+    // ------------------------------ QK^T issuer -------------------------------
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrAttnWait);
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
-      for (int j = 0; ok && j <= nkv; ++j) {
-        if (j < nkv) {
-          const int st = j & 1;
-          if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * C_::KV_BYTES);
-          const uint32_t d_s = tmem + (uint32_t)(st * kBK);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        // S buffer j&1 is free once the softmax has consumed S_{j-2} (it posted P_{j-2}).
+        if (j >= 2 && !mbar_wait(&p_full[st], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * C_::KV_BYTES);
+        const uint32_t d_s = tmem + (uint32_t)(st * kBK);
 #pragma unroll
-          for (int ks = 0; ks < DP / 16; ++ks) {
-            const uint32_t off = (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32);
-            umma_f16_ss(d_s, sdesc_k_sw128(q_addr + off), sdesc_k_sw128(k_addr + off), IDESC_S, ks > 0);
-          }
-          umma_commit(&s_full[st]);
+        for (int ks = 0; ks < DP / 16; ++ks) {
+          const uint32_t off = (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32);
+          umma_f16_ss(d_s, sdesc_k_sw128(q_addr + off), sdesc_k_sw128(k_addr + off), IDESC_S, ks > 0);
         }
-        if (j >= 1) {
-          const int jj = j - 1, b = jj & 1;
-          if (!mbar_wait(&p_full[b], (jj >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + b * C_::P_BYTES);
-          const uint32_t v_addr = smem_u32(sV + b * C_::KV_BYTES);  // V of tile jj lives in stage jj & 1
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+      }
+      umma_commit(&drain[0]);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&drain[0], 0))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kErrWaitDrain);
+          break;
+        }
+    }
+  } else if (warp == 2) {
+    // ------------------------------ PV issuer ---------------------------------
+    if (lane == 0) {
+      for (int j = 0; j < nkv; ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        if (!mbar_wait(&v_full[b], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + b * C_::P_BYTES);
+        const uint32_t v_addr = smem_u32(sV + b * C_::KV_BYTES);
 #pragma unroll
-          for (int ks = 0; ks < kBK / 16; ++ks) {
-            const uint64_t ad = sdesc_k_sw128(p_addr + (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32));
-            const uint64_t bd = sdesc_mn_sw128(v_addr + (uint32_t)(ks * 16 * 128), C_::ATOM, 1024);
-            umma_f16_ss(tmem + C_::O_COL, ad, bd, IDESC_O, (jj > 0 || ks > 0) ? 1u : 0u);
-          }
-          umma_commit(&p_free[b]);
-          umma_commit(&kv_empty[b]);
+        for (int ks = 0; ks < kBK / 16; ++ks) {
+          const uint64_t ad = sdesc_k_sw128(p_addr + (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32));
+          const uint64_t bd = sdesc_mn_sw128(v_addr + (uint32_t)(ks * 16 * 128), C_::ATOM, 1024);
+          umma_f16_ss(tmem + C_::O_COL, ad, bd, IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
         }
+        umma_commit(&p_free[b]);
+        umma_commit(&v_empty[b]);
       }
       umma_commit(o_final);
-      umma_commit(drain);
+      umma_commit(&drain[1]);
       const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(drain, 0))
+      while (!mbar_try_wait(&drain[1], 0))
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           atomicOr(p.err, kErrWaitDrain);
           break;
@@ -214,32 +252,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[kBK];
-      {
-        uint32_t u[4][32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 0), u[0]);
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 32), u[1]);
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 64), u[2]);
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 96), u[3]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < kBK; ++c) s[c] = __uint_as_float(u[c >> 5][c & 31]);
-      }
+      // All 128 scores of this row in registers: four 32-column TMEM loads, one wait.
+      uint32_t u[4][32];
+      __syncwarp();
+      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 0), u[0]);
+      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 32), u[1]);
+      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 64), u[2]);
+      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 96), u[3]);
+      tmem_wait_ld();
       const int kbase = j * kBK;
       const bool full_tile = (kbase + kBK <= p.Skv) && (!p.causal || kbase + kBK - 1 <= q0);
-      float mx = -INFINITY;
+      if (!full_tile) {
 #pragma unroll
-      for (int c = 0; c < kBK; ++c) {
-        float v = s[c] * p.scale_log2;
-        if (!full_tile) {
+        for (int c = 0; c < kBK; ++c) {
           const int key = kbase + c;
-          if (key >= p.Skv || (p.causal && key > row)) v = -INFINITY;
+          if (key >= p.Skv || (p.causal && key > row)) u[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
-        s[c] = v;
-        mx = fmaxf(mx, v);
       }
-      const float m_new = fmaxf(m_used, mx);
+      // Row max of the raw scores, 4 partial maxima (short dependency chains); the
+      // scale is positive, so max(s) * scale = max(s * scale).
+      float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kBK; ++c) pm[c & 3] = fmaxf(pm[c & 3], __uint_as_float(u[c >> 5][c & 31]));
+      const float mx = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+      const float m_new = fmaxf(m_used, mx * p.scale_log2);
       const bool need = m_new > m_used + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
         if (j > 0) {
@@ -249,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const float f = need ? exp2f(m_used - m_new) : 1.0f;
+          const float f = need ? ex2_approx(m_used - m_new) : 1.0f;
 #pragma unroll 1
           for (int c = 0; c < DP; c += 32) {
             uint32_t o[32];
@@ -263,38 +299,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
         if (need) {
-          l *= exp2f(m_used - m_new);
+          l *= ex2_approx(m_used - m_new);
           m_used = m_new;
         }
       }
-      const float m_eff = (m_used == -INFINITY) ? 0.0f : m_used;
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kBK; ++c) {
-        const float e = exp2f(s[c] - m_eff);
-        s[c] = e;
-        rs += e;
-      }
-      l += rs;
+      // The P buffer of this tile must no longer be read by PV_{j-2}.
       if (j >= 2 && !mbar_wait(&p_free[b], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrAttnWait)) {
         ok = false;
         break;
       }
-      // P row r as fp16 into the 128B-swizzled K-major tile: keys [64a, 64a+64) form
+      // p = 2^(s * scale_log2 - m): one FFMA + one MUFU ex2 per score, 4 partial sums,
+      // written as fp16 into the 128B-swizzled K-major P tile: keys [64a, 64a+64) form
       // atom a; 16-byte chunk c of row r sits at chunk position c ^ (r & 7).
+      const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
+      float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       uint8_t* pb = sP + b * C_::P_BYTES + r * 128;
 #pragma unroll
       for (int a = 0; a < 2; ++a)
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float* v = s + a * 64 + c * 8;
+        for (int cc = 0; cc < 8; ++cc) {
+          float e[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int c = a * 64 + cc * 8 + i;
+            e[i] = ex2_approx(fmaf(__uint_as_float(u[c >> 5][c & 31]), p.scale_log2, neg_m));
+            ps[i & 3] += e[i];
+          }
           uint4 w;
-          w.x = pack_half2(v[0], v[1]);
-          w.y = pack_half2(v[2], v[3]);
-          w.z = pack_half2(v[4], v[5]);
-          w.w = pack_half2(v[6], v[7]);
-          *reinterpret_cast<uint4*>(pb + a * C_::ATOM + ((c ^ (r & 7)) << 4)) = w;
+          w.x = pack_half2(e[0], e[1]);
+          w.y = pack_half2(e[2], e[3]);
+          w.z = pack_half2(e[4], e[5]);
+          w.w = pack_half2(e[6], e[7]);
+          *reinterpret_cast<uint4*>(pb + a * C_::ATOM + ((cc ^ (r & 7)) << 4)) = w;
         }
+      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
