@@ -1,6 +1,6 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload dit|gemm]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload dit|gemm|attention]
 
 Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
 random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
@@ -12,6 +12,9 @@ ranks of CUDA-event time.
 
 Workload `gemm`: Y[4096,11520] = X[4096,3840] W[11520,3840]^T + b,
 one GEMM per GPU per step (replicas), TFLOP/s.
+
+Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
+128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
 
 Printed on rank 0 as one JSON line:
   value / ms_per_step  inputs resident in HBM
@@ -470,13 +473,76 @@ def run_gemm(args, world, rank, local, pg, dev):
         print(json.dumps(line), flush=True)
 
 
+def run_attention(args, world, rank, local, pg, dev):
+    """The Z-Image joint-sequence attention at 1024^2 (one image): 4224 tokens, 30 heads
+    of 128, non-causal. value = TFLOP/s of the tensor-core kernel on fp16 operands
+    resident in HBM (4*S^2*d*heads per launch); e2e = the drop-in fp32 API with host
+    buffers."""
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+
+    L = sdb200.lib()
+    S, H, d, dp = 4224, 30, 128, 128
+    FLOP = 4.0 * S * S * d * H
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    q = torch.randn((1, S, H * d), generator=g, device=dev)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    o = torch.empty_like(q)
+    q16, k16, v16 = (torch.empty(S * H * dp, dtype=torch.float16, device=dev) for _ in range(3))
+    for x, y in ((q, q16), (k, k16), (v, v16)):
+        sdb200.check(L.sdb200_pack_heads_f16(x.data_ptr(), y.data_ptr(), S, H, d, dp))
+    stream = torch.cuda.current_stream()
+    step = lambda: sdb200.check(L.sdb200_attention_f16(q16.data_ptr(), k16.data_ptr(), v16.data_ptr(),  # noqa: E731
+                                                       o.data_ptr(), 0, 1, S, S, H, H, d, dp, 0))
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    value = FLOP * args.steps * world / (ms * 1e-3) / 1e12
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty_like(qh).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+
+    def e2e_step():
+        for hsrc, ddst in ((qh, qd), (kh, kd), (vh, vd)):
+            sdb200.check(L.sdb200_upload(ddst.data_ptr(), hsrc.data_ptr(), hsrc.numel() * 4))
+        sdb200.check(L.sdb200_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), 1, S, S, H, H, d, 0))
+        sdb200.check(L.sdb200_download(oh.data_ptr(), o.data_ptr(), oh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
+    pk = peaks()
+    if rank == 0:
+        achieved = FLOP / (ms / args.steps * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "attention TFLOP/s (Z-Image joint attention @1024^2)", "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16 operands, fp32 accumulate and softmax", "data": "synthetic N(0,1) q/k/v",
+            "config": {"workload": "attention S=4224 heads=30 d=128 non-causal, fp16 packed operands",
+                       "parallelism": f"replicas x{world}"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "k_attention_tc<128>", "achieved": achieved,
+                         "peak": pk["burst"], "unit": "TFLOP/s", "frac": achieved / pk["burst"],
+                         "peak_kind": f"{pk['kind']} bf16 burst (dense fp16 = bf16 rate)", "traffic": None},
+            "e2e": {"value": FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(3 * qh.numel() * 4), "d2h_bytes_per_step": int(oh.numel() * 4)},
+            "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "gemm"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "gemm", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -502,6 +568,8 @@ def main():
     be.bind_stream()
     if args.workload == "dit":
         run_dit(args, world, rank, local, pg, dev)
+    elif args.workload == "attention":
+        run_attention(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:
