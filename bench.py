@@ -1,6 +1,7 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload dit|gemm|attention]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload dit|dit_tp|gemm|attention]
 
 Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
 random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
@@ -12,6 +13,10 @@ ranks of CUDA-event time.
 
 Workload `gemm`: Y[4096,11520] = X[4096,3840] W[11520,3840]^T + b,
 one GEMM per GPU per step (replicas), TFLOP/s.
+
+Workload `dit_tp`: the same DiT at batch 1, 2048x2048 (16512 tokens),
+Megatron tensor parallelism over the N ranks with an NCCL all-reduce after each
+row-parallel projection; ms per step.
 
 Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
 128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
@@ -396,6 +401,87 @@ def run_dit(args, world, rank, local, pg, dev):
         print(json.dumps(line), flush=True)
 
 
+def run_dit_tp(args, world, rank, local, pg, dev):
+    """the 30-layer DiT at batch 1, 2048x2048 (256x256 latent: 16384
+    image + 128 text tokens), Megatron tensor parallelism over the N ranks (column-parallel
+    QKV by heads and w1/w3, row-parallel to_out and w2, NCCL all-reduce after each
+    row-parallel projection). Total work fixed: "scaling": "strong"."""
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+    from sdb200.tp import Comm, shard_weights
+    from sdb200.zimage import Z_IMAGE, ZImageB200, random_weights_torch
+
+    L = sdb200.lib()
+    cfg = Z_IMAGE
+    H = W = 256
+    full = random_weights_torch(cfg, 0, dev)
+    shards = shard_weights(full, cfg.heads, cfg.dim // cfg.heads, rank, world)
+    del full
+    torch.cuda.empty_cache()
+    model = ZImageB200(shards, cfg)
+    comm = Comm(rank, world, None)
+    model.set_tp(comm)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000)  # every rank holds the same image and text states
+    x = torch.randn((1, cfg.in_channels, H, W), generator=g, device=dev)
+    cap = torch.randn((1, TEXT_TOKENS, cfg.cap_dim), generator=g, device=dev)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    step = lambda: model.forward(x, 0.5, cap, out)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    ms_step = ms / args.steps
+    model.profile(True)
+    step()
+    prof = model.profile_read()
+    model.profile(False)
+    fl = dit_forward_flops(cfg, H, W)
+    pk = peaks()
+    gemm_tf = prof["gemm_flop"] / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] else None
+    attn_tf = prof["attn_flop"] / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] else None
+    xh, caph = x.cpu().pin_memory(), cap.cpu().pin_memory()
+    outh = torch.empty_like(out, device="cpu").pin_memory()
+    xd, capd = torch.empty_like(x), torch.empty_like(cap)
+
+    def e2e_step():
+        sdb200.check(L.sdb200_upload(xd.data_ptr(), xh.data_ptr(), xh.numel() * 4))
+        sdb200.check(L.sdb200_upload(capd.data_ptr(), caph.data_ptr(), caph.numel() * 4))
+        model.forward(xd, 0.5, capd, out)
+        sdb200.check(L.sdb200_download(outh.data_ptr(), out.data_ptr(), outh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev) / args.steps
+    err = be.device_error_word()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 GEMM operands, fp16 attention operands, fp32 accumulate/activations",
+            "data": "synthetic (random-init Z-Image-shaped weights, N(0,1) latent and text states)",
+            "config": {"workload": "cfg5: 30-layer Z-Image DiT @2048^2 (16512 tokens), batch 1, one denoising step",
+                       "global_batch": 1, "seq_len": 16512, "parallelism": f"tensor-parallel x{world} "
+                       "(column QKV/w1/w3, row to_out/w2, NCCL all-reduce fp32)"},
+            "step_tflops": fl["total"] / (ms_step * 1e-3) / 1e12,
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all GEMMs of one step, rank 0)", "achieved": gemm_tf,
+                         "peak": pk["sustained"], "unit": "TFLOP/s",
+                         "frac": (gemm_tf / pk["sustained"]) if gemm_tf else None,
+                         "peak_kind": f"{pk['kind']} bf16 sustained", "traffic": None,
+                         "gemm_ms_per_step": prof["gemm_ms"], "attention_tflops": attn_tf,
+                         "attention_ms_per_step": prof["attn_ms"], "allreduce_ms_per_step": prof["allreduce_ms"],
+                         "allreduces_per_step": prof["allreduces"], "forward_ms_profiled": prof["forward_ms"]},
+            "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
+                    "d2h_bytes_per_step": int(outh.numel() * 4)},
+            "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": err}), flush=True)
+    comm.close()
+
+
 def run_gemm(args, world, rank, local, pg, dev):
     import torch
 
@@ -542,7 +628,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "gemm", "attention"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -570,6 +656,8 @@ def main():
         run_dit(args, world, rank, local, pg, dev)
     elif args.workload == "attention":
         run_attention(args, world, rank, local, pg, dev)
+    elif args.workload == "dit_tp":
+        run_dit_tp(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:

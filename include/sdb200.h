@@ -166,10 +166,26 @@ int sdb200_zimage_forward(void* model, const float* x, int64_t B, int64_t C, int
                           const float* cap, int64_t L, int64_t capdim, float* out);
 void sdb200_zimage_destroy(void* model);
 /* Per-kernel timing of later forwards with CUDA events on the stream (enable != 0).
- * profile_read fills out8 = {GEMM ms, GEMM FLOP, GEMM launches, attention ms, attention
- * FLOP, attention launches, forward ms, forwards} since the last read, synchronising. */
+ * profile_read fills out10 = {GEMM ms, GEMM FLOP, GEMM launches, attention ms, attention
+ * FLOP, attention launches, forward ms, forwards, all-reduce ms, all-reduces} since the
+ * last read, synchronising. */
 int sdb200_zimage_profile(void* model, int enable);
-int sdb200_zimage_profile_read(void* model, double* out8);
+int sdb200_zimage_profile_read(void* model, double* out10);
+/* Extension (the reference has no multi-GPU mode): Megatron-style tensor parallelism.
+ * The caller registers this rank's shards (to_q/to_k/to_v rows and to_out columns of its
+ * heads, w1/w3 rows and w2 columns of its FFN slice, row-parallel biases on rank 0 only)
+ * and attaches a communicator; the outputs of to_out and w2 are then summed over the
+ * group (NCCL all-reduce on the model's stream) before each post-norm. */
+int sdb200_zimage_set_tp(void* model, void* comm);
+
+/* ---- tensor-parallel communicator (NCCL over NVLink / NVSwitch, loaded at run time) -- */
+/* Writes a 128-byte unique id (on one rank; share it with the others out of band). */
+int sdb200_comm_unique_id(void* out128);
+/* Joins the group as `rank` of `world` on the current device; NULL on failure. */
+void* sdb200_comm_create(const void* unique_id128, int rank, int world);
+/* In-place sum all-reduce of n fp32 values on the current device's stream. */
+int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n);
+void sdb200_comm_destroy(void* comm);
 
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
 /* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */

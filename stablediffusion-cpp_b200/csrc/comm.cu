@@ -1,0 +1,141 @@
+// comm.cu - the tensor-parallel collective of the DiT: a sum all-reduce over NVLink /
+// NVSwitch through NCCL, one communicator per tensor-parallel group, one process (or
+// thread) per GPU. The reference has no collective at all (single device,
+// backend_cuda.cu:64-72); this is the exchange step of Megatron-style row-parallel
+// projections (to_out and w2 of each block).
+//
+// NCCL is loaded at run time (dlopen "libnccl.so.2"): the library itself keeps no
+// link-time dependency on it, and in a process where PyTorch already loaded its NCCL
+// the same copy is reused. Only the NCCL C API is called (no torch types cross here).
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+#include "sdb200.h"
+
+namespace sdb {
+namespace {
+
+struct NcclApi {
+  bool loaded = false;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mutex;
+
+NcclApi& nccl() {
+  std::lock_guard<std::mutex> lk(g_nccl_mutex);
+  if (g_nccl.loaded) return g_nccl;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) fail(kErrUnsupported, std::string("NCCL not available: ") + dlerror());
+  auto sym = [&](const char* n) {
+    void* f = dlsym(h, n);
+    if (!f) fail(kErrUnsupported, std::string("NCCL symbol missing: ") + n);
+    return f;
+  };
+  g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(sym("ncclGetUniqueId"));
+  g_nccl.CommInitRank = reinterpret_cast<decltype(g_nccl.CommInitRank)>(sym("ncclCommInitRank"));
+  g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(sym("ncclAllReduce"));
+  g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
+  g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(sym("ncclCommAbort"));
+  g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
+  g_nccl.loaded = true;
+  return g_nccl;
+}
+
+void check_nccl(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) fail(kErrCuda, std::string(what) + ": " + nccl().GetErrorString(r));
+}
+
+}  // namespace
+
+struct Comm {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1, device = -1;
+};
+
+// Sum all-reduce of n fp32 values in place on the calling context's stream.
+void comm_allreduce_sum(Comm* c, float* buf, size_t n) {
+  if (!c || c->world <= 1 || n == 0) return;
+  check_nccl(nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, c->comm, ctx().stream), "ncclAllReduce");
+}
+int comm_world(const Comm* c) { return c ? c->world : 1; }
+int comm_rank(const Comm* c) { return c ? c->rank : 0; }
+
+}  // namespace sdb
+
+using sdb::Comm;
+
+extern "C" {
+
+int sdb200_comm_unique_id(void* out) {
+  try {
+    if (!out) sdb::fail(sdb::kErrInvalidArg, "comm_unique_id: null output");
+    ncclUniqueId id;
+    sdb::check_nccl(sdb::nccl().GetUniqueId(&id), "ncclGetUniqueId");
+    std::memcpy(out, &id, sizeof(id));
+    return sdb::kOk;
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return e.code;
+  }
+}
+
+void* sdb200_comm_create(const void* unique_id, int rank, int world) {
+  try {
+    if (!unique_id || world < 1 || rank < 0 || rank >= world) sdb::fail(sdb::kErrInvalidArg, "comm_create: bad args");
+    Comm* c = new Comm();
+    c->rank = rank;
+    c->world = world;
+    c->device = sdb::ctx().device;
+    if (world > 1) {
+      ncclUniqueId id;
+      std::memcpy(&id, unique_id, sizeof(id));
+      try {
+        sdb::check_nccl(sdb::nccl().CommInitRank(&c->comm, world, id, rank), "ncclCommInitRank");
+      } catch (...) {
+        delete c;
+        throw;
+      }
+    }
+    return c;
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return nullptr;
+  }
+}
+
+int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n) {
+  try {
+    if (!comm || (!buf && n)) sdb::fail(sdb::kErrInvalidArg, "comm_allreduce: null pointer");
+    sdb::comm_allreduce_sum(static_cast<Comm*>(comm), buf, n);
+    return sdb::kOk;
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return e.code;
+  }
+}
+
+void sdb200_comm_destroy(void* comm) {
+  Comm* c = static_cast<Comm*>(comm);
+  if (!c) return;
+  if (c->comm) {
+    try {
+      sdb::nccl().CommDestroy(c->comm);
+    } catch (...) {
+    }
+  }
+  delete c;
+}
+
+}  // extern "C"

@@ -23,6 +23,7 @@
 // (zimage.cpp:38-67). Block linears must be bf16 (the loader keeps tensors of >= 2^20
 // elements in bf16, safetensors.cpp:119); small layers (x_embed, t_mlp, final) may be
 // fp32 or bf16. finalize() builds the fused QKV and interleaved w1/w3 weights it owns.
+#include <algorithm>
 #include <array>
 #include <cmath>
 #include <cstring>
@@ -36,6 +37,11 @@
 #include "sdb200.h"
 
 namespace sdb {
+
+struct Comm;
+void comm_allreduce_sum(Comm* c, float* buf, size_t n);
+int comm_world(const Comm* c);
+
 namespace {
 
 struct WRef {
@@ -100,7 +106,9 @@ struct Block {
   const float* b2 = nullptr;
   const uint16_t* adaln = nullptr;  // [4D, tdim] or null (context refiner)
   const float* adaln_b = nullptr;
-  int64_t F = 0;
+  int64_t F = 0;       // FFN width held by this rank (all of it without tensor parallelism)
+  int64_t Dq = 0;      // q/k/v width held by this rank = heads_local * 128
+  int heads_local = 0;
 };
 
 // Generic linear on fp32 activations: bf16 or fp32 weights (tensor.cpp:481-501).
@@ -131,8 +139,8 @@ class ZImage {
   ~ZImage() { prof_clear(); }
 
   // ---- optional per-kernel timing (CUDA events on the stream) ------------------------
-  // Category 0: tensor-core GEMMs, 1: attention, 2: whole forward. FLOPs are the
-  // algorithmic 2*M*N*K (GEMM) and 4*Sq*Skv*d*heads (attention).
+  // Category 0: tensor-core GEMMs, 1: attention, 2: whole forward, 3: tensor-parallel
+  // all-reduce. FLOPs are the algorithmic 2*M*N*K (GEMM) and 4*Sq*Skv*d*heads (attention).
   bool prof_on = false;
   struct Mark {
     cudaEvent_t a, b;
@@ -158,14 +166,20 @@ class ZImage {
     }
     marks.clear();
   }
-  // out[0..8]: gemm ms, gemm flop, gemm launches, attention ms, attention flop,
-  // attention launches, forward ms, forwards. Synchronises; resets the record.
+  // out[0..10]: gemm ms, gemm flop, gemm launches, attention ms, attention flop,
+  // attention launches, forward ms, forwards, all-reduce ms, all-reduces.
+  // Synchronises; resets the record.
   void prof_read(double* out) {
-    for (int i = 0; i < 8; ++i) out[i] = 0.0;
+    for (int i = 0; i < 10; ++i) out[i] = 0.0;
     check_cuda(cudaStreamSynchronize(ctx().stream), "profile sync");
     for (Mark& m : marks) {
       float ms = 0.0f;
       check_cuda(cudaEventElapsedTime(&ms, m.a, m.b), "cudaEventElapsedTime");
+      if (m.cat == 3) {
+        out[8] += ms;
+        out[9] += 1.0;
+        continue;
+      }
       const int base = m.cat == 0 ? 0 : m.cat == 1 ? 3 : 6;
       out[base] += ms;
       if (m.cat < 2) {
@@ -209,7 +223,13 @@ class ZImage {
     const uint16_t* wq = bf16w(p + ".attention.to_q.weight");
     const uint16_t* wk = bf16w(p + ".attention.to_k.weight");
     const uint16_t* wv = bf16w(p + ".attention.to_v.weight");
-    const size_t mat = (size_t)(D * D) * 2;
+    // With tensor parallelism the caller registers this rank's column shards: the rows
+    // of to_q / to_k / to_v for its heads, the matching columns of to_out.
+    b.Dq = get(p + ".attention.to_q.weight").dim(0);
+    if (b.Dq % head_dim || get(p + ".attention.to_q.weight").dim(1) != D) fail(kErrInvalidArg, "zimage: to_q shape");
+    b.heads_local = (int)(b.Dq / head_dim);
+    if (get(p + ".attention.to_out.0.weight").dim(1) != b.Dq) fail(kErrInvalidArg, "zimage: to_out shard mismatch");
+    const size_t mat = (size_t)(b.Dq * D) * 2;
     b.wqkv.ensure(3 * mat);
     cudaStream_t s = ctx().stream;
     check_cuda(cudaMemcpyAsync(b.wqkv.as<uint8_t>(), wq, mat, cudaMemcpyDeviceToDevice, s), "zimage wqkv");
@@ -220,12 +240,13 @@ class ZImage {
     const WRef* bv = try_get(p + ".attention.to_v.bias");
     if (bq || bk || bv) {
       b.has_bqkv = true;
-      b.bqkv.ensure((size_t)(3 * D) * 4);
-      check_cuda(cudaMemsetAsync(b.bqkv.p, 0, (size_t)(3 * D) * 4, s), "zimage bqkv");
+      b.bqkv.ensure((size_t)(3 * b.Dq) * 4);
+      check_cuda(cudaMemsetAsync(b.bqkv.p, 0, (size_t)(3 * b.Dq) * 4, s), "zimage bqkv");
       const WRef* bb[3] = {bq, bk, bv};
       for (int i = 0; i < 3; ++i)
         if (bb[i])
-          check_cuda(cudaMemcpyAsync(b.bqkv.as<float>() + i * D, bb[i]->p, (size_t)D * 4, cudaMemcpyDeviceToDevice, s),
+          check_cuda(cudaMemcpyAsync(b.bqkv.as<float>() + i * b.Dq, bb[i]->p, (size_t)b.Dq * 4,
+                                     cudaMemcpyDeviceToDevice, s),
                      "zimage bqkv");
     }
     b.wout = bf16w(p + ".attention.to_out.0.weight");
@@ -330,7 +351,12 @@ class ZImage {
     return raw;
   }
 
-  // One block on x [B*S, D] (B sequences of S rows), rotary tables [S, 128].
+  // Tensor-parallel group (null or world 1: the whole model on this GPU).
+  Comm* comm = nullptr;
+
+  // One block on x [B*S, D] (B sequences of S rows), rotary tables [S, 128]. Under tensor
+  // parallelism this rank holds heads_local heads and F of the FFN; the row-parallel
+  // outputs of to_out and w2 are summed over the group before the post-norm.
   void run_block(const Block& b, float* x, int64_t B, int64_t S, const float* cs, const float* sn, bool modulated) {
     const int64_t R = B * S;
     const float *scale_msa = nullptr, *gate_msa = nullptr, *scale_mlp = nullptr, *gate_mlp = nullptr;
@@ -345,27 +371,31 @@ class ZImage {
     }
     // attention
     dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.attn_norm1, scale_msa, norm_eps);
-    const double gf = 2.0 * (double)R * (double)D;  // 2*M*K, times N per GEMM below
-    timed(0, gf * 3 * D, [&] {
-      gemm_bf16_epilogue_impl(R, 3 * D, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * D, false,
+    const int64_t Dq = b.Dq;
+    const int Hl = b.heads_local;
+    const double gf = 2.0 * (double)R;  // 2*M, times N*K per GEMM below
+    timed(0, gf * 3 * Dq * D, [&] {
+      gemm_bf16_epilogue_impl(R, 3 * Dq, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * Dq, false,
                               b.has_bqkv ? b.bqkv.as<float>() : nullptr, 0);
     });
     for (int64_t n = 0; n < B; ++n)
-      dit_qk_norm_rope_pack(qkv.as<float>() + n * S * 3 * D, (int)S, heads, b.norm_q, b.norm_k, cs, sn, 1e-5f,
-                            q16.as<uint8_t>() + n * S * D * 2, k16.as<uint8_t>() + n * S * D * 2,
-                            v16.as<uint8_t>() + n * S * D * 2);
-    timed(1, 4.0 * (double)B * S * S * D, [&] {
-      launch_attention_f16(q16.p, k16.p, v16.p, ao.p, D, S * D, true, B, S, S, heads, heads, head_dim, 128, false);
+      dit_qk_norm_rope_pack(qkv.as<float>() + n * S * 3 * Dq, (int)S, Hl, b.norm_q, b.norm_k, cs, sn, 1e-5f,
+                            q16.as<uint8_t>() + n * S * Dq * 2, k16.as<uint8_t>() + n * S * Dq * 2,
+                            v16.as<uint8_t>() + n * S * Dq * 2);
+    timed(1, 4.0 * (double)B * S * S * Dq, [&] {
+      launch_attention_f16(q16.p, k16.p, v16.p, ao.p, Dq, S * Dq, true, B, S, S, Hl, Hl, head_dim, 128, false);
     });
-    timed(0, gf * D, [&] { gemm_bf16_epilogue_impl(R, D, D, ao.p, D, true, b.wout, D, a.p, D, false, b.bout, 0); });
+    timed(0, gf * D * Dq, [&] { gemm_bf16_epilogue_impl(R, D, Dq, ao.p, Dq, true, b.wout, Dq, a.p, D, false, b.bout, 0); });
+    if (comm_world(comm) > 1) timed(3, 0.0, [&] { comm_allreduce_sum(comm, a.as<float>(), (size_t)(R * D)); });
     dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.attn_norm2, gate_msa, norm_eps);
     // feed-forward
     dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.ffn_norm1, scale_mlp, norm_eps);
-    timed(0, gf * 2 * b.F, [&] {
+    timed(0, gf * 2 * b.F * D, [&] {
       gemm_bf16_epilogue_impl(R, 2 * b.F, D, h.p, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
                               b.has_b13 ? b.b13.as<float>() : nullptr, 1);
     });
-    timed(0, gf * b.F, [&] { gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0); });
+    timed(0, gf * b.F * D, [&] { gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0); });
+    if (comm_world(comm) > 1) timed(3, 0.0, [&] { comm_allreduce_sum(comm, a.as<float>(), (size_t)(R * D)); });
     dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.ffn_norm2, gate_mlp, norm_eps);
   }
 
@@ -384,7 +414,12 @@ class ZImage {
     if (C != in_ch || H % p || W % p || B < 1) fail(kErrInvalidArg, "zimage: bad latent shape");
     const int64_t Ht = H / p, Wt = W / p, n_img = Ht * Wt, n_img_pad = pad_to(n_img);
     const int64_t n_cap_pad = pad_to(L), S = n_img_pad + n_cap_pad;
-    const int64_t F = layers[0].F;
+    int64_t F = 0, Dq = 0;
+    for (const std::vector<Block>* v : {&noise, &context, &layers})
+      for (const Block& b : *v) {
+        F = std::max(F, b.F);
+        Dq = std::max(Dq, b.Dq);
+      }
     cudaStream_t st = ctx().stream;
     DBuf* tb = get_tables(Ht, Wt, n_img_pad, n_cap_pad);
     // activations
@@ -394,11 +429,11 @@ class ZImage {
     cap.ensure((size_t)(B * n_cap_pad * D) * 4);
     uni.ensure((size_t)(Rmax * D) * 4);
     h.ensure((size_t)(Rmax * D) * 2);
-    qkv.ensure((size_t)(Rmax * 3 * D) * 4);
-    q16.ensure((size_t)(Rmax * D) * 2);
-    k16.ensure((size_t)(Rmax * D) * 2);
-    v16.ensure((size_t)(Rmax * D) * 2);
-    ao.ensure((size_t)(Rmax * D) * 2);
+    qkv.ensure((size_t)(Rmax * 3 * Dq) * 4);
+    q16.ensure((size_t)(Rmax * Dq) * 2);
+    k16.ensure((size_t)(Rmax * Dq) * 2);
+    v16.ensure((size_t)(Rmax * Dq) * 2);
+    ao.ensure((size_t)(Rmax * Dq) * 2);
     a.ensure((size_t)(Rmax * D) * 4);
     g.ensure((size_t)(Rmax * F) * 2);
     mod.ensure((size_t)(4 * D) * 4);
@@ -534,10 +569,17 @@ int sdb200_zimage_profile(void* m, int enable) {
   })
 }
 
-int sdb200_zimage_profile_read(void* m, double* out8) {
+int sdb200_zimage_profile_read(void* m, double* out10) {
   SDB_GUARD({
-    if (!m || !out8) sdb::fail(sdb::kErrInvalidArg, "zimage_profile_read: null pointer");
-    static_cast<ZImage*>(m)->prof_read(out8);
+    if (!m || !out10) sdb::fail(sdb::kErrInvalidArg, "zimage_profile_read: null pointer");
+    static_cast<ZImage*>(m)->prof_read(out10);
+  })
+}
+
+int sdb200_zimage_set_tp(void* m, void* comm) {
+  SDB_GUARD({
+    if (!m) sdb::fail(sdb::kErrInvalidArg, "zimage_set_tp: null model");
+    static_cast<ZImage*>(m)->comm = static_cast<sdb::Comm*>(comm);
   })
 }
 

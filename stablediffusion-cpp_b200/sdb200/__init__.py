@@ -79,6 +79,11 @@ _SIGS = {
     "sdb200_zimage_destroy": ([_v], None),
     "sdb200_zimage_profile": ([_v, _i], _i),
     "sdb200_zimage_profile_read": ([_v, C.POINTER(C.c_double)], _i),
+    "sdb200_zimage_set_tp": ([_v, _v], _i),
+    "sdb200_comm_unique_id": ([_v], _i),
+    "sdb200_comm_create": ([_v, _i, _i], _v),
+    "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
+    "sdb200_comm_destroy": ([_v], None),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
     "sdb200_group_norm": ([_v, _v, _i64, _i64, _i64, _i, _v, _v, _f], _i),
     "sdb200_layer_norm": ([_v, _v, _i64, _i64, _v, _v, _f], _i),

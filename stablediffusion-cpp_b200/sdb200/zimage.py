@@ -159,11 +159,17 @@ class ZImageB200:
         check(lib().sdb200_zimage_profile(self._m, int(enable)))
 
     def profile_read(self) -> dict:
-        out = (C.c_double * 8)()
+        out = (C.c_double * 10)()
         check(lib().sdb200_zimage_profile_read(self._m, out))
         keys = ("gemm_ms", "gemm_flop", "gemm_launches", "attn_ms", "attn_flop", "attn_launches", "forward_ms",
-                "forwards")
+                "forwards", "allreduce_ms", "allreduces")
         return dict(zip(keys, list(out)))
+
+    def set_tp(self, comm):
+        """Attaches a tensor-parallel communicator (sdb200.tp.Comm); the registered weights
+        must be this rank's shards (sdb200.tp.shard_weights)."""
+        self._comm = comm
+        check(lib().sdb200_zimage_set_tp(self._m, comm.handle if comm is not None else None))
 
     def __del__(self):
         try:

@@ -1,0 +1,60 @@
+"""Worker run under torchrun by tests/test_tp_gpu.py: the Z-Image forward with tensor
+parallelism over the launched GPUs (heads 3 and FFN 528 split unevenly over 2 ranks)
+against the single-GPU forward and the CPU oracle. Rank 0 prints one JSON line."""
+import datetime
+import json
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path[:0] = [os.path.join(ROOT, "stablediffusion-cpp_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    import sdb200
+    from sdb200.tp import Comm, shard_weights
+    from sdb200.zimage import ZConfig, ZImageB200, random_weights_numpy
+
+    cfg = ZConfig(dim=384, heads=3, ffn=528, t_dim=256, t_hidden=256, cap_dim=128, layers=2, noise_refiners=1,
+                  context_refiners=1)
+    w, bf = random_weights_numpy(cfg, 0)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1, 16, 16, 24)).astype(np.float32)
+    cap = rng.standard_normal((1, 20, 128)).astype(np.float32)
+    xt, capt = torch.from_numpy(x).to(dev), torch.from_numpy(cap).to(dev)
+    comm = Comm(rank, world)
+    m = ZImageB200(shard_weights(w, cfg.heads, 128, rank, world), cfg, bf16_names=bf)
+    m.set_tp(comm)
+    y = m.forward(xt, 0.6, capt)
+    torch.cuda.synchronize()
+    y0 = y.clone()
+    dist.broadcast(y0, src=0)
+    same = float((y - y0).abs().max().item())
+    t = torch.tensor([same], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        from oracle import Oracle
+        from zimage_oracle import ZImageOracle
+
+        single = ZImageB200(w, cfg, bf16_names=bf).forward(xt, 0.6, capt).cpu().numpy()
+        want = ZImageOracle(Oracle(), w, bf, heads=cfg.heads).forward(x, 0.6, cap)
+        got = y.cpu().numpy()
+        rel = lambda a, b: float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))  # noqa: E731
+        print(json.dumps({"world": world, "rel_vs_single_gpu": rel(got, single), "rel_vs_oracle": rel(got, want),
+                          "max_rank_diff": float(t.item()), "finite": bool(np.isfinite(got).all()),
+                          "err_word": sdb200.backend.device_error_word()}), flush=True)
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
