@@ -4,19 +4,25 @@
 // (backend_cuda.cu:550-586: two batched SGEMMs around a softmax, the full Sq x Skv
 // matrix in HBM) and the CPU path it is checked against (tensor.cpp:771-810).
 //
-// One CTA owns 128 query rows of one (sample, head); 224 threads in four roles:
-//   warp 0     TMA: Q once, then K and V tiles of 128 keys through separate 2-stage
-//              rings (K is freed when QK^T is done, so it runs ahead of the PV chain)
-//   warp 1     QK^T issuer: S_j = Q K_j^T into one of two TMEM score buffers
-//              (ping-pong: the next tile's QK^T overlaps this tile's softmax)
-//   warp 2     PV issuer: O += P_j V_j into a TMEM accumulator as soon as P_j and V_j
-//              are ready; two issuer threads keep one role's wait from blocking the other
-//   warps 3-6  softmax: one query row per thread (TMEM lane). Loads S_j, applies the
-//              scale (in log2 units) and the masks, keeps the running max m and sum l,
-//              writes P_j = 2^(s - m) as fp16 into a swizzled shared-memory tile for
-//              the PV MMA, and at the end normalises O by 1/l and stores it.
-// O is rescaled only when a row's max grows by more than 2^8 since the value used so
-// far (P stays <= 256, fine for fp16 and fp32); the stale max cancels in O / l.
+// One CTA owns two 128-row query tiles (A and B) of one (sample, head), 384 threads:
+//   warp 0      TMA: Q_A and Q_B once, then K_0, V_0, K_1, V_1, ... (128 keys each) in
+//               order through one 5-slot ring; a slot is free again once the MMAs of
+//               both tiles that read it are done
+//   warps 1, 2  MMA issuers of tiles A and B. Step j, once the tile's softmax has posted
+//               P_t(j-1): O_t += P_t(j-1) V_(j-1), then S_t = Q_t K_j^T. P_t lives in TMEM
+//               over the first 64 columns of S_t (fp16 pairs) and is the A operand of
+//               the PV MMA; one thread's MMAs execute in issue order, so the PV has read
+//               P before the next QK^T overwrites S_t, and when the softmax sees S_t(j)
+//               the PV of step j-1 is complete too
+//   warp 3      idle
+//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: one query row per thread
+//               (TMEM lane). Loads S, applies the scale (in log2 units) and the masks,
+//               keeps the running max m and sum l, writes P = 2^(s - m) as fp16 back into
+//               TMEM, and at the end normalises O by 1/l and stores it.
+// The two softmax warpgroups take turns at the exp pass, so that while one works the
+// tensor core runs the other tile's MMAs. O is rescaled only when a row's max grows by
+// more than 2^8 since the value used so far (P stays <= 256, fine for fp16 and fp32);
+// the stale max cancels in O / l. TMEM: S_A | S_B | O_A | O_B = 512 columns.
 //
 // Operands are fp16 (10-bit mantissa, as tf32), not bf16: with bf16 Q/K/V/P the result
 // misses the 2e-3 relative-Frobenius parity gate (about 3e-3 at d = 128); with fp16 it
@@ -33,9 +39,17 @@
 namespace sdb {
 namespace {
 
-constexpr int kBQ = 128;
-constexpr int kBK = 128;
-constexpr int kThreads = 224;  // TMA, QK^T issuer, PV issuer, 4 softmax warps
+constexpr int kBQ = 128;      // rows per query tile (TMEM lanes)
+constexpr int kBK = 128;      // keys per K / V tile
+constexpr int kTiles = 2;     // query tiles per CTA (ping-pong)
+constexpr int kThreads = 384; // control warpgroup (TMA, 2 MMA issuers, idle) + 2 softmax warpgroups
+// Register split by setmaxnreg: launched at kRegsLaunch per thread (384 x 168 = 64512),
+// the control warpgroup gives registers back and the softmax warpgroups take them, so
+// each softmax thread can hold a whole 128-column row of S. The shares add up to the
+// launch total exactly (128 x 56 + 256 x 224 = 64512); the launcher checks the compiled
+// register count so the increase can always be satisfied.
+constexpr int kRegsLaunch = 168, kRegsControl = 56, kRegsSoftmax = 224;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct AttnParams {
@@ -52,11 +66,12 @@ template <int DP>
 struct ACfg {
   static constexpr int ATOM = kBQ * 128;  // one 128-byte-wide swizzle atom of 128 rows
   static constexpr int ATOMS = DP / 64;
-  static constexpr int Q_BYTES = ATOMS * ATOM;
+  static constexpr int Q_BYTES = ATOMS * ATOM;   // one query tile
   static constexpr int KV_BYTES = ATOMS * ATOM;  // one K or one V tile
-  static constexpr int P_BYTES = 2 * ATOM;       // 128 x 128 fp16
-  static constexpr int SMEM = Q_BYTES + 2 * 2 * KV_BYTES + 2 * P_BYTES + 1024 + 256;  // Q | K[2] | V[2] | P[2]
-  static constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O
+  static constexpr int SLOTS = 5;                // K / V ring
+  // Q[2] | ring[5] | barriers
+  static constexpr int SMEM = kTiles * Q_BYTES + SLOTS * KV_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 512;     // S_A | S_B | O_A | O_B
   static constexpr uint32_t O_COL = 256;
 };
 
@@ -65,6 +80,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input max (sm_100 max.f32 with two sources and a third operand).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -82,43 +104,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + C_::Q_BYTES;          // [2 stages]
-  uint8_t* sV = sK + 2 * C_::KV_BYTES;     // [2 stages]
-  uint8_t* sP = sV + 2 * C_::KV_BYTES;     // [2 buffers]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C_::P_BYTES);
+  uint8_t* sQ = smem;                            // [2 tiles]
+  uint8_t* sR = sQ + kTiles * C_::Q_BYTES;       // ring [5 slots]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + C_::SLOTS * C_::KV_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;     // [2]
-  uint64_t* k_empty = bars + 3;    // [2]
-  uint64_t* v_full = bars + 5;     // [2]
-  uint64_t* v_empty = bars + 7;    // [2]
-  uint64_t* s_full = bars + 9;     // [2]
-  uint64_t* p_full = bars + 11;    // [2]
-  uint64_t* p_free = bars + 13;    // [2]
-  uint64_t* o_final = bars + 15;
-  uint64_t* drain = bars + 16;     // [2] one per MMA thread
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* r_full = bars + 1;     // [5 slots]
+  uint64_t* r_empty = bars + 6;    // [5 slots]
+  uint64_t* s_full = bars + 11;    // [2 tiles] S_t(j) ready (and PV_t(j-1) done)
+  uint64_t* p_full = bars + 13;    // [2 tiles] P_t(j) in TMEM, O_t rescaled
+  uint64_t* o_final = bars + 15;   // [2 tiles]
+  uint64_t* drain = bars + 17;     // [2] one per MMA issuer
+  uint64_t* turn = bars + 19;      // [2 tiles] the tile's softmax finished its exp pass
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * kBQ, h = blockIdx.y, n = blockIdx.z;
+  const int q0 = blockIdx.x * (kTiles * kBQ), h = blockIdx.y, n = blockIdx.z;
   const int kvh = h / (p.heads / p.kv_heads);
   int nkv = (p.Skv + kBK - 1) / kBK;
-  if (p.causal) nkv = min(nkv, (q0 + kBQ - 1) / kBK + 1);
+  if (p.causal) nkv = min(nkv, (q0 + kTiles * kBQ - 1) / kBK + 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < C_::SLOTS; ++i) {
+      mbar_init(&r_full[i], 1);
+      mbar_init(&r_empty[i], 2);  // both MMA issuers
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
-      mbar_init(&p_free[i], 1);
+      mbar_init(&o_final[i], 1);
       mbar_init(&drain[i], 1);
+      mbar_init(&turn[i], 4);
     }
-    mbar_init(o_final, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -135,210 +153,204 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  if (warp < 4) {
+  // Control warpgroup: gives its registers back (all four warps, warp-group aligned).
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
-    // K_j and V_j have separate 2-stage rings: K_j is released as soon as S_j is
-    // computed, V_j only after PV_j, so K loads run ahead of the PV chain.
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, C_::Q_BYTES);
-      for (int a = 0; a < C_::ATOMS; ++a)
-        tma_load_3d(sQ + a * C_::ATOM, &tmQ, q_full, h * p.dp + a * 64, q0, n);
-      int k_issued = -1, v_issued = -1;
-      bool ok = true;
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1u;
-        if (!mbar_wait(&k_empty[st], par, abort_flag, p.err, kErrAttnWait)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&k_full[st], C_::KV_BYTES);
+      mbar_arrive_expect_tx(q_full, kTiles * C_::Q_BYTES);
+      for (int t = 0; t < kTiles; ++t)
         for (int a = 0; a < C_::ATOMS; ++a)
-          tma_load_3d(sK + st * C_::KV_BYTES + a * C_::ATOM, &tmK, &k_full[st], kvh * p.dp + a * 64, j * kBK, n);
-        k_issued = j;
-        if (!mbar_wait(&v_empty[st], par, abort_flag, p.err, kErrAttnWait)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[st], C_::KV_BYTES);
+          tma_load_3d(sQ + t * C_::Q_BYTES + a * C_::ATOM, &tmQ, q_full, h * p.dp + a * 64, q0 + t * kBQ, n);
+      // Load i = 2j is K_j, i = 2j + 1 is V_j; slot i % SLOTS, use i / SLOTS of that slot.
+      int issued = -1;
+      for (int i = 0; i < 2 * nkv; ++i) {
+        const int sl = i % C_::SLOTS, u = i / C_::SLOTS;
+        if (!mbar_wait(&r_empty[sl], (u & 1) ^ 1u, abort_flag, p.err, kErrAttnWait)) break;
+        mbar_arrive_expect_tx(&r_full[sl], C_::KV_BYTES);
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         for (int a = 0; a < C_::ATOMS; ++a)
-          tma_load_3d(sV + st * C_::KV_BYTES + a * C_::ATOM, &tmV, &v_full[st], kvh * p.dp + a * 64, j * kBK, n);
-        v_issued = j;
+          tma_load_3d(sR + sl * C_::KV_BYTES + a * C_::ATOM, tm, &r_full[sl], kvh * p.dp + a * 64, (i >> 1) * kBK, n);
+        issued = i;
       }
-      if (!ok) {
+      if (issued < 2 * nkv - 1) {
         // Aborted: wait (bounded) for the loads this CTA still has in flight.
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
-        for (int j = max(0, k_issued - 1); j <= k_issued; ++j)
-          while (!mbar_try_wait(&k_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
-          }
-        for (int j = max(0, v_issued - 1); j <= v_issued; ++j)
-          while (!mbar_try_wait(&v_full[j & 1], (j >> 1) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        for (int i = max(0, issued - C_::SLOTS + 1); i <= issued; ++i)
+          while (!mbar_try_wait(&r_full[i % C_::SLOTS], (i / C_::SLOTS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {
           }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------ QK^T issuer -------------------------------
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------ MMA issuers -------------------------------
+    const int t = warp - 1;
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrAttnWait);
       tc_fence_after();
-      const uint32_t q_addr = smem_u32(sQ);
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int st = j & 1;
-        // S buffer j&1 is free once the softmax has consumed S_{j-2} (it posted P_{j-2}).
-        if (j >= 2 && !mbar_wait(&p_full[st], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + st * C_::KV_BYTES);
-        const uint32_t d_s = tmem + (uint32_t)(st * kBK);
+      const uint32_t q_addr = smem_u32(sQ + t * C_::Q_BYTES);
+      const uint32_t d_s = tmem + (uint32_t)(t * kBK);  // S_t; P_t over its first 64 columns
+      const uint32_t d_o = tmem + C_::O_COL + (uint32_t)(t * DP);
+      // Descriptors of the K steps (16 wide): Q_t (fixed), P_t in TMEM (8 columns per
+      // step), K_j and V_(j-1) per step, all built before the waits so that the eight
+      // MMAs of a product issue back to back.
+      static_assert(DP == 64 || DP == 128, "head dim padded to 64 or 128");
+      uint64_t qd[8] = {};
+      uint32_t pa[8];
 #pragma unroll
-        for (int ks = 0; ks < DP / 16; ++ks) {
-          const uint32_t off = (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32);
-          umma_f16_ss(d_s, sdesc_k_sw128(q_addr + off), sdesc_k_sw128(k_addr + off), IDESC_S, ks > 0);
-        }
-        umma_commit(&s_full[st]);
-        umma_commit(&k_empty[st]);
+      for (int ks = 0; ks < 8; ++ks) {
+        if (ks < DP / 16) qd[ks] = sdesc_k_sw128(q_addr + (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32));
+        pa[ks] = d_s + (uint32_t)(ks * 8);
       }
-      umma_commit(&drain[0]);
+      for (int j = 0; ok && j <= nkv; ++j) {
+        const int vsl = (2 * j - 1 + C_::SLOTS) % C_::SLOTS, ksl = (2 * j) % C_::SLOTS;
+        const uint32_t v_addr = smem_u32(sR + vsl * C_::KV_BYTES), k_addr = smem_u32(sR + ksl * C_::KV_BYTES);
+        uint64_t vd[8], kd[8] = {};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          vd[ks] = sdesc_mn_sw128(v_addr + (uint32_t)(ks * 16 * 128), C_::ATOM, 1024);
+          if (ks < DP / 16) kd[ks] = sdesc_k_sw128(k_addr + (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32));
+        }
+        // K_j and V_(j-1) normally landed long ago; wait for them before P_t(j-1), so
+        // the PV and the QK^T go out back to back once P is there.
+        if (j > 0 && !mbar_wait(&r_full[vsl], ((2 * j - 1) / C_::SLOTS) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        if (j < nkv && !mbar_wait(&r_full[ksl], ((2 * j) / C_::SLOTS) & 1, abort_flag, p.err, kErrAttnWait)) break;
+        if (j > 0) {
+          // O_t += P_t(j-1) V_(j-1): A = P from TMEM, B = V (MN-major).
+          if (!mbar_wait(&p_full[t], (j - 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+          tc_fence_after();
+          umma8_f16_ts(d_o, pa, vd, IDESC_O, j > 1 ? 1u : 0u);
+          umma_commit(&r_empty[vsl]);
+        }
+        if (j < nkv) {
+          // S_t = Q_t K_j^T
+          tc_fence_after();
+          if constexpr (DP == 128)
+            umma8_f16_ss(d_s, qd, kd, IDESC_S, 0u);
+          else
+            umma4_f16_ss(d_s, qd, kd, IDESC_S, 0u);  // dp = 64: four K steps
+          umma_commit(&s_full[t]);
+          umma_commit(&r_empty[ksl]);
+        }
+      }
+      umma_commit(&o_final[t]);
+      umma_commit(&drain[t]);
       const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&drain[0], 0))
+      while (!mbar_try_wait(&drain[t], 0))
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           atomicOr(p.err, kErrWaitDrain);
           break;
         }
     }
-  } else if (warp == 2) {
-    // ------------------------------ PV issuer ---------------------------------
-    if (lane == 0) {
-      for (int j = 0; j < nkv; ++j) {
-        const int b = j & 1;
-        if (!mbar_wait(&p_full[b], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-        if (!mbar_wait(&v_full[b], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + b * C_::P_BYTES);
-        const uint32_t v_addr = smem_u32(sV + b * C_::KV_BYTES);
-#pragma unroll
-        for (int ks = 0; ks < kBK / 16; ++ks) {
-          const uint64_t ad = sdesc_k_sw128(p_addr + (uint32_t)((ks >> 2) * C_::ATOM + (ks & 3) * 32));
-          const uint64_t bd = sdesc_mn_sw128(v_addr + (uint32_t)(ks * 16 * 128), C_::ATOM, 1024);
-          umma_f16_ss(tmem + C_::O_COL, ad, bd, IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(&p_free[b]);
-        umma_commit(&v_empty[b]);
-      }
-      umma_commit(o_final);
-      umma_commit(&drain[1]);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&drain[1], 0))
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          atomicOr(p.err, kErrWaitDrain);
-          break;
-        }
-    }
+  }
   } else {
     // ------------------------------ softmax / epilogue ------------------------
-    const int qq = warp & 3;
-    const int r = qq * 32 + lane;     // tile row == TMEM lane
-    const int row = q0 + r;           // query index
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    const int t = (warp - 4) >> 2;   // query tile of this warpgroup (warps 4..11)
+    const int qq = warp & 3;         // TMEM lane quarter this warp may access
+    const int r = qq * 32 + lane;    // tile row == TMEM lane
+    const int row = q0 + t * kBQ + r;
+    const int tile_q0 = q0 + t * kBQ;
     const uint32_t lane_base = tmem + ((uint32_t)(qq * 32) << 16);
+    const uint32_t s_addr = lane_base + (uint32_t)(t * kBK);
+    const uint32_t o_addr = lane_base + C_::O_COL + (uint32_t)(t * DP);
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
+    // Keys past Skv (and, if causal, past the row) read as -inf. full_tile is uniform
+    // over the CTA, so the fast path runs no per-score mask code.
+    auto mask_row = [&](uint32_t(&u)[4][32], int key0) {
+#pragma unroll
+      for (int c = 0; c < kBK; ++c) {
+        const int key = key0 + c;
+        if (key >= p.Skv || (p.causal && key > row)) u[c >> 5][c & 31] = 0xff800000u;
+      }
+    };
     for (int j = 0; j < nkv; ++j) {
-      const int b = j & 1;
-      if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, p.err, kErrAttnWait)) {
+      if (!mbar_wait(&s_full[t], j & 1, abort_flag, p.err, kErrAttnWait)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // All 128 scores of this row in registers: four 32-column TMEM loads, one wait.
+      const int kbase = j * kBK;
+      const bool full_tile = (kbase + kBK <= p.Skv) && (!p.causal || kbase + kBK - 1 <= tile_q0);
+      // The whole 128-key row of S in registers: one TMEM round trip per step.
       uint32_t u[4][32];
       __syncwarp();
-      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 0), u[0]);
-      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 32), u[1]);
-      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 64), u[2]);
-      tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBK + 96), u[3]);
-      tmem_wait_ld();
-      const int kbase = j * kBK;
-      const bool full_tile = (kbase + kBK <= p.Skv) && (!p.causal || kbase + kBK - 1 <= q0);
-      if (!full_tile) {
 #pragma unroll
-        for (int c = 0; c < kBK; ++c) {
-          const int key = kbase + c;
-          if (key >= p.Skv || (p.causal && key > row)) u[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-        }
-      }
-      // Row max of the raw scores, 4 partial maxima (short dependency chains); the
-      // scale is positive, so max(s) * scale = max(s * scale).
+      for (int g = 0; g < 4; ++g) tmem_ld_32x32b_x32(s_addr + (uint32_t)(g * 32), u[g]);
+      tmem_wait_ld();
+      if (!full_tile) mask_row(u, kbase);
+      // Row max of the raw scores, 4 partial maxima; the scale is positive, so
+      // max(s) * scale = max(s * scale).
       float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kBK; ++c) pm[c & 3] = fmaxf(pm[c & 3], __uint_as_float(u[c >> 5][c & 31]));
+      for (int c = 0; c < kBK; c += 8)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          pm[i] = fmax3(pm[i], __uint_as_float(u[c >> 5][(c & 31) + 2 * i]), __uint_as_float(u[c >> 5][(c & 31) + 2 * i + 1]));
       const float mx = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       const bool need = m_new > m_used + kRescaleThreshold;
+      // PV_t(j-1) completed before S_t(j) was posted, so O_t can be rescaled here.
       if (__any_sync(0xffffffffu, need)) {
         if (j > 0) {
-          // O must hold PV_{j-1} before it is rescaled.
-          if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.err, kErrAttnWait)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           const float f = need ? ex2_approx(m_used - m_new) : 1.0f;
 #pragma unroll 1
           for (int c = 0; c < DP; c += 32) {
             uint32_t o[32];
             __syncwarp();
-            tmem_ld_32x32b_x32(lane_base + C_::O_COL + (uint32_t)c, o);
+            tmem_ld_32x32b_x32(o_addr + (uint32_t)c, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st_32x32b_x32(lane_base + C_::O_COL + (uint32_t)c, o);
+            tmem_st_32x32b_x32(o_addr + (uint32_t)c, o);
           }
-          tmem_wait_st();
         }
         if (need) {
           l *= ex2_approx(m_used - m_new);
           m_used = m_new;
         }
       }
-      // The P buffer of this tile must no longer be read by PV_{j-2}.
-      if (j >= 2 && !mbar_wait(&p_free[b], ((j - 2) >> 1) & 1, abort_flag, p.err, kErrAttnWait)) {
+      // The two softmax warpgroups take turns at the exp pass (A(0), B(0), A(1), ...), so
+      // that each has the MUFU pipes to itself while the tensor core runs the other
+      // tile's MMAs; left alone they fall into lockstep and the MMAs of both tiles wait.
+      if (!(t == 0 && j == 0) &&
+          !mbar_wait(&turn[t ^ 1], (t == 0 ? j - 1 : j) & 1, abort_flag, p.err, kErrAttnWait)) {
         ok = false;
         break;
       }
-      // p = 2^(s * scale_log2 - m): one FFMA + one MUFU ex2 per score, 4 partial sums,
-      // written as fp16 into the 128B-swizzled K-major P tile: keys [64a, 64a+64) form
-      // atom a; 16-byte chunk c of row r sits at chunk position c ^ (r & 7).
+      // p = 2^(s * scale_log2 - m) (one FFMA + one MUFU ex2 per score), 4 partial sums; keys
+      // 2c and 2c + 1 of the tile go to TMEM column c of S_t as an fp16 pair, the layout
+      // of a 16-bit A operand in tensor memory.
       const float neg_m = (m_used == -INFINITY) ? 0.0f : -m_used;
       float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      uint8_t* pb = sP + b * C_::P_BYTES + r * 128;
 #pragma unroll
-      for (int a = 0; a < 2; ++a)
+      for (int g = 0; g < 4; ++g) {
+        uint32_t w[16];
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          float e[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int c = a * 64 + cc * 8 + i;
-            e[i] = ex2_approx(fmaf(__uint_as_float(u[c >> 5][c & 31]), p.scale_log2, neg_m));
-            ps[i & 3] += e[i];
-          }
-          uint4 w;
-          w.x = pack_half2(e[0], e[1]);
-          w.y = pack_half2(e[2], e[3]);
-          w.z = pack_half2(e[4], e[5]);
-          w.w = pack_half2(e[6], e[7]);
-          *reinterpret_cast<uint4*>(pb + a * C_::ATOM + ((cc ^ (r & 7)) << 4)) = w;
+        for (int c = 0; c < 16; ++c) {
+          const float x0 = fmaf(__uint_as_float(u[g][2 * c]), p.scale_log2, neg_m);
+          const float x1 = fmaf(__uint_as_float(u[g][2 * c + 1]), p.scale_log2, neg_m);
+          const float e0 = ex2_approx(x0);
+          const float e1 = ex2_approx(x1);
+          ps[(2 * c) & 3] += e0;
+          ps[(2 * c + 1) & 3] += e1;
+          w[c] = pack_half2(e0, e1);
         }
+        tmem_st_32x32b_x16(s_addr + (uint32_t)(g * 16), w);
+      }
       l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) {
+        mbar_arrive(&p_full[t]);
+        mbar_arrive(&turn[t]);
+      }
     }
-    if (ok && mbar_wait(o_final, 0, abort_flag, p.err, kErrAttnWait)) {
+    if (ok && mbar_wait(&o_final[t], 0, abort_flag, p.err, kErrAttnWait)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       const bool row_ok = row < p.Sq;
@@ -346,16 +358,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < DP; c += 32) {
         uint32_t o[32];
         __syncwarp();
-        tmem_ld_32x32b_x32(lane_base + C_::O_COL + (uint32_t)c, o);
+        tmem_ld_32x32b_x32(o_addr + (uint32_t)c, o);
         tmem_wait_ld();
         if (!row_ok || c >= p.d) continue;
         const long long base = (long long)n * p.out_batch + (long long)row * p.out_row + (long long)h * p.d + c;
         const int cnt = min(32, p.d - c);
         if (p.out_bf16) {
           uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + base;
+          if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < cnt) dst[i] = f32_to_bf16_rne(__uint_as_float(o[i]) * inv);
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
+              w.y = pack_bf16x2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              w.z = pack_bf16x2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+              w.w = pack_bf16x2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + i) = w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < cnt) dst[i] = f32_to_bf16_rne(__uint_as_float(o[i]) * inv);
+          }
         } else {
           float* dst = reinterpret_cast<float*>(p.out) + base;
           if (cnt == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
@@ -436,11 +460,18 @@ void launch_tc(const __half* q, const __half* k, const __half* v, void* out, lon
   static bool attr_set[64] = {};
   const int dev = ctx().device;
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    // setmaxnreg.inc waits until the registers it asks for are free; the split only adds
+    // up if the kernel was compiled to exactly kRegsLaunch registers per thread.
+    cudaFuncAttributes fa{};
+    check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(attention)");
+    if (fa.numRegs != kRegsLaunch)
+      fail(kErrUnsupported, "attention_tc: compiled with " + std::to_string(fa.numRegs) +
+                                " registers per thread, the register split needs " + std::to_string(kRegsLaunch));
     check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM),
                "cudaFuncSetAttribute(attention)");
     attr_set[dev] = true;
   }
-  dim3 grid((unsigned)((Sq + kBQ - 1) / kBQ), (unsigned)heads, (unsigned)N);
+  dim3 grid((unsigned)((Sq + kTiles * kBQ - 1) / (kTiles * kBQ)), (unsigned)heads, (unsigned)N);
   kern<<<grid, kThreads, C_::SMEM, ctx().stream>>>(tq, tk, tv, p);
   check_launch("attention_tc");
 }

@@ -182,6 +182,69 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Eight back-to-back kind::f16 MMAs (K = 8 x 16) into one accumulator from a single asm
+// block, with every descriptor computed beforehand: one issued instruction per MMA, so a
+// warp that shares its scheduler with busy warps still keeps the tensor pipe fed. The
+// first MMA accumulates iff acc_first != 0, the other seven always do.
+__device__ __forceinline__ void umma8_f16_ss(uint32_t d_tmem, const uint64_t (&a)[8], const uint64_t (&b)[8],
+                                             uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %17, 0;\n\t"
+      "setp.eq.b32 p1, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %9, %18, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %10, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %11, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %12, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %13, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %14, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %15, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %16, %18, p1;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
+// Four back-to-back kind::f16 MMAs (K = 4 x 16), as umma8_f16_ss.
+__device__ __forceinline__ void umma4_f16_ss(uint32_t d_tmem, const uint64_t (&a)[8], const uint64_t (&b)[8],
+                                             uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %9, 0;\n\t"
+      "setp.eq.b32 p1, %9, %9;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %10, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %10, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %10, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %10, p1;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(acc_first),
+      "r"(idesc)
+      : "memory");
+}
+
+// As umma8_f16_ss with the A operand in tensor memory: a[i] is the TMEM address of the
+// i-th 16-wide K slice (8 columns of 16-bit pairs further on per slice).
+__device__ __forceinline__ void umma8_f16_ts(uint32_t d_tmem, const uint32_t (&a)[8], const uint64_t (&b)[8],
+                                             uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %17, 0;\n\t"
+      "setp.eq.b32 p1, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %18, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %13, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %14, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %15, %18, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %16, %18, p1;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
 // Arrives once on `bar` when all previously issued tcgen05 async ops of this thread
 // have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
