@@ -115,7 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_final = bars + 15;   // [2 tiles]
   uint64_t* drain = bars + 17;     // [2] one per MMA issuer
   uint64_t* turn = bars + 19;      // [2 tiles] the tile's softmax finished its exp pass
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  uint64_t* p_half = bars + 21;    // [2 tiles] keys 0..63 of P_t(j) in TMEM, O_t rescaled
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_final[i], 1);
       mbar_init(&drain[i], 1);
       mbar_init(&turn[i], 4);
+      mbar_init(&p_half[i], 4);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -218,10 +220,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j > 0 && !mbar_wait(&r_full[vsl], ((2 * j - 1) / C_::SLOTS) & 1, abort_flag, p.err, kErrAttnWait)) break;
         if (j < nkv && !mbar_wait(&r_full[ksl], ((2 * j) / C_::SLOTS) & 1, abort_flag, p.err, kErrAttnWait)) break;
         if (j > 0) {
-          // O_t += P_t(j-1) V_(j-1): A = P from TMEM, B = V (MN-major).
+          // O_t += P_t(j-1) V_(j-1): A = P from TMEM, B = V (MN-major). Keys 0..63 go as
+          // soon as the softmax has posted them, keys 64..127 once P is complete.
+          if (!mbar_wait(&p_half[t], (j - 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
+          tc_fence_after();
+          {
+            const uint32_t a4[4] = {pa[0], pa[1], pa[2], pa[3]};
+            const uint64_t b4[4] = {vd[0], vd[1], vd[2], vd[3]};
+            umma4_f16_ts(d_o, a4, b4, IDESC_O, j > 1 ? 1u : 0u);
+          }
           if (!mbar_wait(&p_full[t], (j - 1) & 1, abort_flag, p.err, kErrAttnWait)) break;
           tc_fence_after();
-          umma8_f16_ts(d_o, pa, vd, IDESC_O, j > 1 ? 1u : 0u);
+          {
+            const uint32_t a4[4] = {pa[4], pa[5], pa[6], pa[7]};
+            const uint64_t b4[4] = {vd[4], vd[5], vd[6], vd[7]};
+            umma4_f16_ts(d_o, a4, b4, IDESC_O, 1u);
+          }
           umma_commit(&r_empty[vsl]);
         }
         if (j < nkv) {
@@ -229,8 +243,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           if constexpr (DP == 128)
             umma8_f16_ss(d_s, qd, kd, IDESC_S, 0u);
-          else
-            umma4_f16_ss(d_s, qd, kd, IDESC_S, 0u);  // dp = 64: four K steps
+          else {
+            const uint64_t a4[4] = {qd[0], qd[1], qd[2], qd[3]};  // dp = 64: four K steps
+            const uint64_t b4[4] = {kd[0], kd[1], kd[2], kd[3]};
+            umma4_f16_ss(d_s, a4, b4, IDESC_S, 0u);
+          }
           umma_commit(&s_full[t]);
           umma_commit(&r_empty[ksl]);
         }
@@ -340,6 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           w[c] = pack_half2(e0, e1);
         }
         tmem_st_32x32b_x16(s_addr + (uint32_t)(g * 16), w);
+        if (g == 1) {
+          // Keys 0..63 are in place: the PV of this half can start.
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_half[t]);
+        }
       }
       l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       tmem_wait_st();

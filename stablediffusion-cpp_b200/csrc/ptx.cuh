@@ -207,7 +207,7 @@ __device__ __forceinline__ void umma8_f16_ss(uint32_t d_tmem, const uint64_t (&a
 }
 
 // Four back-to-back kind::f16 MMAs (K = 4 x 16), as umma8_f16_ss.
-__device__ __forceinline__ void umma4_f16_ss(uint32_t d_tmem, const uint64_t (&a)[8], const uint64_t (&b)[8],
+__device__ __forceinline__ void umma4_f16_ss(uint32_t d_tmem, const uint64_t (&a)[4], const uint64_t (&b)[4],
                                              uint32_t idesc, uint32_t acc_first) {
   asm volatile(
       "{\n\t.reg .pred p0, p1;\n\t"
@@ -219,6 +219,23 @@ __device__ __forceinline__ void umma4_f16_ss(uint32_t d_tmem, const uint64_t (&a
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %10, p1;\n\t"
       "}\n" ::"r"(d_tmem),
       "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(acc_first),
+      "r"(idesc)
+      : "memory");
+}
+
+// Four back-to-back kind::f16 MMAs with the A operand in tensor memory, as umma8_f16_ts.
+__device__ __forceinline__ void umma4_f16_ts(uint32_t d_tmem, const uint32_t (&a)[4], const uint64_t (&b)[4],
+                                             uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %9, 0;\n\t"
+      "setp.eq.b32 p1, %9, %9;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %10, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %10, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %10, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %10, p1;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "r"(acc_first),
       "r"(idesc)
       : "memory");
 }
