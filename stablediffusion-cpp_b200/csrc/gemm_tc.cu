@@ -22,6 +22,8 @@
 //     word and the CTA drains and frees TMEM instead of hanging the GPU.
 #include <algorithm>
 #include <cstdio>
+#include <cuda_fp16.h>
+
 #include <string>
 
 #include "internal.h"
@@ -45,6 +47,7 @@ struct GemmParams {
   int out_bf16;  // store bf16 instead of fp32
   int vec_ok;    // C base and ldc allow 16-byte stores
   int* err;
+  QkvRope rope;  // Epi::kQkvRope
 };
 
 template <int BN>
@@ -110,6 +113,85 @@ __device__ __forceinline__ void store_row32(const GemmParams& p, int row, int co
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < n) c[j] = p.accumulate ? c[j] + v[j] : v[j];
+  }
+}
+
+// Epi::kQkvRope for one row and one 128-column head of the accumulator at TMEM address
+// `hcol` (lane of this thread), head columns [col0, col0 + 128) of the GEMM output.
+// q and k: two passes over TMEM (sum of squares, then normalise, gamma, rotate, store);
+// v: one pass. The rotary pair (2i, 2i+1) maps to (x0 c - x1 s, x1 c + x0 s) with the
+// angle's cos c / sin s stored at both 2i and 2i + 1 of the table row.
+__device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol, int row, bool row_ok, int col0) {
+  const QkvRope& q = p.rope;
+  const int which = col0 / q.Dq;  // 0 q, 1 k, 2 v
+  const int hc = col0 - which * q.Dq;
+  __half* dst = reinterpret_cast<__half*>(which == 0 ? q.q16 : which == 1 ? q.k16 : q.v16) +
+                (long long)row * q.Dq + hc;
+  auto load = [&](int cc, float (&v)[32]) {
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the masked stores
+    tmem_ld_32x32b_x32(hcol + (uint32_t)(cc * 32), r);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (p.bias) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + cc * 32 + j);
+    }
+  };
+  auto store32 = [&](int cc, const float (&o)[32]) {
+    if (!row_ok) return;
+    uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      __half2 h0 = __floats2half2_rn(o[j], o[j + 1]), h1 = __floats2half2_rn(o[j + 2], o[j + 3]);
+      __half2 h2 = __floats2half2_rn(o[j + 4], o[j + 5]), h3 = __floats2half2_rn(o[j + 6], o[j + 7]);
+      w.x = *reinterpret_cast<uint32_t*>(&h0);
+      w.y = *reinterpret_cast<uint32_t*>(&h1);
+      w.z = *reinterpret_cast<uint32_t*>(&h2);
+      w.w = *reinterpret_cast<uint32_t*>(&h3);
+      d4[j / 8] = w;
+    }
+  };
+  if (which == 2) {
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      float v[32];
+      load(cc, v);
+      store32(cc, v);
+    }
+    return;
+  }
+  float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    float v[32];
+    load(cc, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ss[j & 3] = fmaf(v[j], v[j], ss[j & 3]);
+  }
+  const float rstd = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / 128.0f + q.eps);
+  const float* gam = which == 0 ? q.gq : q.gk;
+  const int s = row_ok ? row % q.S : 0;
+  const float* cr = q.cs + (long long)s * 128;
+  const float* sr = q.sn + (long long)s * 128;
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    float v[32], o[32];
+    load(cc, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gam ? v[j] * rstd * __ldg(gam + cc * 32 + j) : v[j] * rstd;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr + cc * 32 + j));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr + cc * 32 + j));
+      o[j] = v[j] * c4.x - v[j + 1] * s4.x;
+      o[j + 1] = v[j + 1] * c4.x + v[j] * s4.x;
+      o[j + 2] = v[j + 2] * c4.z - v[j + 3] * s4.z;
+      o[j + 3] = v[j + 3] * c4.z + v[j + 2] * s4.z;
+    }
+    store32(cc, o);
   }
 }
 
@@ -303,6 +385,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + q * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (BN % 128 == 0) {
+        if (p.epi == (int)Epi::kQkvRope) {
+          // The launcher only pairs this epilogue with 128- or 256-column tiles, which
+          // hold whole heads; N = 3 Dq is a multiple of 128.
+#pragma unroll 1
+          for (int hg = 0; hg < BN / 128; ++hg) {
+            const int col0 = nb * BN + hg * 128;
+            if (col0 >= p.N) break;  // uniform over the warp
+            qkv_rope_head(p, tbase + (uint32_t)(hg * 128), row, row_ok, col0);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -424,12 +524,14 @@ void launch_bn_explicit(const GemmCall& g, const GemmParams& p, int num_sms, cud
 }
 
 int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
-  (void)epi;  // every candidate BN is a multiple of the 32-column gated chunk
+  // Every candidate BN is a multiple of the 32-column gated chunk; the QKV epilogue
+  // needs whole 128-column heads per tile.
   const int cands[4] = {256, 192, 128, 64};
   int best = 256;
   double best_cost = 1e30;
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   for (int bn : cands) {
+    if (epi == Epi::kQkvRope && bn % 128 != 0) continue;
     const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
     const int64_t waves = (tiles + num_sms - 1) / num_sms;
     // Per-tile time grows with BN; 48 columns of fixed cost model the lower
@@ -455,7 +557,12 @@ void launch_gemm_tc(const GemmCall& g) {
   p.M = (int)g.M;
   p.N = (int)g.N;
   p.K = (int)g.K;
-  const int bn = g.bn ? g.bn : g_forced_bn ? g_forced_bn : choose_bn(g.M, g.N, c.num_sms, g.epi);
+  int bn = g.bn ? g.bn : g_forced_bn ? g_forced_bn : choose_bn(g.M, g.N, c.num_sms, g.epi);
+  if (g.epi == Epi::kQkvRope) {
+    if (!g.rope || g.tf32 || g.N % 128 != 0 || g.N != 3 * (int64_t)g.rope->Dq)
+      fail(kErrInvalidArg, "gemm_tc: QKV epilogue needs bf16 operands and N = 3 * Dq, Dq % 128 == 0");
+    if (bn % 128 != 0) bn = choose_bn(g.M, g.N, c.num_sms, g.epi);
+  }
   p.m_tiles = (int)((g.M + kBM - 1) / kBM);
   p.n_tiles = (int)((g.N + bn - 1) / bn);
   p.num_tiles = p.m_tiles * p.n_tiles;
@@ -470,6 +577,7 @@ void launch_gemm_tc(const GemmCall& g) {
   const int oesz = g.out_bf16 ? 2 : 4;
   p.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * oesz) % 16 == 0);
   p.err = c.err_word;
+  if (g.rope) p.rope = *g.rope;
   if (g.tf32) {
     switch (bn) {
       case 256: launch_bn<256, true>(g, p, c.num_sms); break;
@@ -493,6 +601,7 @@ void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream
   p.M = (int)g.M;
   p.N = (int)g.N;
   p.K = (int)g.K;
+  if (g.epi == Epi::kQkvRope) fail(kErrInvalidArg, "gemm_tc: the QKV epilogue needs a device context");
   const int bn = g.bn ? g.bn : choose_bn(g.M, g.N, num_sms, g.epi);
   p.m_tiles = (int)((g.M + kBM - 1) / kBM);
   p.n_tiles = (int)((g.N + bn - 1) / bn);

@@ -72,6 +72,23 @@ enum class Epi : int {
   kStore = 0,      // C = acc (+bias) (+C)
   kSwiglu = 1,     // columns interleaved gate/up per 16: Y[m, n/2] = silu(g) * u
   kGeglu = 2,      // columns interleaved value/gate per 16: Y[m, n/2] = v * gelu_erf(g)
+  kQkvRope = 3,    // fused-QKV output [rows, 3 Dq] -> fp16 q, k (RMS-normalised, rotated), v
+};
+// Operands of Epi::kQkvRope. The GEMM output columns are q | k | v, Dq = heads * 128
+// each; row r is token r % S of its sequence. Per 128-column head of q and k: RMS norm
+// over the head (eps), times gamma, then interleaved rotary pairs (2i, 2i+1) with the
+// token's cos / sin row; v is only converted. All three go to fp16 [rows, Dq].
+struct QkvRope {
+  int S;
+  int Dq;
+  const float* gq;  // [128] or null (1)
+  const float* gk;  // [128] or null (1)
+  const float* cs;  // [S, 128], each angle at 2i and 2i + 1
+  const float* sn;  // [S, 128]
+  float eps;
+  void* q16;
+  void* k16;
+  void* v16;
 };
 struct GemmCall {
   int64_t M, N, K;
@@ -87,6 +104,7 @@ struct GemmCall {
   Epi epi;
   bool out_bf16;    // store C as bf16 (ldc in bf16 elements); no accumulate
   int bn;           // 0 = choose
+  const QkvRope* rope = nullptr;  // Epi::kQkvRope only (C unused)
 };
 void launch_gemm_tc(const GemmCall& g);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
@@ -139,6 +157,8 @@ void gemm_nt_bf16_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t 
                        float* C, int64_t ldc, const float* bias, bool acc);
 void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                       float* C, int64_t ldc, const float* bias, bool acc);
+void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
+                             int64_t ldb, const float* bias, const QkvRope& r);
 void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16,
                              const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, bool y_bf16, const float* bias,
                              int epi);

@@ -48,7 +48,8 @@ void check_gemm_args(const char* op, int64_t M, int64_t N, int64_t K, const void
 
 // bf16 x bf16 GEMM with A either fp32 (packed here) or bf16.
 void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
-                    int64_t ldb, void* C, int64_t ldc, bool c_bf16, const float* bias, bool acc, Epi epi) {
+                    int64_t ldb, void* C, int64_t ldc, bool c_bf16, const float* bias, bool acc, Epi epi,
+                    const QkvRope* rope = nullptr) {
   const int64_t Kp = round_up(K, 8);  // 16-byte rows of bf16
   const bool a_direct = a_bf16 && aligned16(A) && (lda % 8 == 0);
   const bool b_direct = aligned16(B) && (ldb % 8 == 0);
@@ -90,6 +91,7 @@ void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
   g.epi = epi;
   g.out_bf16 = c_bf16;
   g.bn = 0;
+  g.rope = rope;
   launch_gemm_tc(g);
 }
 
@@ -161,6 +163,30 @@ void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int
   check_gemm_args(op, M, ncols, K, A, lda, B, ldb, Y, ldy);
   require(K > 0, op, "K == 0");
   gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, Y, ldy, y_bf16, bias, false, (Epi)epi);
+}
+
+// Fused-QKV projection with the attention prologue in the GEMM epilogue: X[M, K] times
+// Wqkv[3 Dq, K]^T (+bias), then per head the q / k RMS norm, rotary embedding and fp16
+// packing of zimage.cpp:117-120 (Epi::kQkvRope). q16 / k16 / v16 are fp16 [M, Dq].
+void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
+                             int64_t ldb, const float* bias, const QkvRope& r) {
+  const char* op = "gemm_bf16_qkv_rope";
+  require(r.Dq > 0 && r.Dq % 128 == 0, op, "Dq must be a positive multiple of 128");
+  require(r.S > 0, op, "S must be positive");
+  require_ptr(r.cs, op, "cs");
+  require_ptr(r.sn, op, "sn");
+  require_ptr(r.q16, op, "q16");
+  require_ptr(r.k16, op, "k16");
+  require_ptr(r.v16, op, "v16");
+  require((((uintptr_t)r.q16 | (uintptr_t)r.k16 | (uintptr_t)r.v16 | (uintptr_t)r.cs | (uintptr_t)r.sn) & 15) == 0, op,
+          "outputs and tables must be 16-byte aligned");
+  if (M <= 0) return;
+  const int64_t N = 3 * (int64_t)r.Dq;
+  require(K > 0, op, "K == 0");
+  require_ptr(A, op, "A");
+  require_ptr(B, op, "B");
+  require(lda >= K && ldb >= K, op, "leading dimension < K");
+  gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kQkvRope, &r);
 }
 
 // conv2d as im2col + tf32 GEMM, writing NCHW directly (ldc = HW), as

@@ -6,8 +6,9 @@
 //   mod  = adaLN(t_emb)               GEMV, M=1 (bf16 W)        -> k_gemm_skinny
 //          1 + s, tanh(g)             affine_/tanh_             -> k_adaln_split
 //   h    = bf16(rms_norm(x)*scale)    rms_norm + mul_rows_      -> k_rms_mod_bf16
-//   qkv  = h Wqkv^T                   to_q / to_k / to_v (3 GEMMs) -> one tcgen05 GEMM, N = 3D
-//   q,k,v -> fp16 heads               rms_norm_heads_ + rope_   -> k_qk_norm_rope_pack
+//   qkv  = h Wqkv^T                   to_q / to_k / to_v (3 GEMMs) -> one tcgen05 GEMM, N = 3D,
+//   q,k,v -> fp16 heads               rms_norm_heads_ + rope_      whose epilogue normalises,
+//                                                                  rotates and packs (kQkvRope)
 //   o    = attention(q,k,v)           attention                  -> k_attention_tc (bf16 out)
 //   a    = o Wout^T                   to_out                     -> tcgen05 GEMM
 //   x   += g_msa * rms_norm(a)        rms_norm + add_rows_scaled_ -> k_post_norm_residual
@@ -299,7 +300,7 @@ class ZImage {
   bool has(const std::string& n) const { return w.count(n) != 0; }
 
   // ---- activations (grown on demand) ----------------------------------------------
-  DBuf tok, img, cap, uni, h, qkv, q16, k16, v16, ao, a, g, mod, temb, thid, adaln, fscale, capn, outtok, fin;
+  DBuf tok, img, cap, uni, h, q16, k16, v16, ao, a, g, mod, temb, thid, adaln, fscale, capn, outtok, fin;
   std::map<std::array<int64_t, 3>, std::unique_ptr<DBuf[]>> tables;  // (Ht, Wt, n_cap_pad) -> cos/sin sets
 
   // Rotary tables for (axis0, h, w) positions, interleaved layout (zimage.cpp:71-88):
@@ -374,14 +375,23 @@ class ZImage {
     const int64_t Dq = b.Dq;
     const int Hl = b.heads_local;
     const double gf = 2.0 * (double)R;  // 2*M, times N*K per GEMM below
+    // QKV projection with the QK norm, rotary embedding and fp16 head packing in the GEMM
+    // epilogue (q16 / k16 / v16 = [B*S, Dq] = [B, S, heads, 128]).
+    QkvRope rp{};
+    rp.S = (int)S;
+    rp.Dq = (int)Dq;
+    rp.gq = b.norm_q;
+    rp.gk = b.norm_k;
+    rp.cs = cs;
+    rp.sn = sn;
+    rp.eps = 1e-5f;
+    rp.q16 = q16.p;
+    rp.k16 = k16.p;
+    rp.v16 = v16.p;
     timed(0, gf * 3 * Dq * D, [&] {
-      gemm_bf16_epilogue_impl(R, 3 * Dq, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, qkv.p, 3 * Dq, false,
-                              b.has_bqkv ? b.bqkv.as<float>() : nullptr, 0);
+      gemm_bf16_qkv_rope_impl(R, D, h.p, D, true, b.wqkv.as<uint16_t>(), D, b.has_bqkv ? b.bqkv.as<float>() : nullptr,
+                              rp);
     });
-    for (int64_t n = 0; n < B; ++n)
-      dit_qk_norm_rope_pack(qkv.as<float>() + n * S * 3 * Dq, (int)S, Hl, b.norm_q, b.norm_k, cs, sn, 1e-5f,
-                            q16.as<uint8_t>() + n * S * Dq * 2, k16.as<uint8_t>() + n * S * Dq * 2,
-                            v16.as<uint8_t>() + n * S * Dq * 2);
     timed(1, 4.0 * (double)B * S * S * Dq, [&] {
       launch_attention_f16(q16.p, k16.p, v16.p, ao.p, Dq, S * Dq, true, B, S, S, Hl, Hl, head_dim, 128, false);
     });
@@ -429,7 +439,6 @@ class ZImage {
     cap.ensure((size_t)(B * n_cap_pad * D) * 4);
     uni.ensure((size_t)(Rmax * D) * 4);
     h.ensure((size_t)(Rmax * D) * 2);
-    qkv.ensure((size_t)(Rmax * 3 * Dq) * 4);
     q16.ensure((size_t)(Rmax * Dq) * 2);
     k16.ensure((size_t)(Rmax * Dq) * 2);
     v16.ensure((size_t)(Rmax * Dq) * 2);
