@@ -1,12 +1,11 @@
 // dit_ops.cu - the memory-bound glue of one Z-Image DiT block, fused around the
 // tensor-core GEMMs so activations cross HBM as few times as possible. Each kernel
 // names the chain of reference ops it replaces (zimage.cpp:90-136 run_block, built on
-// tensor.cpp's rms_norm / mul_rows_ / rms_norm_heads_ / rope_ / add_rows_scaled_).
+// tensor.cpp's rms_norm / mul_rows_ / add_rows_scaled_). The per-head QK norm and the
+// rotary embedding (rms_norm_heads_ / rope_) run in the QKV GEMM's epilogue (gemm_tc.cu).
 //
 //   k_rms_mod_bf16       h = bf16( rms_norm(x, gamma) * scale )   (GEMM A operand)
 //   k_post_norm_residual x += gate * rms_norm(a, gamma2)           (or x += rms_norm(a))
-//   k_qk_norm_rope_pack  per (token, head): q, k RMS-normalised, rotated (interleaved
-//                        RoPE) and packed with v to fp16 [S, heads, 128] for attention
 //   k_adaln_split        mod[4D] -> (1 + scale_msa, tanh gate_msa, 1 + scale_mlp, tanh gate_mlp)
 //   k_timestep_embed     the 256-d sinusoid of t * t_scale (zimage.cpp:151-157)
 //   k_layer_norm_mod     y = layer_norm(x, eps) * scale (final layer, zimage.cpp:221-223)
@@ -83,56 +82,6 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_residual(float* __res
     const float v = p[i] * rstd * (gamma ? gamma[i] : 1.0f);
     y[i] += g ? g[i] * v : v;
   }
-}
-
-// One warp per (token, head): q and k (columns h*128.. of the [S, 3*H*128] QKV output)
-// are RMS-normalised over the head (eps 1e-5, gammas norm_q / norm_k), rotated by the
-// interleaved RoPE tables [S, 128] and written as fp16 to [S, H, 128]; v is copied to
-// fp16. Reference: rms_norm_heads_ + rope_(interleaved) (zimage.cpp:117-120).
-__global__ void k_qk_norm_rope_pack(const float* __restrict__ qkv, int S, int H, const float* __restrict__ gq,
-                                    const float* __restrict__ gk, const float* __restrict__ cs,
-                                    const float* __restrict__ sn, float eps, __half* __restrict__ q16,
-                                    __half* __restrict__ k16, __half* __restrict__ v16) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= (int64_t)S * H) return;
-  const int s = (int)(w / H), h = (int)(w % H);
-  const int D = H * 128;
-  const float* row = qkv + (int64_t)s * 3 * D + h * 128;
-  const int c = lane * 4;  // this lane's 4 consecutive dims = 2 rotary pairs
-  const float4 cv = *reinterpret_cast<const float4*>(cs + (int64_t)s * 128 + c);
-  const float4 sv = *reinterpret_cast<const float4*>(sn + (int64_t)s * 128 + c);
-  const int64_t o = w * 128 + c;
-#pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    const float* src = row + which * D;
-    const float* gam = which == 0 ? gq : gk;
-    float4 v = *reinterpret_cast<const float4*>(src + c);
-    const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-    const float rstd = rsqrtf(ss / 128.0f + eps);
-    if (gam) {
-      const float4 gv = *reinterpret_cast<const float4*>(gam + c);
-      v.x = v.x * rstd * gv.x;
-      v.y = v.y * rstd * gv.y;
-      v.z = v.z * rstd * gv.z;
-      v.w = v.w * rstd * gv.w;
-    } else {
-      v.x *= rstd;
-      v.y *= rstd;
-      v.z *= rstd;
-      v.w *= rstd;
-    }
-    // interleaved pairs (c, c+1) and (c+2, c+3); the tables repeat each angle twice
-    const float r0 = v.x * cv.x - v.y * sv.x, r1 = v.y * cv.x + v.x * sv.x;
-    const float r2 = v.z * cv.z - v.w * sv.z, r3 = v.w * cv.z + v.z * sv.z;
-    __half2* dst = reinterpret_cast<__half2*>((which == 0 ? q16 : k16) + o);
-    dst[0] = __floats2half2_rn(r0, r1);
-    dst[1] = __floats2half2_rn(r2, r3);
-  }
-  const float4 vv = *reinterpret_cast<const float4*>(row + 2 * D + c);
-  __half2* dv = reinterpret_cast<__half2*>(v16 + o);
-  dv[0] = __floats2half2_rn(vv.x, vv.y);
-  dv[1] = __floats2half2_rn(vv.z, vv.w);
 }
 
 // mod [4D] = scale_msa | gate_msa | scale_mlp | gate_mlp -> 1 + s, tanh(g) in place
@@ -224,15 +173,6 @@ void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const
   if (rows <= 0) return;
   k_post_norm_residual<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, a, D, gamma, g, eps);
   check_launch("post_norm_residual");
-}
-void dit_qk_norm_rope_pack(const float* qkv, int S, int H, const float* gq, const float* gk, const float* cs,
-                           const float* sn, float eps, void* q16, void* k16, void* v16) {
-  const int64_t warps = (int64_t)S * H;
-  if (warps <= 0) return;
-  const int wpb = 8;
-  k_qk_norm_rope_pack<<<(unsigned)((warps + wpb - 1) / wpb), wpb * 32, 0, ctx().stream>>>(
-      qkv, S, H, gq, gk, cs, sn, eps, (__half*)q16, (__half*)k16, (__half*)v16);
-  check_launch("qk_norm_rope_pack");
 }
 void dit_adaln_split(float* mod, int D) {
   k_adaln_split<<<(unsigned)((4 * D + 255) / 256), 256, 0, ctx().stream>>>(mod, D);

@@ -168,8 +168,6 @@ void dit_rms_mod_bf16(const float* x, uint16_t* h, int64_t rows, int D, const fl
                       float eps);
 void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const float* gamma, const float* g,
                             float eps);
-void dit_qk_norm_rope_pack(const float* qkv, int S, int H, const float* gq, const float* gk, const float* cs,
-                           const float* sn, float eps, void* q16, void* k16, void* v16);
 void dit_adaln_split(float* mod, int D);
 void dit_timestep_embed(float* out, int F, float tt);
 void dit_layer_norm_mod(const float* x, float* y, int64_t rows, int D, const float* scale, float eps);
