@@ -15,8 +15,9 @@ Workload `gemm`: Y[4096,11520] = X[4096,3840] W[11520,3840]^
 one GEMM per GPU per step (replicas), TFLOP/s.
 
 Workload `dit_tp`: the same DiT at batch 1, 2048x2048 (16512 tokens),
-Megatron tensor parallelism over the N ranks with an NCCL all-reduce after each
-row-parallel projection; ms per step.
+Megatron tensor parallelism over the N ranks; ms per step. The row-parallel outputs are
+combined inside the kernels (--tp-mode 1, default: GEMM epilogue stores to the owner
+rank over NVLink, sequence-sharded post-norm) or by an NCCL all-reduce (--tp-mode 0).
 
 Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
 128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
@@ -405,7 +406,8 @@ def run_dit_tp(args, world, rank, local, pg, dev):
     """the 30-layer DiT at batch 1, 2048x2048 (256x256 latent: 16384
     image + 128 text tokens), Megatron tensor parallelism over the N ranks (column-parallel
     QKV by heads and w1/w3, row-parallel to_out and w2, NCCL all-reduce after each
-    row-parallel projection). Total work fixed: "scaling": "strong"."""
+    row-parallel projection, or with --tp-mode 1 the exchange fused into the kernels).
+    Total work fixed: "scaling": "strong"."""
     import torch
 
     import sdb200
@@ -422,7 +424,7 @@ def run_dit_tp(args, world, rank, local, pg, dev):
     torch.cuda.empty_cache()
     model = ZImageB200(shards, cfg)
     comm = Comm(rank, world, None)
-    model.set_tp(comm)
+    model.set_tp(comm, mode=args.tp_mode)
     g = torch.Generator(device=dev)
     g.manual_seed(2000)  # every rank holds the same image and text states
     x = torch.randn((1, cfg.in_channels, H, W), generator=g, device=dev)
@@ -466,7 +468,10 @@ def run_dit_tp(args, world, rank, local, pg, dev):
             "data": "synthetic (random-init Z-Image-shaped weights, N(0,1) latent and text states)",
             "config": {"workload": "cfg5: 30-layer Z-Image DiT @2048^2 (16512 tokens), batch 1, one denoising step",
                        "global_batch": 1, "seq_len": 16512, "parallelism": f"tensor-parallel x{world} "
-                       "(column QKV/w1/w3, row to_out/w2, NCCL all-reduce fp32)"},
+                       "(column QKV/w1/w3, row to_out/w2; " + (
+                           "partial rows scattered to their owner rank from the GEMM epilogue over NVLink, "
+                           "sequence-sharded post-norm broadcasting the next bf16 input)" if args.tp_mode == 1 else
+                           "NCCL all-reduce fp32)")},
             "step_tflops": fl["total"] / (ms_step * 1e-3) / 1e12,
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all GEMMs of one step, rank 0)", "achieved": gemm_tf,
@@ -474,8 +479,8 @@ def run_dit_tp(args, world, rank, local, pg, dev):
                          "frac": (gemm_tf / pk["sustained"]) if gemm_tf else None,
                          "peak_kind": f"{pk['kind']} bf16 sustained", "traffic": None,
                          "gemm_ms_per_step": prof["gemm_ms"], "attention_tflops": attn_tf,
-                         "attention_ms_per_step": prof["attn_ms"], "allreduce_ms_per_step": prof["allreduce_ms"],
-                         "allreduces_per_step": prof["allreduces"], "forward_ms_profiled": prof["forward_ms"]},
+                         "attention_ms_per_step": prof["attn_ms"], "comm_ms_per_step": prof["allreduce_ms"],
+                         "comm_calls_per_step": prof["allreduces"], "forward_ms_profiled": prof["forward_ms"]},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
                     "d2h_bytes_per_step": int(outh.numel() * 4)},
             "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": err}), flush=True)
@@ -630,6 +635,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-mode", type=int, default=1, choices=[0, 1],
+                    help="dit_tp: 1 = exchange fused into the GEMM epilogue and post-norm over NVLink, "
+                         "0 = NCCL all-reduce")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()

@@ -174,9 +174,16 @@ int sdb200_zimage_profile_read(void* model, double* out10);
 /* Extension (the reference has no multi-GPU mode): Megatron-style tensor parallelism.
  * The caller registers this rank's shards (to_q/to_k/to_v rows and to_out columns of its
  * heads, w1/w3 rows and w2 columns of its FFN slice, row-parallel biases on rank 0 only)
- * and attaches a communicator; the outputs of to_out and w2 are then summed over the
- * group (NCCL all-reduce on the model's stream) before each post-norm. */
+ * and attaches a communicator (NULL detaches; also releases the peer mappings). Every
+ * rank of the group must then call zimage_forward with the same shapes. */
 int sdb200_zimage_set_tp(void* model, void* comm);
+/* How the row-parallel outputs of to_out and w2 are combined (default 1):
+ *   1  fused: the GEMM epilogue stores each partial row into the owner rank's memory
+ *      over NVLink (CUDA IPC mappings), the owner sums them in its post-norm kernel on
+ *      its share of the rows and stores the next GEMM's bf16 input row on every rank;
+ *      NCCL only orders the steps (4-byte barrier) and gathers x at the end of a stage
+ *   0  NCCL all-reduce of the full fp32 partial outputs, post-norm on every rank */
+int sdb200_zimage_set_tp_mode(void* model, int mode);
 
 /* ---- tensor-parallel communicator (NCCL over NVLink / NVSwitch, loaded at run time) -- */
 /* Writes a 128-byte unique id (on one rank; share it with the others out of band). */

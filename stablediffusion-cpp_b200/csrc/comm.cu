@@ -7,12 +7,22 @@
 // NCCL is loaded at run time (dlopen "libnccl.so.2"): the library itself keeps no
 // link-time dependency on it, and in a process where PyTorch already loaded its NCCL
 // the same copy is reused. Only the NCCL C API is called (no torch types cross here).
+//
+// Symmetric buffers (SymBuf): every rank allocates the same size with cudaMalloc and
+// maps every peer's allocation through CUDA IPC (handles exchanged with one NCCL
+// all-gather), so kernels can store straight into a peer's memory over NVLink. The
+// fused tensor-parallel path uses them: the row-parallel GEMMs scatter their partial
+// tiles into the owner rank's slots from the epilogue, and the post-norm kernel
+// broadcasts the next GEMM's bf16 input rows. comm_barrier (a 4-byte all-reduce on the
+// stream) orders those kernels across ranks; kernels that store to peers end with a
+// system-scope fence.
 #include <dlfcn.h>
 #include <nccl.h>
 
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "internal.h"
 #include "sdb200.h"
@@ -26,6 +36,7 @@ struct NcclApi {
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -46,6 +57,7 @@ NcclApi& nccl() {
   g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(sym("ncclGetUniqueId"));
   g_nccl.CommInitRank = reinterpret_cast<decltype(g_nccl.CommInitRank)>(sym("ncclCommInitRank"));
   g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(sym("ncclAllReduce"));
+  g_nccl.AllGather = reinterpret_cast<decltype(g_nccl.AllGather)>(sym("ncclAllGather"));
   g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
   g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(sym("ncclCommAbort"));
   g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
@@ -62,6 +74,8 @@ void check_nccl(ncclResult_t r, const char* what) {
 struct Comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1, device = -1;
+  float* bar = nullptr;     // device word of comm_barrier
+  uint8_t* hbuf = nullptr;  // device staging of the IPC handle exchange (world x 64 bytes)
 };
 
 // Sum all-reduce of n fp32 values in place on the calling context's stream.
@@ -71,6 +85,59 @@ void comm_allreduce_sum(Comm* c, float* buf, size_t n) {
 }
 int comm_world(const Comm* c) { return c ? c->world : 1; }
 int comm_rank(const Comm* c) { return c ? c->rank : 0; }
+
+// Stream-ordered barrier: completes on every rank only after all ranks reached it, so
+// work after it sees what every rank's earlier kernels stored into its memory.
+void comm_barrier(Comm* c) {
+  if (!c || c->world <= 1) return;
+  check_nccl(nccl().AllReduce(c->bar, c->bar, 1, ncclFloat32, ncclSum, c->comm, ctx().stream), "ncclAllReduce(barrier)");
+}
+
+// recv[r * bytes ...] = rank r's send (in place when send == recv + rank * bytes).
+void comm_allgather(Comm* c, const void* send, void* recv, size_t bytes) {
+  if (!c || c->world <= 1 || bytes == 0) return;
+  check_nccl(nccl().AllGather(send, recv, bytes, ncclInt8, c->comm, ctx().stream), "ncclAllGather");
+}
+
+// Collective: every rank calls with the same size. Frees a previous allocation of b.
+void comm_sym_alloc(Comm* c, SymBuf& b, size_t bytes) {
+  comm_sym_free(c, b);
+  const int w = comm_world(c);
+  if (w > kMaxTpRanks) fail(kErrUnsupported, "symmetric buffers: at most 8 ranks");
+  check_cuda(cudaMalloc(&b.local, bytes), "cudaMalloc(symmetric)");
+  b.bytes = bytes;
+  b.peer[comm_rank(c)] = b.local;
+  if (w <= 1) return;
+  cudaIpcMemHandle_t mine;
+  check_cuda(cudaIpcGetMemHandle(&mine, b.local), "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  check_cuda(cudaMemcpyAsync(c->hbuf + (size_t)c->rank * 64, &mine, 64, cudaMemcpyHostToDevice, ctx().stream),
+             "symmetric: handle upload");
+  comm_allgather(c, c->hbuf + (size_t)c->rank * 64, c->hbuf, 64);
+  std::vector<cudaIpcMemHandle_t> all((size_t)w);
+  check_cuda(cudaMemcpyAsync(all.data(), c->hbuf, (size_t)w * 64, cudaMemcpyDeviceToHost, ctx().stream),
+             "symmetric: handle download");
+  check_cuda(cudaStreamSynchronize(ctx().stream), "symmetric: handle exchange");
+  for (int r = 0; r < w; ++r) {
+    if (r == c->rank) continue;
+    void* p = nullptr;
+    check_cuda(cudaIpcOpenMemHandle(&p, all[(size_t)r], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    b.peer[r] = p;
+  }
+}
+
+// Not collective. Callers free only between forwards: every store a peer makes into
+// this buffer happens before that peer enters the forward's last collective, which this
+// rank has completed once its stream is drained here.
+void comm_sym_free(Comm* c, SymBuf& b) {
+  (void)c;
+  if (!b.local) return;
+  cudaStreamSynchronize(ctx().stream);
+  for (int r = 0; r < kMaxTpRanks; ++r)
+    if (b.peer[r] && b.peer[r] != b.local) cudaIpcCloseMemHandle(b.peer[r]);
+  cudaFree(b.local);
+  b = SymBuf{};
+}
 
 }  // namespace sdb
 
@@ -103,7 +170,13 @@ void* sdb200_comm_create(const void* unique_id, int rank, int world) {
       std::memcpy(&id, unique_id, sizeof(id));
       try {
         sdb::check_nccl(sdb::nccl().CommInitRank(&c->comm, world, id, rank), "ncclCommInitRank");
+        sdb::check_cuda(cudaMalloc(&c->bar, 256), "comm: barrier word");
+        sdb::check_cuda(cudaMemset(c->bar, 0, 256), "comm: barrier word");
+        sdb::check_cuda(cudaMalloc(&c->hbuf, (size_t)world * 64), "comm: handle staging");
       } catch (...) {
+        if (c->comm) sdb::nccl().CommDestroy(c->comm);
+        cudaFree(c->bar);
+        cudaFree(c->hbuf);
         delete c;
         throw;
       }
@@ -135,6 +208,8 @@ void sdb200_comm_destroy(void* comm) {
     } catch (...) {
     }
   }
+  cudaFree(c->bar);
+  cudaFree(c->hbuf);
   delete c;
 }
 

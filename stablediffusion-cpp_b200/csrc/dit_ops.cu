@@ -84,6 +84,64 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_residual(float* __res
   }
 }
 
+// Destinations of a broadcast row: the same buffer on every rank of the group.
+struct BcastDst {
+  uint16_t* p[kMaxTpRanks];
+  int n;
+};
+
+// Tensor-parallel post-norm on this rank's rows, fused with the reduction of the
+// row-parallel partial outputs and with the next GEMM's input. Owned row lr (global row
+// row0 + lr):
+//   a   = sum over s of slots[(s * slot_rows + lr) * D + :]   (every rank's partial row,
+//         stored there by the GEMM's scatter epilogue; the bias came with rank 0's)
+//   x  += g * (a * rstd(a) * gamma2)                          (as k_post_norm_residual)
+//   h   = bf16(x * rstd(x) * gamma_n * scale_n) at row row0 + lr of every rank's h,
+//         when hd.n > 0                                         (as k_rms_mod_bf16)
+// The row lives in shared memory between the passes (D * 4 bytes).
+__global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast(
+    const float* __restrict__ slots, long long slot_rows, int world, long long row0, float* __restrict__ x, int D,
+    const float* __restrict__ gamma2, const float* __restrict__ g, const float* __restrict__ gamma_n,
+    const float* __restrict__ scale_n, BcastDst hd, float eps) {
+  extern __shared__ float rowbuf[];
+  __shared__ float red[32];
+  const long long lr = blockIdx.x, row = row0 + lr;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) {
+    float a = 0.0f;
+    for (int s = 0; s < world; ++s) a += slots[((long long)s * slot_rows + lr) * D + i];
+    rowbuf[i] = a;
+    ss += a * a;
+  }
+  const float rstd = rsqrtf(block_sum256(ss, red) / (float)D + eps);
+  float* y = x + row * D;
+  float ss2 = 0.0f;
+  for (int i = threadIdx.x; i < D; i += kRowThreads) {
+    const float v = rowbuf[i] * rstd * (gamma2 ? gamma2[i] : 1.0f);
+    const float xn = y[i] + (g ? g[i] * v : v);
+    y[i] = xn;
+    rowbuf[i] = xn;
+    ss2 += xn * xn;
+  }
+  if (hd.n == 0) return;
+  const float rstd2 = rsqrtf(block_sum256(ss2, red) / (float)D + eps);  // also orders the rowbuf writes
+  for (int i = threadIdx.x * 2; i < D; i += kRowThreads * 2) {
+    float a = rowbuf[i] * rstd2 * (gamma_n ? gamma_n[i] : 1.0f);
+    if (scale_n) a *= scale_n[i];
+    if (i + 1 < D) {
+      float b = rowbuf[i + 1] * rstd2 * (gamma_n ? gamma_n[i + 1] : 1.0f);
+      if (scale_n) b *= scale_n[i + 1];
+      const uint32_t w = pack_bf16x2(a, b);
+      for (int q = 0; q < hd.n; ++q) *reinterpret_cast<uint32_t*>(hd.p[q] + row * D + i) = w;
+    } else {
+      const uint16_t w = f32_to_bf16_rne(a);
+      for (int q = 0; q < hd.n; ++q) hd.p[q][row * D + i] = w;
+    }
+  }
+  // Stores into peers' memory are visible system-wide before this kernel completes.
+  __threadfence_system();
+}
+
 // mod [4D] = scale_msa | gate_msa | scale_mlp | gate_mlp -> 1 + s, tanh(g) in place
 // (zimage.cpp:97-112: affine_(1, 1) and tanh_).
 __global__ void k_adaln_split(float* __restrict__ mod, int D) {
@@ -173,6 +231,20 @@ void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const
   if (rows <= 0) return;
   k_post_norm_residual<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, a, D, gamma, g, eps);
   check_launch("post_norm_residual");
+}
+
+void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,
+                             int D, const float* gamma2, const float* g, const float* gamma_n, const float* scale_n,
+                             uint16_t* const* hdst, int nh, float eps) {
+  if (rows <= 0) return;
+  if ((size_t)D * 4 > 48 * 1024) fail(kErrUnsupported, "post_norm_mod_bcast: row of more than 12288 values");
+  if (world < 1 || world > kMaxTpRanks || nh < 0 || nh > kMaxTpRanks) fail(kErrInvalidArg, "post_norm_mod_bcast: ranks");
+  BcastDst hd{};
+  hd.n = nh;
+  for (int q = 0; q < nh; ++q) hd.p[q] = hdst[q];
+  k_post_norm_mod_bcast<<<(unsigned)rows, kRowThreads, (size_t)D * 4, ctx().stream>>>(
+      slots, slot_rows, world, row0, x, D, gamma2, g, gamma_n, scale_n, hd, eps);
+  check_launch("post_norm_mod_bcast");
 }
 void dit_adaln_split(float* mod, int D) {
   k_adaln_split<<<(unsigned)((4 * D + 255) / 256), 256, 0, ctx().stream>>>(mod, D);

@@ -48,7 +48,10 @@ struct GemmParams {
   int vec_ok;    // C base and ldc allow 16-byte stores
   int* err;
   QkvRope rope;  // Epi::kQkvRope
+  ScatterOut sc;  // Epi::kScatter
 };
+
+constexpr int kStgPitch = 36;  // floats per staged row: 16-byte aligned, spreads banks
 
 template <int BN>
 struct Cfg {
@@ -59,7 +62,8 @@ struct Cfg {
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr uint32_t TMEM_COLS =
       (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STG_BYTES = 4 * 32 * kStgPitch * 4;  // scatter staging, one 32x32 block per epilogue warp
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + STG_BYTES;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mb, int& nb) {
@@ -195,6 +199,41 @@ __device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol
   }
 }
 
+// Epi::kScatter for one 32-column chunk of the warp's 32 rows (row_base..+31): each lane
+// stages its row in shared memory, then the warp stores four full 128-byte row segments
+// per instruction, so stores to a peer cross NVLink as whole lines rather than 16-byte
+// pieces of 32 different rows.
+__device__ __forceinline__ void scatter_chunk(const GemmParams& p, float* stg, const uint32_t (&r)[32], int row_base,
+                                              int col0, int lane) {
+  float* mine = stg + lane * kStgPitch;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    float4 o = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                           __uint_as_float(r[j + 3]));
+    if (p.bias) {
+      if (col0 + j + 3 < p.N) {
+        o.x += __ldg(p.bias + col0 + j);
+        o.y += __ldg(p.bias + col0 + j + 1);
+        o.z += __ldg(p.bias + col0 + j + 2);
+        o.w += __ldg(p.bias + col0 + j + 3);
+      }
+    }
+    *reinterpret_cast<float4*>(mine + j) = o;
+  }
+  __syncwarp();
+  const int sub = lane >> 3, c4 = (lane & 7) * 4;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += 4) {
+    const int rr = r0 + sub, grow = row_base + rr;
+    if (grow < p.M && col0 + c4 < p.N) {
+      const int o = grow / p.sc.rs;
+      float* dst = p.sc.base[o] + ((long long)p.sc.rank * p.sc.slot_rows + (grow - o * p.sc.rs)) * p.ldc + col0 + c4;
+      *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(stg + rr * kStgPitch + c4);
+    }
+  }
+  __syncwarp();
+}
+
 // Stores 16 gated results (from 16 gate + 16 up columns) at output column ocol0.
 __device__ __forceinline__ void store_row16(const GemmParams& p, int row, int ocol0, const float (&y)[16]) {
   const int on = p.N / 2;
@@ -251,6 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;       // [1] MMA completion before TMEM is freed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // scatter staging
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -410,6 +450,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
         tmem_wait_ld();
         const int col0 = nb * BN + c * 32;
+        if (p.epi == (int)Epi::kScatter) {
+          if (col0 < p.N) scatter_chunk(p, stg + q * (32 * kStgPitch), r, mb * kBM + q * 32, col0, lane);
+          continue;
+        }
         if (!row_ok || col0 >= p.N) continue;
         float v[32];
 #pragma unroll
@@ -446,6 +490,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // Stores into peers' memory are visible system-wide before this kernel completes.
+    if (p.epi == (int)Epi::kScatter) __threadfence_system();
   }
 
   // Teardown: all roles are done; the MMA thread has seen its final commit.
@@ -563,6 +609,13 @@ void launch_gemm_tc(const GemmCall& g) {
       fail(kErrInvalidArg, "gemm_tc: QKV epilogue needs bf16 operands and N = 3 * Dq, Dq % 128 == 0");
     if (bn % 128 != 0) bn = choose_bn(g.M, g.N, c.num_sms, g.epi);
   }
+  if (g.epi == Epi::kScatter) {
+    if (!g.scatter || g.scatter->rs <= 0 || g.accumulate || g.out_bf16 || g.ldc % 4 != 0)
+      fail(kErrInvalidArg, "gemm_tc: scatter epilogue needs fp32 rows of 16-byte pitch and no accumulate");
+    for (int64_t o = 0; o * g.scatter->rs < g.M; ++o)
+      if (o >= 8 || !g.scatter->base[o] || (reinterpret_cast<uintptr_t>(g.scatter->base[o]) & 15))
+        fail(kErrInvalidArg, "gemm_tc: scatter epilogue: missing or misaligned owner slot");
+  }
   p.m_tiles = (int)((g.M + kBM - 1) / kBM);
   p.n_tiles = (int)((g.N + bn - 1) / bn);
   p.num_tiles = p.m_tiles * p.n_tiles;
@@ -578,6 +631,7 @@ void launch_gemm_tc(const GemmCall& g) {
   p.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * oesz) % 16 == 0);
   p.err = c.err_word;
   if (g.rope) p.rope = *g.rope;
+  if (g.scatter) p.sc = *g.scatter;
   if (g.tf32) {
     switch (bn) {
       case 256: launch_bn<256, true>(g, p, c.num_sms); break;
@@ -601,7 +655,8 @@ void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream
   p.M = (int)g.M;
   p.N = (int)g.N;
   p.K = (int)g.K;
-  if (g.epi == Epi::kQkvRope) fail(kErrInvalidArg, "gemm_tc: the QKV epilogue needs a device context");
+  if (g.epi == Epi::kQkvRope || g.epi == Epi::kScatter)
+    fail(kErrInvalidArg, "gemm_tc: the QKV and scatter epilogues need a device context");
   const int bn = g.bn ? g.bn : choose_bn(g.M, g.N, num_sms, g.epi);
   p.m_tiles = (int)((g.M + kBM - 1) / kBM);
   p.n_tiles = (int)((g.N + bn - 1) / bn);

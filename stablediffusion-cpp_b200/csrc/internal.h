@@ -73,6 +73,16 @@ enum class Epi : int {
   kSwiglu = 1,     // columns interleaved gate/up per 16: Y[m, n/2] = silu(g) * u
   kGeglu = 2,      // columns interleaved value/gate per 16: Y[m, n/2] = v * gelu_erf(g)
   kQkvRope = 3,    // fused-QKV output [rows, 3 Dq] -> fp16 q, k (RMS-normalised, rotated), v
+  kScatter = 4,    // fp32 C (+bias) rows stored into their owner rank's slot (ScatterOut)
+};
+// Operands of Epi::kScatter (tensor parallelism, row-parallel partial outputs). Row r
+// belongs to rank o = r / rs; it is stored at row (rank * slot_rows + r - o * rs) of
+// base[o], a buffer of rank o mapped into this process (local for o == rank).
+struct ScatterOut {
+  float* base[8];
+  long long slot_rows;
+  int rs;
+  int rank;
 };
 // Operands of Epi::kQkvRope. The GEMM output columns are q | k | v, Dq = heads * 128
 // each; row r is token r % S of its sequence. Per 128-column head of q and k: RMS norm
@@ -105,6 +115,7 @@ struct GemmCall {
   bool out_bf16;    // store C as bf16 (ldc in bf16 elements); no accumulate
   int bn;           // 0 = choose
   const QkvRope* rope = nullptr;  // Epi::kQkvRope only (C unused)
+  const ScatterOut* scatter = nullptr;  // Epi::kScatter only (C unused, ldc = row length)
 };
 void launch_gemm_tc(const GemmCall& g);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
@@ -148,6 +159,24 @@ void op_im2col(const float*, float*, int64_t, int64_t, int64_t, int64_t, int64_t
                int64_t, int64_t);
 void set_last_error(const std::string& s);
 
+// ---- tensor-parallel communicator (comm.cu) ----
+struct Comm;
+constexpr int kMaxTpRanks = 8;
+// A device buffer of the same size on every rank of a communicator, with every peer's
+// copy mapped into this process (peer[rank] == local).
+struct SymBuf {
+  void* local = nullptr;
+  void* peer[kMaxTpRanks] = {};
+  size_t bytes = 0;
+};
+void comm_allreduce_sum(Comm* c, float* buf, size_t n);
+int comm_world(const Comm* c);
+int comm_rank(const Comm* c);
+void comm_barrier(Comm* c);
+void comm_allgather(Comm* c, const void* send, void* recv, size_t bytes);
+void comm_sym_alloc(Comm* c, SymBuf& b, size_t bytes);
+void comm_sym_free(Comm* c, SymBuf& b);
+
 // Caching allocator (runtime.cu).
 void* pool_malloc(size_t bytes);
 void pool_free(void* p);
@@ -157,6 +186,8 @@ void gemm_nt_bf16_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t 
                        float* C, int64_t ldc, const float* bias, bool acc);
 void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                       float* C, int64_t ldc, const float* bias, bool acc);
+void gemm_bf16_scatter_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
+                            int64_t ldb, const float* bias, const ScatterOut& so);
 void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
                              int64_t ldb, const float* bias, const QkvRope& r);
 void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16,
@@ -168,6 +199,11 @@ void dit_rms_mod_bf16(const float* x, uint16_t* h, int64_t rows, int D, const fl
                       float eps);
 void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const float* gamma, const float* g,
                             float eps);
+// Tensor-parallel post-norm of rows [row0, row0 + rows): sums the world partial slots,
+// updates x, and (nh > 0) stores the next GEMM's bf16 input row into nh buffers.
+void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,
+                             int D, const float* gamma2, const float* g, const float* gamma_n, const float* scale_n,
+                             uint16_t* const* hdst, int nh, float eps);
 void dit_adaln_split(float* mod, int D);
 void dit_timestep_embed(float* out, int F, float tt);
 void dit_layer_norm_mod(const float* x, float* y, int64_t rows, int D, const float* scale, float eps);

@@ -49,7 +49,7 @@ void check_gemm_args(const char* op, int64_t M, int64_t N, int64_t K, const void
 // bf16 x bf16 GEMM with A either fp32 (packed here) or bf16.
 void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
                     int64_t ldb, void* C, int64_t ldc, bool c_bf16, const float* bias, bool acc, Epi epi,
-                    const QkvRope* rope = nullptr) {
+                    const QkvRope* rope = nullptr, const ScatterOut* scatter = nullptr) {
   const int64_t Kp = round_up(K, 8);  // 16-byte rows of bf16
   const bool a_direct = a_bf16 && aligned16(A) && (lda % 8 == 0);
   const bool b_direct = aligned16(B) && (ldb % 8 == 0);
@@ -92,6 +92,7 @@ void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
   g.out_bf16 = c_bf16;
   g.bn = 0;
   g.rope = rope;
+  g.scatter = scatter;
   launch_gemm_tc(g);
 }
 
@@ -187,6 +188,20 @@ void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, b
   require_ptr(B, op, "B");
   require(lda >= K && ldb >= K, op, "leading dimension < K");
   gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kQkvRope, &r);
+}
+
+// Row-parallel projection of tensor parallelism: X[M, K] times W[N, K]^T (+bias), every
+// output row stored into its owner rank's slot (Epi::kScatter) instead of C.
+void gemm_bf16_scatter_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
+                            int64_t ldb, const float* bias, const ScatterOut& so) {
+  const char* op = "gemm_bf16_scatter";
+  if (M <= 0 || N <= 0) return;
+  require(K > 0, op, "K == 0");
+  require_ptr(A, op, "A");
+  require_ptr(B, op, "B");
+  require(lda >= K && ldb >= K, op, "leading dimension < K");
+  require(N % 4 == 0, op, "N % 4 != 0 (16-byte rows)");
+  gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kScatter, nullptr, &so);
 }
 
 // conv2d as im2col + tf32 GEMM, writing NCHW directly (ldc = HW), as

@@ -39,10 +39,6 @@
 
 namespace sdb {
 
-struct Comm;
-void comm_allreduce_sum(Comm* c, float* buf, size_t n);
-int comm_world(const Comm* c);
-
 namespace {
 
 struct WRef {
@@ -137,7 +133,10 @@ class ZImage {
 
   ZImage(int h, int p, float eps, float theta, float ts, int a0, int a1, int a2)
       : heads(h), patch(p), norm_eps(eps), rope_theta(theta), t_scale(ts), axes{a0, a1, a2} {}
-  ~ZImage() { prof_clear(); }
+  ~ZImage() {
+    prof_clear();
+    release_tp();
+  }
 
   // ---- optional per-kernel timing (CUDA events on the stream) ------------------------
   // Category 0: tensor-core GEMMs, 1: attention, 2: whole forward, 3: tensor-parallel
@@ -354,6 +353,121 @@ class ZImage {
 
   // Tensor-parallel group (null or world 1: the whole model on this GPU).
   Comm* comm = nullptr;
+  // world > 1: 1 = row-parallel GEMMs scatter their partial rows to the owner rank from
+  // the epilogue and the post-norm runs sequence-sharded (run_stage_sp), 0 = NCCL
+  // all-reduce of the full partial outputs (run_block).
+  int tp_mode = 1;
+  SymBuf tp_slots, tp_h;  // per rank: world partial slots of its rows (fp32), the full bf16 GEMM input
+  DBuf mods;              // modulation vectors of every block of a stage [blocks, 4D]
+
+  void release_tp() {
+    comm_sym_free(comm, tp_slots);
+    comm_sym_free(comm, tp_h);
+  }
+  int64_t rows_alloc(int64_t R) const {
+    const int64_t w = comm_world(comm);
+    return (R + w - 1) / w * w;
+  }
+
+  void run_stage(const std::vector<Block>& blocks, float* x, int64_t B, int64_t S, const float* cs, const float* sn,
+                 bool modulated) {
+    if (blocks.empty()) return;
+    if (comm_world(comm) > 1 && tp_mode == 1) {
+      run_stage_sp(blocks, x, B, S, cs, sn, modulated);
+      return;
+    }
+    for (const Block& b : blocks) run_block(b, x, B, S, cs, sn, modulated);
+  }
+
+  // A stage of blocks under tensor parallelism with the exchange fused into the kernels.
+  // Rank rk owns rows [rk * Rs, rk * Rs + Rs) of the B*S rows. Per block:
+  //   QKV GEMM (column-parallel, this rank's heads) + attention on all rows, then
+  //   to_out GEMM whose epilogue stores each partial row into its owner's slot;
+  //   barrier; the owner sums the world slots of its rows, applies post-norm + gated
+  //   residual to its rows of x, and stores the FFN's bf16 input row on every rank;
+  //   barrier; w1/w3 SwiGLU and w2 the same way; the second post-norm stores the next
+  //   block's attention input. x is exact on owned rows only; the stage ends with an
+  //   all-gather of x. NCCL moves no activation data inside the stage.
+  void run_stage_sp(const std::vector<Block>& blocks, float* x, int64_t B, int64_t S, const float* cs, const float* sn,
+                    bool modulated) {
+    const int w = comm_world(comm), rk = comm_rank(comm);
+    const int64_t R = B * S, Rs = (R + w - 1) / w, row0 = (int64_t)rk * Rs;
+    const int64_t own = std::max<int64_t>(0, std::min<int64_t>(Rs, R - row0));
+    // Symmetric buffers; every rank runs the same shapes, so growth is collective.
+    const size_t slot_bytes = (size_t)(w * Rs * D) * 4, h_bytes = (size_t)(w * Rs * D) * 2;
+    if (tp_slots.bytes < slot_bytes) comm_sym_alloc(comm, tp_slots, slot_bytes);
+    if (tp_h.bytes < h_bytes) comm_sym_alloc(comm, tp_h, h_bytes);
+    const int64_t nb = (int64_t)blocks.size();
+    mods.ensure((size_t)(nb * 4 * D) * 4);
+    if (modulated)
+      for (int64_t i = 0; i < nb; ++i) {
+        float* mi = mods.as<float>() + i * 4 * D;
+        gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, blocks[i].adaln, tdim, mi, 4 * D, blocks[i].adaln_b,
+                          false);
+        dit_adaln_split(mi, (int)D);
+      }
+    auto part = [&](int64_t i, int k) -> const float* {  // 0 scale_msa, 1 gate_msa, 2 scale_mlp, 3 gate_mlp
+      return modulated ? mods.as<float>() + i * 4 * D + k * D : nullptr;
+    };
+    uint16_t* hloc = static_cast<uint16_t*>(tp_h.local);
+    uint16_t* hall[kMaxTpRanks] = {};
+    ScatterOut so{};
+    for (int q = 0; q < w; ++q) {
+      hall[q] = static_cast<uint16_t*>(tp_h.peer[q]);
+      so.base[q] = static_cast<float*>(tp_slots.peer[q]);
+    }
+    so.slot_rows = Rs;
+    so.rs = (int)Rs;
+    so.rank = rk;
+    const float* slots = static_cast<const float*>(tp_slots.local);
+    const double gf = 2.0 * (double)R;
+    // The stage's first input: x is complete on every rank here.
+    dit_rms_mod_bf16(x, hloc, R, (int)D, blocks[0].attn_norm1, part(0, 0), norm_eps);
+    for (int64_t i = 0; i < nb; ++i) {
+      const Block& b = blocks[i];
+      const int64_t Dq = b.Dq;
+      const int Hl = b.heads_local;
+      QkvRope rp{};
+      rp.S = (int)S;
+      rp.Dq = (int)Dq;
+      rp.gq = b.norm_q;
+      rp.gk = b.norm_k;
+      rp.cs = cs;
+      rp.sn = sn;
+      rp.eps = 1e-5f;
+      rp.q16 = q16.p;
+      rp.k16 = k16.p;
+      rp.v16 = v16.p;
+      timed(0, gf * 3 * Dq * D, [&] {
+        gemm_bf16_qkv_rope_impl(R, D, hloc, D, true, b.wqkv.as<uint16_t>(), D, b.has_bqkv ? b.bqkv.as<float>() : nullptr,
+                                rp);
+      });
+      timed(1, 4.0 * (double)B * S * S * Dq, [&] {
+        launch_attention_f16(q16.p, k16.p, v16.p, ao.p, Dq, S * Dq, true, B, S, S, Hl, Hl, head_dim, 128, false);
+      });
+      timed(0, gf * D * Dq, [&] { gemm_bf16_scatter_impl(R, D, Dq, ao.p, Dq, true, b.wout, Dq, b.bout, so); });
+      timed(3, 0.0, [&] { comm_barrier(comm); });
+      dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.attn_norm2, part(i, 1), b.ffn_norm1, part(i, 2),
+                              hall, w, norm_eps);
+      timed(3, 0.0, [&] { comm_barrier(comm); });
+      timed(0, gf * 2 * b.F * D, [&] {
+        gemm_bf16_epilogue_impl(R, 2 * b.F, D, hloc, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
+                                b.has_b13 ? b.b13.as<float>() : nullptr, 1);
+      });
+      timed(0, gf * b.F * D, [&] { gemm_bf16_scatter_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, b.b2, so); });
+      timed(3, 0.0, [&] { comm_barrier(comm); });
+      if (i + 1 < nb) {
+        dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), blocks[i + 1].attn_norm1,
+                                part(i + 1, 0), hall, w, norm_eps);
+        timed(3, 0.0, [&] { comm_barrier(comm); });
+      } else {
+        dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), nullptr, nullptr, hall, 0,
+                                norm_eps);
+      }
+    }
+    // Every rank gets every row of x (the buffer holds w * Rs rows).
+    timed(3, 0.0, [&] { comm_allgather(comm, x + row0 * D, x, (size_t)(Rs * D) * 4); });
+  }
 
   // One block on x [B*S, D] (B sequences of S rows), rotary tables [S, 128]. Under tensor
   // parallelism this rank holds heads_local heads and F of the FFN; the row-parallel
@@ -435,9 +549,10 @@ class ZImage {
     // activations
     const int64_t Rmax = B * S;
     tok.ensure((size_t)(B * n_img * p * p * C) * 4);
-    img.ensure((size_t)(B * n_img_pad * D) * 4);
-    cap.ensure((size_t)(B * n_cap_pad * D) * 4);
-    uni.ensure((size_t)(Rmax * D) * 4);
+    // x buffers hold a whole number of per-rank row blocks (tensor parallelism gathers them)
+    img.ensure((size_t)(rows_alloc(B * n_img_pad) * D) * 4);
+    cap.ensure((size_t)(rows_alloc(B * n_cap_pad) * D) * 4);
+    uni.ensure((size_t)(rows_alloc(Rmax) * D) * 4);
     h.ensure((size_t)(Rmax * D) * 2);
     q16.ensure((size_t)(Rmax * Dq) * 2);
     k16.ensure((size_t)(Rmax * Dq) * 2);
@@ -455,6 +570,13 @@ class ZImage {
     outtok.ensure((size_t)(B * n_img * p * p * C) * 4);
     fin.ensure((size_t)(B * n_img * D) * 4);
 
+    // Tensor parallelism with fused exchange: size the symmetric buffers once for the
+    // largest stage (collective; every rank runs the same shapes).
+    if (comm_world(comm) > 1 && tp_mode == 1) {
+      const int64_t w = comm_world(comm), Rs = (Rmax + w - 1) / w;
+      if (tp_slots.bytes < (size_t)(w * Rs * D) * 4) comm_sym_alloc(comm, tp_slots, (size_t)(w * Rs * D) * 4);
+      if (tp_h.bytes < (size_t)(w * Rs * D) * 2) comm_sym_alloc(comm, tp_h, (size_t)(w * Rs * D) * 2);
+    }
     // 1. timestep embedding -> adaln [1, tdim]
     dit_timestep_embed(temb.as<float>(), (int)tdim, t * t_scale);
     linear(temb.as<float>(), 1, tdim, t0, try_get("t_embedder.mlp.0.bias"), thid.as<float>());
@@ -477,10 +599,8 @@ class ZImage {
       dit_fill_rows(cap.as<float>() + n * n_cap_pad * D, f32("cap_pad_token"), L, n_cap_pad, (int)D);
     }
     // refiners
-    for (const Block& b : noise)
-      run_block(b, img.as<float>(), B, n_img_pad, tb[0].as<float>(), tb[1].as<float>(), true);
-    for (const Block& b : context)
-      run_block(b, cap.as<float>(), B, n_cap_pad, tb[2].as<float>(), tb[3].as<float>(), false);
+    run_stage(noise, img.as<float>(), B, n_img_pad, tb[0].as<float>(), tb[1].as<float>(), true);
+    run_stage(context, cap.as<float>(), B, n_cap_pad, tb[2].as<float>(), tb[3].as<float>(), false);
     // 4. unified [image, text] per sample, main stack
     for (int64_t n = 0; n < B; ++n) {
       check_cuda(cudaMemcpyAsync(uni.as<float>() + n * S * D, img.as<float>() + n * n_img_pad * D,
@@ -490,7 +610,7 @@ class ZImage {
                                  (size_t)(n_cap_pad * D) * 4, cudaMemcpyDeviceToDevice, st),
                  "zimage concat");
     }
-    for (const Block& b : layers) run_block(b, uni.as<float>(), B, S, tb[4].as<float>(), tb[5].as<float>(), true);
+    run_stage(layers, uni.as<float>(), B, S, tb[4].as<float>(), tb[5].as<float>(), true);
     // 5. final layer on the image tokens: LayerNorm * (1 + adaLN(silu(t_emb))), linear, unpatchify
     {
       check_cuda(cudaMemcpyAsync(temb.p, adaln.p, (size_t)tdim * 4, cudaMemcpyDeviceToDevice, st), "zimage final");
@@ -588,7 +708,16 @@ int sdb200_zimage_profile_read(void* m, double* out10) {
 int sdb200_zimage_set_tp(void* m, void* comm) {
   SDB_GUARD({
     if (!m) sdb::fail(sdb::kErrInvalidArg, "zimage_set_tp: null model");
-    static_cast<ZImage*>(m)->comm = static_cast<sdb::Comm*>(comm);
+    ZImage* z = static_cast<ZImage*>(m);
+    z->release_tp();
+    z->comm = static_cast<sdb::Comm*>(comm);
+  })
+}
+
+int sdb200_zimage_set_tp_mode(void* m, int mode) {
+  SDB_GUARD({
+    if (!m || mode < 0 || mode > 1) sdb::fail(sdb::kErrInvalidArg, "zimage_set_tp_mode: null model or mode not 0/1");
+    static_cast<ZImage*>(m)->tp_mode = mode;
   })
 }
 

@@ -80,6 +80,7 @@ _SIGS = {
     "sdb200_zimage_profile": ([_v, _i], _i),
     "sdb200_zimage_profile_read": ([_v, C.POINTER(C.c_double)], _i),
     "sdb200_zimage_set_tp": ([_v, _v], _i),
+    "sdb200_zimage_set_tp_mode": ([_v, _i], _i),
     "sdb200_comm_unique_id": ([_v], _i),
     "sdb200_comm_create": ([_v, _i, _i], _v),
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),

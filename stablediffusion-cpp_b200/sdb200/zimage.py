@@ -165,11 +165,14 @@ class ZImageB200:
                 "forwards", "allreduce_ms", "allreduces")
         return dict(zip(keys, list(out)))
 
-    def set_tp(self, comm):
+    def set_tp(self, comm, mode: int = 1):
         """Attaches a tensor-parallel communicator (sdb200.tp.Comm); the registered weights
-        must be this rank's shards (sdb200.tp.shard_weights)."""
+        must be this rank's shards (sdb200.tp.shard_weights). mode 1 combines the
+        row-parallel outputs inside the kernels over NVLink, mode 0 with an NCCL
+        all-reduce (sdb200_zimage_set_tp_mode)."""
         self._comm = comm
         check(lib().sdb200_zimage_set_tp(self._m, comm.handle if comm is not None else None))
+        check(lib().sdb200_zimage_set_tp_mode(self._m, int(mode)))
 
     def __del__(self):
         try:

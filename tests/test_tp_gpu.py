@@ -1,7 +1,9 @@
-"""GPU, 2 devices: the tensor-parallel Z-Image forward (NCCL all-reduce after the
-row-parallel projections) against the single-GPU forward (relative Frobenius <= 1e-3,
-only the order of the fp32 partial sums differs) and the CPU oracle (<= 1e-2), with all
-ranks holding identical outputs. Skipped where fewer than 2 GPUs are visible."""
+"""GPU, 2 devices: the tensor-parallel Z-Image forward against the single-GPU forward
+(relative Frobenius <= 1e-3, only the order of the fp32 partial sums differs) and the CPU
+oracle (<= 1e-2), with all ranks holding identical outputs. Both exchange modes: the
+row-parallel partial outputs scattered to their owner rank from the GEMM epilogue and
+reduced in the sequence-sharded post-norm (default), and an NCCL all-reduce. Skipped
+where fewer than 2 GPUs are visible."""
 import json
 import os
 import socket
@@ -35,3 +37,5 @@ def test_tensor_parallel_forward_two_gpus():
     assert r["max_rank_diff"] == 0.0
     assert r["rel_vs_single_gpu"] <= 1e-3, r
     assert r["rel_vs_oracle"] <= 1e-2, r
+    assert r["allreduce_rel_vs_single_gpu"] <= 1e-3, r
+    assert r["allreduce_rel_vs_oracle"] <= 1e-2, r

@@ -1,6 +1,7 @@
 """Worker run under torchrun by tests/test_tp_gpu.py: the Z-Image forward with tensor
-parallelism over the launched GPUs (heads 3 and FFN 528 split unevenly over 2 ranks)
-against the single-GPU forward and the CPU oracle. Rank 0 prints one JSON line."""
+parallelism over the launched GPUs (heads 3 and FFN 528 split unevenly over 2 ranks), in
+both exchange modes (fused into the kernels over NVLink, and NCCL all-reduce), against
+the single-GPU forward and the CPU oracle. Rank 0 prints one JSON line."""
 import datetime
 import json
 import os
@@ -32,24 +33,32 @@ def main():
     xt, capt = torch.from_numpy(x).to(dev), torch.from_numpy(cap).to(dev)
     comm = Comm(rank, world)
     m = ZImageB200(shard_weights(w, cfg.heads, 128, rank, world), cfg, bf16_names=bf)
-    m.set_tp(comm)
-    y = m.forward(xt, 0.6, capt)
-    torch.cuda.synchronize()
-    y0 = y.clone()
-    dist.broadcast(y0, src=0)
-    same = float((y - y0).abs().max().item())
-    t = torch.tensor([same], device=dev)
+    ys = {}
+    diffs = []
+    for mode in (1, 0):  # 1: exchange fused into the GEMM epilogue / post-norm, 0: NCCL all-reduce
+        m.set_tp(comm, mode=mode)
+        y = m.forward(xt, 0.6, capt)
+        y = m.forward(xt, 0.6, capt)  # second call reuses the peer mappings
+        torch.cuda.synchronize()
+        y0 = y.clone()
+        dist.broadcast(y0, src=0)
+        diffs.append(float((y - y0).abs().max().item()))
+        ys[mode] = y
+    t = torch.tensor([max(diffs)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    m.set_tp(None)
     if rank == 0:
         from oracle import Oracle
         from zimage_oracle import ZImageOracle
 
         single = ZImageB200(w, cfg, bf16_names=bf).forward(xt, 0.6, capt).cpu().numpy()
         want = ZImageOracle(Oracle(), w, bf, heads=cfg.heads).forward(x, 0.6, cap)
-        got = y.cpu().numpy()
         rel = lambda a, b: float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))  # noqa: E731
-        print(json.dumps({"world": world, "rel_vs_single_gpu": rel(got, single), "rel_vs_oracle": rel(got, want),
-                          "max_rank_diff": float(t.item()), "finite": bool(np.isfinite(got).all()),
+        fused, allred = ys[1].cpu().numpy(), ys[0].cpu().numpy()
+        print(json.dumps({"world": world, "rel_vs_single_gpu": rel(fused, single), "rel_vs_oracle": rel(fused, want),
+                          "allreduce_rel_vs_single_gpu": rel(allred, single),
+                          "allreduce_rel_vs_oracle": rel(allred, want), "max_rank_diff": float(t.item()),
+                          "finite": bool(np.isfinite(fused).all() and np.isfinite(allred).all()),
                           "err_word": sdb200.backend.device_error_word()}), flush=True)
     comm.close()
     dist.barrier()
