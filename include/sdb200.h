@@ -181,8 +181,11 @@ int sdb200_zimage_set_tp(void* model, void* comm);
  *   1  fused: the GEMM epilogue stores each partial row into the owner rank's memory
  *      over NVLink (CUDA IPC mappings), the owner sums them in its post-norm kernel on
  *      its share of the rows and stores the next GEMM's bf16 input row on every rank;
- *      NCCL only orders the steps (4-byte barrier) and gathers x at the end of a stage
- *   0  NCCL all-reduce of the full fp32 partial outputs, post-norm on every rank */
+ *      NCCL only orders the steps (4-byte barrier) and gathers x at the end of a stage.
+ *      On one GPU the same kernels run with local stores (post-norm and the next
+ *      RMSNorm + modulation in one pass)
+ *   0  per-block form: separate post-norm and RMSNorm kernels, and under tensor
+ *      parallelism an NCCL all-reduce of the full fp32 partial outputs */
 int sdb200_zimage_set_tp_mode(void* model, int mode);
 
 /* ---- tensor-parallel communicator (NCCL over NVLink / NVSwitch, loaded at run time) -- */

@@ -97,19 +97,24 @@ struct BcastDst {
 //         stored there by the GEMM's scatter epilogue; the bias came with rank 0's)
 //   x  += g * (a * rstd(a) * gamma2)                          (as k_post_norm_residual)
 //   h   = bf16(x * rstd(x) * gamma_n * scale_n) at row row0 + lr of every rank's h,
-//         when hd.n > 0                                         (as k_rms_mod_bf16)
+//         when hd.n > 0 (then hd.n == W)                        (as k_rms_mod_bf16)
 // The row lives in shared memory between the passes (D * 4 bytes).
+template <int W>
 __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast(
-    const float* __restrict__ slots, long long slot_rows, int world, long long row0, float* __restrict__ x, int D,
+    const float* __restrict__ slots, long long slot_rows, long long row0, float* __restrict__ x, int D,
     const float* __restrict__ gamma2, const float* __restrict__ g, const float* __restrict__ gamma_n,
     const float* __restrict__ scale_n, BcastDst hd, float eps) {
   extern __shared__ float rowbuf[];
   __shared__ float red[32];
   const long long lr = blockIdx.x, row = row0 + lr;
   float ss = 0.0f;
+  const float* src = slots + lr * D;
+  const long long sstride = slot_rows * D;
+#pragma unroll 4
   for (int i = threadIdx.x; i < D; i += kRowThreads) {
-    float a = 0.0f;
-    for (int s = 0; s < world; ++s) a += slots[((long long)s * slot_rows + lr) * D + i];
+    float a = src[i];
+#pragma unroll
+    for (int s = 1; s < W; ++s) a += src[s * sstride + i];
     rowbuf[i] = a;
     ss += a * a;
   }
@@ -132,10 +137,12 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast(
       float b = rowbuf[i + 1] * rstd2 * (gamma_n ? gamma_n[i + 1] : 1.0f);
       if (scale_n) b *= scale_n[i + 1];
       const uint32_t w = pack_bf16x2(a, b);
-      for (int q = 0; q < hd.n; ++q) *reinterpret_cast<uint32_t*>(hd.p[q] + row * D + i) = w;
+#pragma unroll
+      for (int q = 0; q < W; ++q) *reinterpret_cast<uint32_t*>(hd.p[q] + row * D + i) = w;
     } else {
       const uint16_t w = f32_to_bf16_rne(a);
-      for (int q = 0; q < hd.n; ++q) hd.p[q][row * D + i] = w;
+#pragma unroll
+      for (int q = 0; q < W; ++q) hd.p[q][row * D + i] = w;
     }
   }
   // Stores into peers' memory are visible system-wide before this kernel completes.
@@ -238,12 +245,23 @@ void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, i
                              uint16_t* const* hdst, int nh, float eps) {
   if (rows <= 0) return;
   if ((size_t)D * 4 > 48 * 1024) fail(kErrUnsupported, "post_norm_mod_bcast: row of more than 12288 values");
-  if (world < 1 || world > kMaxTpRanks || nh < 0 || nh > kMaxTpRanks) fail(kErrInvalidArg, "post_norm_mod_bcast: ranks");
+  if (world < 1 || world > kMaxTpRanks || (nh != 0 && nh != world))
+    fail(kErrInvalidArg, "post_norm_mod_bcast: ranks (the row goes to every rank or to none)");
   BcastDst hd{};
   hd.n = nh;
   for (int q = 0; q < nh; ++q) hd.p[q] = hdst[q];
-  k_post_norm_mod_bcast<<<(unsigned)rows, kRowThreads, (size_t)D * 4, ctx().stream>>>(
-      slots, slot_rows, world, row0, x, D, gamma2, g, gamma_n, scale_n, hd, eps);
+  const dim3 grid((unsigned)rows);
+  const size_t sm = (size_t)D * 4;
+  cudaStream_t st = ctx().stream;
+  switch (world) {
+#define SDB_PNMB(W)                                                                                          \
+  case W:                                                                                                    \
+    k_post_norm_mod_bcast<W><<<grid, kRowThreads, sm, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n, \
+                                                           scale_n, hd, eps);                                \
+    break;
+    SDB_PNMB(1) SDB_PNMB(2) SDB_PNMB(3) SDB_PNMB(4) SDB_PNMB(5) SDB_PNMB(6) SDB_PNMB(7) SDB_PNMB(8)
+#undef SDB_PNMB
+  }
   check_launch("post_norm_mod_bcast");
 }
 void dit_adaln_split(float* mod, int D) {

@@ -353,9 +353,10 @@ class ZImage {
 
   // Tensor-parallel group (null or world 1: the whole model on this GPU).
   Comm* comm = nullptr;
-  // world > 1: 1 = row-parallel GEMMs scatter their partial rows to the owner rank from
-  // the epilogue and the post-norm runs sequence-sharded (run_stage_sp), 0 = NCCL
-  // all-reduce of the full partial outputs (run_block).
+  // 1: stages run through run_stage_sp (on one GPU too, where the scatter is a local
+  // store and the post-norm also forms the next GEMM input); world > 1 then shares the
+  // row-parallel outputs through the owners' memory. 0: run_block per block, with an
+  // NCCL all-reduce of the full partial outputs under tensor parallelism.
   int tp_mode = 1;
   SymBuf tp_slots, tp_h;  // per rank: world partial slots of its rows (fp32), the full bf16 GEMM input
   DBuf mods;              // modulation vectors of every block of a stage [blocks, 4D]
@@ -372,7 +373,7 @@ class ZImage {
   void run_stage(const std::vector<Block>& blocks, float* x, int64_t B, int64_t S, const float* cs, const float* sn,
                  bool modulated) {
     if (blocks.empty()) return;
-    if (comm_world(comm) > 1 && tp_mode == 1) {
+    if (tp_mode == 1) {
       run_stage_sp(blocks, x, B, S, cs, sn, modulated);
       return;
     }
@@ -553,12 +554,12 @@ class ZImage {
     img.ensure((size_t)(rows_alloc(B * n_img_pad) * D) * 4);
     cap.ensure((size_t)(rows_alloc(B * n_cap_pad) * D) * 4);
     uni.ensure((size_t)(rows_alloc(Rmax) * D) * 4);
-    h.ensure((size_t)(Rmax * D) * 2);
+    if (tp_mode == 0) h.ensure((size_t)(Rmax * D) * 2);  // run_block's GEMM input
     q16.ensure((size_t)(Rmax * Dq) * 2);
     k16.ensure((size_t)(Rmax * Dq) * 2);
     v16.ensure((size_t)(Rmax * Dq) * 2);
     ao.ensure((size_t)(Rmax * Dq) * 2);
-    a.ensure((size_t)(Rmax * D) * 4);
+    if (tp_mode == 0) a.ensure((size_t)(Rmax * D) * 4);  // run_block's row-parallel outputs
     g.ensure((size_t)(Rmax * F) * 2);
     mod.ensure((size_t)(4 * D) * 4);
     const WRef& t0 = get("t_embedder.mlp.0.weight");
@@ -572,7 +573,7 @@ class ZImage {
 
     // Tensor parallelism with fused exchange: size the symmetric buffers once for the
     // largest stage (collective; every rank runs the same shapes).
-    if (comm_world(comm) > 1 && tp_mode == 1) {
+    if (tp_mode == 1) {
       const int64_t w = comm_world(comm), Rs = (Rmax + w - 1) / w;
       if (tp_slots.bytes < (size_t)(w * Rs * D) * 4) comm_sym_alloc(comm, tp_slots, (size_t)(w * Rs * D) * 4);
       if (tp_h.bytes < (size_t)(w * Rs * D) * 2) comm_sym_alloc(comm, tp_h, (size_t)(w * Rs * D) * 2);
