@@ -129,6 +129,10 @@ int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, in
 /* Tuning extension (no reference counterpart): forces the GEMM tile width N (64, 128,
  * 192 or 256) for later calls of this process; 0 restores the automatic choice. */
 int sdb200_set_gemm_tile(int bn);
+/* Tuning extension (no reference counterpart): bf16 GEMMs with 256-wide tiles run on
+ * pairs of SMs with 256 x 256 tiles (M = 256 MMAs over a cluster of two CTAs) when
+ * enable != 0 (default), on single SMs with 128 x 256 tiles otherwise. */
+int sdb200_set_gemm_pair(int enable);
 
 /* ---- attention ------------------------------------------------------------------- */
 /* backend_cuda.h:58-59 attention(): q [N, Sq, heads*d]; k, v [N, Skv, kv_heads*d];

@@ -269,6 +269,70 @@ __device__ __forceinline__ void store_row16(const GemmParams& p, int row, int oc
   }
 }
 
+// The epilogue of one accumulator tile for one warp: TMEM lanes of rows
+// row_base..row_base+31 (this thread: row_base + lane) at TMEM address tbase, tile column
+// block nb. stg is this warp's 32 x kStgPitch staging block (Epi::kScatter).
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, uint32_t tbase, int row_base, int nb,
+                                              int lane) {
+  const int row = row_base + lane;
+  const bool row_ok = row < p.M;
+  if constexpr (BN % 128 == 0) {
+    if (p.epi == (int)Epi::kQkvRope) {
+      // The launcher only pairs this epilogue with 128- or 256-column tiles, which
+      // hold whole heads; N = 3 Dq is a multiple of 128.
+#pragma unroll 1
+      for (int hg = 0; hg < BN / 128; ++hg) {
+        const int col0 = nb * BN + hg * 128;
+        if (col0 >= p.N) break;  // uniform over the warp
+        qkv_rope_head(p, tbase + (uint32_t)(hg * 128), row, row_ok, col0);
+      }
+      return;
+    }
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the masked stores
+    tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
+    tmem_wait_ld();
+    const int col0 = nb * BN + c * 32;
+    if (p.epi == (int)Epi::kScatter) {
+      if (col0 < p.N) scatter_chunk(p, stg, r, row_base, col0, lane);
+      continue;
+    }
+    if (!row_ok || col0 >= p.N) continue;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (p.bias) {
+      if (col0 + 32 <= p.N) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+      }
+    }
+    if (p.epi == (int)Epi::kStore) {
+      store_row32(p, row, col0, v);
+    } else {
+      // Interleaved pairs: columns [16j, 16j+16) are gates (SwiGLU) / values
+      // (GEGLU) and [16j+16, 16j+32) the matching up / gate columns.
+      float y[16];
+      if (p.epi == (int)Epi::kSwiglu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = silu_f(v[j]) * v[16 + j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = v[j] * gelu_erf_f(v[16 + j]);
+      }
+      store_row16(p, row, col0 / 2, y);
+    }
+  }
+}
+
 template <int BN, bool TF32>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
@@ -422,68 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
-      const int row = mb * kBM + q * 32 + lane;
-      const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr (BN % 128 == 0) {
-        if (p.epi == (int)Epi::kQkvRope) {
-          // The launcher only pairs this epilogue with 128- or 256-column tiles, which
-          // hold whole heads; N = 3 Dq is a multiple of 128.
-#pragma unroll 1
-          for (int hg = 0; hg < BN / 128; ++hg) {
-            const int col0 = nb * BN + hg * 128;
-            if (col0 >= p.N) break;  // uniform over the warp
-            qkv_rope_head(p, tbase + (uint32_t)(hg * 128), row, row_ok, col0);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1u;
-          continue;
-        }
-      }
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the masked stores
-        tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
-        tmem_wait_ld();
-        const int col0 = nb * BN + c * 32;
-        if (p.epi == (int)Epi::kScatter) {
-          if (col0 < p.N) scatter_chunk(p, stg + q * (32 * kStgPitch), r, mb * kBM + q * 32, col0, lane);
-          continue;
-        }
-        if (!row_ok || col0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (p.bias) {
-          if (col0 + 32 <= p.N) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
-          }
-        }
-        if (p.epi == (int)Epi::kStore) {
-          store_row32(p, row, col0, v);
-        } else {
-          // Interleaved pairs: columns [16j, 16j+16) are gates (SwiGLU) / values
-          // (GEGLU) and [16j+16, 16j+32) the matching up / gate columns.
-          float y[16];
-          if (p.epi == (int)Epi::kSwiglu) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) y[j] = silu_f(v[j]) * v[16 + j];
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) y[j] = v[j] * gelu_erf_f(v[16 + j]);
-          }
-          store_row16(p, row, col0 / 2, y);
-        }
-      }
+      epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -502,6 +506,247 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::TMEM_COLS);
   }
+}
+
+// ------------------------------------------------------------------------------------
+// Pair kernel: a cluster of two CTAs (on two SMs of one TPC) computes 256 x 256 tiles
+// with M = 256 tcgen05 MMAs (.cta_group::2) issued by the leader (cluster rank 0). Each
+// CTA stages its own 128 rows of A and its own 128 rows (half) of B, so the pair reads
+// each operand tile once per 256 x 256 outputs instead of twice per two 128 x 256 tiles
+// (a third less L2 -> shared memory traffic per FLOP), and each CTA's TMEM holds its 128
+// rows of the accumulator (double-buffered, 2 x 256 columns). Both CTAs' loads complete
+// on the leader's "full" barrier; the leader's MMA commits arrive on both CTAs' "empty" /
+// accumulator barriers (tcgen05.commit multicast); both CTAs' epilogue warps release the
+// leader's accumulator barrier. No load uses cluster multicast. bf16 operands only.
+struct PairCfg {
+  static constexpr int BN = 256;
+  static constexpr int A_BYTES = kBM * 128;       // 128 rows x 64 bf16
+  static constexpr int B_BYTES = (BN / 2) * 128;  // this CTA's half of the B tile
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int STG_BYTES = 4 * 32 * kStgPitch * 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + STG_BYTES;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_gemm_tc_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  using C_ = PairCfg;
+  constexpr int BN = C_::BN;
+  constexpr int STAGES = C_::STAGES;
+  constexpr int BK = 64;
+  constexpr int KSTEPS = 4;
+  constexpr uint32_t IDESC = make_idesc(1u /*bf16*/, 0, 0, 2 * kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * C_::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C_::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2] (the leader's are the ones used)
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* stg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = (int)(blockIdx.x >> 1), nclusters = (int)(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any signal crosses the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(&full[0], 0);  // the leader's barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_par = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+        int mb, nb;
+        tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);
+          const uint32_t fb = full0 + (uint32_t)(stage * 8);
+          tma_load_2d_pair(sA + stage * C_::A_BYTES, &tmA, fb, kb * BK, mb * 2 * kBM + (int)rank * kBM);
+          tma_load_2d_pair(sB + stage * C_::B_BYTES, &tmB, fb, kb * BK, nb * BN + (int)rank * (BN / 2));
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Aborted: wait (bounded) for loads still in flight (both CTAs' complete here).
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[s], (last_par >> s) & 1u))
+              if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(p.err, kErrWaitDrain);
+                break;
+              }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C_::A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * C_::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < KSTEPS; ++k)
+            umma_f16_ss_pair(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32), IDESC, (kb | k) != 0);
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit_pair(drain, 0x3);
+    }
+    if (lane == 0) {
+      // Both CTAs: every pair MMA has completed before TMEM and shared memory go away.
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kErrWaitDrain);
+          break;
+        }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int q = warp & 3;
+    const uint32_t acc_empty0 = mapa_shared(&acc_empty[0], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < p.num_tiles; t += nclusters) {
+      int mb, nb;
+      tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * 2 * kBM + (int)rank * kBM + q * 32, nb, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + (uint32_t)(acc * 8));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (p.epi == (int)Epi::kScatter) __threadfence_system();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs are done with TMEM, shared memory and each other's barriers
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+// Clusters of the pair kernel that fit on the device at once (cached per device).
+int pair_clusters(int dev) {
+  static int cached[64] = {};
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  check_cuda(cudaFuncSetAttribute(k_gemm_tc_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM),
+             "cudaFuncSetAttribute(gemm pair)");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::SMEM;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  check_cuda(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc_pair, &cfg), "cudaOccupancyMaxActiveClusters");
+  if (n <= 0) fail(kErrUnsupported, "gemm pair kernel: no cluster of 2 fits");
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  return n;
+}
+
+void launch_pair(const GemmCall& g, GemmParams p, int dev, cudaStream_t stream) {
+  using C_ = PairCfg;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.M};
+    const uint64_t strides[1] = {(uint64_t)g.lda * 2};
+    const uint32_t box[2] = {64, (uint32_t)kBM};
+    encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)g.K, (uint64_t)g.N};
+    const uint64_t strides[1] = {(uint64_t)g.ldb * 2};
+    const uint32_t box[2] = {64, (uint32_t)(C_::BN / 2)};
+    encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, g.B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  p.m_tiles = (int)((g.M + 2 * kBM - 1) / (2 * kBM));
+  p.n_tiles = (int)((g.N + C_::BN - 1) / C_::BN);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  const int clusters = std::min(pair_clusters(dev), p.num_tiles);
+  k_gemm_tc_pair<<<(unsigned)(2 * clusters), kThreads, C_::SMEM, stream>>>(ta, tb, p);
+  check_launch("gemm_tc_pair");
 }
 
 template <int BN, bool TF32>
@@ -597,6 +842,10 @@ int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
 static int g_forced_bn = 0;
 void set_gemm_tile(int bn) { g_forced_bn = bn; }
 
+// 256 x 256 tiles on CTA pairs (k_gemm_tc_pair) for bf16 GEMMs with 256-column tiles.
+static bool g_gemm_pair = true;
+void set_gemm_pair(bool on) { g_gemm_pair = on; }
+
 void launch_gemm_tc(const GemmCall& g) {
   DeviceContext& c = ctx();
   GemmParams p{};
@@ -632,6 +881,10 @@ void launch_gemm_tc(const GemmCall& g) {
   p.err = c.err_word;
   if (g.rope) p.rope = *g.rope;
   if (g.scatter) p.sc = *g.scatter;
+  if (!g.tf32 && bn == 256 && g_gemm_pair && g.M >= 2 * kBM) {
+    launch_pair(g, p, c.device, c.stream);
+    return;
+  }
   if (g.tf32) {
     switch (bn) {
       case 256: launch_bn<256, true>(g, p, c.num_sms); break;

@@ -120,6 +120,8 @@ struct GemmCall {
 void launch_gemm_tc(const GemmCall& g);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
 void set_gemm_tile(int bn);
+// Enables (default) or disables the CTA-pair kernel for bf16 GEMMs with 256-wide tiles.
+void set_gemm_pair(bool on);
 // bf16 tcgen05 GEMM on an explicit device / stream / error word; no device context.
 void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream, int* err_word, int dev);
 // Small-M (M <= 16) GEMM through a memory-bound SIMT kernel (weights streamed once).

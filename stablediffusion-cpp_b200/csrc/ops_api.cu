@@ -268,6 +268,10 @@ int sdb200_set_gemm_tile(int bn) {
   })
 }
 
+int sdb200_set_gemm_pair(int enable) {
+  SDB_GUARD(sdb::set_gemm_pair(enable != 0))
+}
+
 int sdb200_set_attention_path(int path) {
   SDB_GUARD({
     require(path == 0 || path == 1, "set_attention_path", "path must be 0 (tensor cores) or 1 (exact fp32)");
