@@ -881,9 +881,19 @@ void launch_gemm_tc(const GemmCall& g) {
   p.err = c.err_word;
   if (g.rope) p.rope = *g.rope;
   if (g.scatter) p.sc = *g.scatter;
-  if (!g.tf32 && bn == 256 && g_gemm_pair && g.M >= 2 * kBM) {
-    launch_pair(g, p, c.device, c.stream);
-    return;
+  if (!g.tf32 && g_gemm_pair && g.M >= 2 * kBM && (bn == 256 || (!g.bn && !g_forced_bn))) {
+    // Same wave-count cost model as choose_bn; a pair tile (256 x 256 over two SMs)
+    // costs one 128 x 256 tile-time at about 8% better efficiency (measured on the DiT
+    // shapes), so narrow single-SM tiles win only where they fill the last wave better.
+    const int64_t single_tiles = ((g.M + kBM - 1) / kBM) * ((g.N + bn - 1) / bn);
+    const double single_cost = (double)((single_tiles + c.num_sms - 1) / c.num_sms) * (bn + 48);
+    const int64_t pair_tiles = ((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + 255) / 256);
+    const int64_t clusters = pair_clusters(c.device);
+    const double pair_cost = (double)((pair_tiles + clusters - 1) / clusters) * (256 + 48) * 0.92;
+    if (pair_cost <= single_cost) {
+      launch_pair(g, p, c.device, c.stream);
+      return;
+    }
   }
   if (g.tf32) {
     switch (bn) {
