@@ -149,6 +149,87 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast(
   __threadfence_system();
 }
 
+// Register-resident form of k_post_norm_mod_bcast for D % 4 == 0 and D <= 4096: thread t
+// owns the float4 chunks t, t + 256, t + 512, t + 768 of the row, kept in registers across
+// the three passes; every global access is 16 bytes (8 for the bf16 rows). Same
+// arithmetic per element as the scalar form.
+constexpr int kPnChunks = 4;  // float4 chunks per thread: D <= 256 * 4 * 4
+template <int W>
+__global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
+    const float* __restrict__ slots, long long slot_rows, long long row0, float* __restrict__ x, int D,
+    const float* __restrict__ gamma2, const float* __restrict__ g, const float* __restrict__ gamma_n,
+    const float* __restrict__ scale_n, BcastDst hd, float eps) {
+  __shared__ float red[32];
+  const long long lr = blockIdx.x, row = row0 + lr;
+  const int D4 = D >> 2;
+  const float4* src = reinterpret_cast<const float4*>(slots + lr * D);
+  const long long sstride4 = (slot_rows * D) >> 2;
+  float4 a[kPnChunks];
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPnChunks; ++k) {
+    const int i4 = threadIdx.x + k * kRowThreads;
+    a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i4 < D4) {
+      a[k] = src[i4];
+#pragma unroll
+      for (int s = 1; s < W; ++s) {
+        const float4 t = src[s * sstride4 + i4];
+        a[k].x += t.x;
+        a[k].y += t.y;
+        a[k].z += t.z;
+        a[k].w += t.w;
+      }
+      ss += a[k].x * a[k].x + a[k].y * a[k].y + a[k].z * a[k].z + a[k].w * a[k].w;
+    }
+  }
+  const float rstd = rsqrtf(block_sum256(ss, red) / (float)D + eps);
+  float4* y = reinterpret_cast<float4*>(x + row * D);
+  const float4* g2 = reinterpret_cast<const float4*>(gamma2);
+  const float4* gt = reinterpret_cast<const float4*>(g);
+  float ss2 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kPnChunks; ++k) {
+    const int i4 = threadIdx.x + k * kRowThreads;
+    if (i4 < D4) {
+      const float4 gm = gamma2 ? g2[i4] : make_float4(1.f, 1.f, 1.f, 1.f);
+      float4 v = make_float4(a[k].x * rstd * gm.x, a[k].y * rstd * gm.y, a[k].z * rstd * gm.z, a[k].w * rstd * gm.w);
+      if (g) {
+        const float4 gg = gt[i4];
+        v = make_float4(gg.x * v.x, gg.y * v.y, gg.z * v.z, gg.w * v.w);
+      }
+      const float4 xo = y[i4];
+      const float4 xn = make_float4(xo.x + v.x, xo.y + v.y, xo.z + v.z, xo.w + v.w);
+      y[i4] = xn;
+      a[k] = xn;
+      ss2 += xn.x * xn.x + xn.y * xn.y + xn.z * xn.z + xn.w * xn.w;
+    }
+  }
+  if (hd.n == 0) return;
+  const float rstd2 = rsqrtf(block_sum256(ss2, red) / (float)D + eps);
+  const float4* gn = reinterpret_cast<const float4*>(gamma_n);
+  const float4* sc = reinterpret_cast<const float4*>(scale_n);
+#pragma unroll
+  for (int k = 0; k < kPnChunks; ++k) {
+    const int i4 = threadIdx.x + k * kRowThreads;
+    if (i4 < D4) {
+      const float4 gm = gamma_n ? gn[i4] : make_float4(1.f, 1.f, 1.f, 1.f);
+      float4 hv = make_float4(a[k].x * rstd2 * gm.x, a[k].y * rstd2 * gm.y, a[k].z * rstd2 * gm.z, a[k].w * rstd2 * gm.w);
+      if (scale_n) {
+        const float4 sv = sc[i4];
+        hv = make_float4(hv.x * sv.x, hv.y * sv.y, hv.z * sv.z, hv.w * sv.w);
+      }
+      uint2 w;
+      w.x = pack_bf16x2(hv.x, hv.y);
+      w.y = pack_bf16x2(hv.z, hv.w);
+#pragma unroll
+      for (int q = 0; q < W; ++q) *reinterpret_cast<uint2*>(hd.p[q] + row * D + 4 * i4) = w;
+    }
+  }
+  // Stores into peers' memory are visible system-wide before this kernel completes.
+  __threadfence_system();
+}
+
 // mod [4D] = scale_msa | gate_msa | scale_mlp | gate_mlp -> 1 + s, tanh(g) in place
 // (zimage.cpp:97-112: affine_(1, 1) and tanh_).
 __global__ void k_adaln_split(float* __restrict__ mod, int D) {
@@ -253,11 +334,22 @@ void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, i
   const dim3 grid((unsigned)rows);
   const size_t sm = (size_t)D * 4;
   cudaStream_t st = ctx().stream;
+  // The register-resident form needs 16-byte rows and vectors (all cudaMalloc'd / pool).
+  const bool v4 = D % 4 == 0 && D <= 4 * kRowThreads * kPnChunks &&
+                  ((reinterpret_cast<uintptr_t>(slots) | reinterpret_cast<uintptr_t>(x) |
+                    reinterpret_cast<uintptr_t>(gamma2) | reinterpret_cast<uintptr_t>(g) |
+                    reinterpret_cast<uintptr_t>(gamma_n) | reinterpret_cast<uintptr_t>(scale_n)) & 15) == 0;
+  bool hd_ok = true;
+  for (int q = 0; q < nh; ++q) hd_ok = hd_ok && (reinterpret_cast<uintptr_t>(hdst[q]) & 7) == 0;
   switch (world) {
-#define SDB_PNMB(W)                                                                                          \
-  case W:                                                                                                    \
-    k_post_norm_mod_bcast<W><<<grid, kRowThreads, sm, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n, \
-                                                           scale_n, hd, eps);                                \
+#define SDB_PNMB(W)                                                                                             \
+  case W:                                                                                                       \
+    if (v4 && hd_ok)                                                                                            \
+      k_post_norm_mod_bcast_v4<W><<<grid, kRowThreads, 0, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n, \
+                                                                scale_n, hd, eps);                              \
+    else                                                                                                        \
+      k_post_norm_mod_bcast<W><<<grid, kRowThreads, sm, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n,   \
+                                                             scale_n, hd, eps);                                 \
     break;
     SDB_PNMB(1) SDB_PNMB(2) SDB_PNMB(3) SDB_PNMB(4) SDB_PNMB(5) SDB_PNMB(6) SDB_PNMB(7) SDB_PNMB(8)
 #undef SDB_PNMB
