@@ -368,6 +368,9 @@ def run_dit(args, world, rank, local, pg, dev):
 
     e2e_step()
     e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev) / args.steps
+    # The whole sampler of BASELINE config 4 (8 flow-matching Euler steps, shift 3,
+    # scheduler.cpp:117-135) on the device, once, after the per-step timing.
+    sampler_ms = timed_loop(lambda: model.sample(x, cap, steps=8, shift=3.0), 1, stream, pg, dev)
     err = be.device_error_word()
     cpu = cpu_baseline("dit") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
@@ -395,6 +398,8 @@ def run_dit(args, world, rank, local, pg, dev):
                          "forward_ms_profiled": prof["forward_ms"]},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
                     "d2h_bytes_per_step": int(outh.numel() * 4)},
+            "sampler_8_steps": {"ms": sampler_ms, "ms_per_step": sampler_ms / 8,
+                                "note": "sdb200_zimage_sample: 8 flow-matching Euler steps, shift 3, on the device"},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "device_error_word": err,

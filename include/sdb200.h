@@ -191,6 +191,17 @@ int sdb200_zimage_set_tp(void* model, void* comm);
  *   0  per-block form: separate post-norm and RMSNorm kernels, and under tensor
  *      parallelism an NCCL all-reduce of the full fp32 partial outputs */
 int sdb200_zimage_set_tp_mode(void* model, int mode);
+/* Extension (pipeline.cpp:229-244 runs this loop on the host, one device round trip per
+ * step): the flow-matching Euler sampler of the Z-Image pipeline on the device. x
+ * [B, C, H, W] (device fp32) is the initial noise on entry and the denoised latent on
+ * return; per step i the model runs at time 1 - sigma_i on cap (and on cap_neg when
+ * cfg > 0, prediction = out + cfg (out - neg)), then x += (sigma_i - sigma_(i+1)) *
+ * prediction. steps >= 1; shift is the schedule's shift (3 for Z-Image). */
+int sdb200_zimage_sample(void* model, float* x, int64_t B, int64_t C, int64_t H, int64_t W, const float* cap,
+                         const float* cap_neg, int64_t L, int64_t capdim, float cfg, int steps, float shift);
+/* FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127) on the host: sigmas[0..steps],
+ * bit-identical to the reference's values. */
+int sdb200_flow_sigmas(int steps, float shift, float* sigmas);
 
 /* ---- tensor-parallel communicator (NCCL over NVLink / NVSwitch, loaded at run time) -- */
 /* Writes a 128-byte unique id (on one rank; share it with the others out of band). */

@@ -466,3 +466,30 @@ void orc_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, co
   }
   free(cols);
 }
+
+/* ---- flow-matching sampler (scheduler.cpp:117-135, pipeline.cpp:237-243) ------------ */
+/* sigma_i = shift s / (1 + (shift - 1) s), s from 1 down to 1/steps, sigma_steps = 0. The
+ * reference is compiled for x86-64-v3, where its compiler fuses the denominator into one
+ * multiply-add; fmaf reproduces that rounding. */
+void orc_flow_sigmas(int steps, float shift, float* sig) {
+  for (int i = 0; i < steps; ++i) {
+    const float s = steps == 1 ? 1.0f : 1.0f - (float)i * (1.0f - 1.0f / (float)steps) / (float)(steps - 1);
+    sig[i] = shift * s / fmaf(shift - 1.0f, s, 1.0f);
+  }
+  sig[steps] = 0.0f;
+}
+
+/* x += dt * (out + cfg (out - neg)) (neg NULL: x += dt * out). Built as the reference's
+ * loops compile for x86-64-v3: the guidance mix as a separate multiply and add, the
+ * Euler update as one fused multiply-add (pinned against the reference library). */
+__attribute__((optimize("fp-contract=off"))) void orc_flow_step(float* x, const float* out, const float* neg,
+                                                                float cfg, float dt, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    float o = out[i];
+    if (neg) {
+      const float t = cfg * (o - neg[i]);
+      o = o + t;
+    }
+    x[i] = fmaf(dt, o, x[i]);
+  }
+}

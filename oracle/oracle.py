@@ -83,6 +83,21 @@ class Oracle(_Base):
         self.num_threads = self.fn("num_threads", [], C.c_int)
 
     # bf16 rounding of the reference (tensor.cpp:114-121)
+    def flow_sigmas(self, steps: int, shift: float = 3.0) -> np.ndarray:
+        """FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127): sigma_0..sigma_steps."""
+        out = np.zeros(steps + 1, np.float32)
+        self.fn("flow_sigmas", [C.c_int, C.c_float, C.c_void_p])(steps, shift, _ptr(out))
+        return out
+
+    def flow_step(self, x, out, neg, cfg, dt):
+        """One sampler update (pipeline.cpp:237-243 + scheduler.cpp:129-134); returns new x."""
+        x = np.ascontiguousarray(x, np.float32).copy()
+        out = np.ascontiguousarray(out, np.float32)
+        negp = _ptr(np.ascontiguousarray(neg, np.float32)) if neg is not None else None
+        self.fn("flow_step", [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float, _i64])(
+            _ptr(x), _ptr(out), negp, cfg, dt, x.size)
+        return x
+
     def to_bf16(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)
         y = np.empty(x.shape, np.uint16)
@@ -353,6 +368,23 @@ class RefCPU(_Base):
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
         self._chk(self._conv(_ptr(x), N, Cin, H, W, _ptr(w), Cout, kh, kw, _ptr(b), stride, pad, _ptr(out)))
         return out
+
+    # ---- flow-matching sampler (the reference's FlowMatchScheduler) ---------------
+    def flow_sigmas(self, steps: int, shift: float = 3.0) -> np.ndarray:
+        sig = np.zeros(steps + 1, np.float32)
+        times = np.zeros(steps, np.float32)
+        self._chk(self.fn("flow_sigmas", [C.c_int, C.c_float, C.c_void_p, C.c_void_p], C.c_int)(
+            steps, shift, _ptr(sig), _ptr(times)))
+        return sig
+
+    def flow_step(self, x, out, neg, cfg, step, steps, shift=3.0):
+        """FlowMatchScheduler::step after the pipeline's guidance mix; returns new x."""
+        x = np.ascontiguousarray(x, np.float32).copy()
+        out = np.ascontiguousarray(out, np.float32)
+        negp = _ptr(np.ascontiguousarray(neg, np.float32)) if neg is not None else None
+        self._chk(self.fn("flow_step", [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, _i64, C.c_int, C.c_int,
+                                        C.c_float], C.c_int)(_ptr(x), _ptr(out), negp, cfg, x.size, step, steps, shift))
+        return x
 
     # ---- Z-Image transformer on random-init weights ------------------------------
     def zimage(self, weights: dict, bf16_names: set, heads=30, patch=2, norm_eps=1e-5, rope_theta=256.0,

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "safetensors.h"
+#include "scheduler.h"
 #include "tensor.h"
 #include "zimage.h"
 
@@ -185,6 +186,33 @@ int sdref_zimage_forward(void* m, const float* x, int64_t C, int64_t H, int64_t 
     Tensor tx = make(x, {1, C, H, W});
     Tensor tc = make(cap, {1, L, capdim});
     put(static_cast<ZImageTransformer*>(m)->forward(tx, t, tc), out);
+  });
+}
+
+// FlowMatchScheduler (scheduler.cpp:117-135): sigmas[0..steps] and the model-facing times
+// 1 - sigma_i of a `steps`-step schedule with the given shift.
+int sdref_flow_sigmas(int steps, float shift, float* sigmas, float* model_times) {
+  return guard([&] {
+    FlowMatchScheduler s(shift);
+    s.set_timesteps(steps);
+    for (int i = 0; i <= steps; ++i) sigmas[i] = s.sigma(i);
+    for (int i = 0; i < steps; ++i) model_times[i] = s.model_time(i);
+  });
+}
+
+// One sampler step as the Z-Image pipeline takes it (pipeline.cpp:237-243): with cfg > 0,
+// out += cfg * (out - neg) first, then FlowMatchScheduler::step(out, step, x).
+int sdref_flow_step(float* x, const float* out, const float* neg, float cfg, int64_t n, int step, int steps,
+                    float shift) {
+  return guard([&] {
+    FlowMatchScheduler s(shift);
+    s.set_timesteps(steps);
+    Tensor tx = make(x, {n});
+    Tensor to = make(out, {n});
+    if (neg && cfg > 0.0f)
+      for (int64_t j = 0; j < n; ++j) to.ptr()[j] += cfg * (to.ptr()[j] - neg[j]);
+    s.step(to, step, tx);
+    put(tx, x);
   });
 }
 

@@ -230,6 +230,20 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
   __threadfence_system();
 }
 
+// One flow-matching Euler step of the sampler on the device (pipeline.cpp:237-243,
+// scheduler.cpp:129-134): with classifier-free guidance (neg != null) the prediction is
+// out + cfg (out - neg), then x += dt * prediction, dt = sigma_i - sigma_(i+1). Rounded
+// as the reference's loops compile for x86-64-v3: the guidance mix as a separate
+// multiply and add (no contraction), the Euler update as one fused multiply-add.
+__global__ void k_flow_step(float* __restrict__ x, const float* __restrict__ out, const float* __restrict__ neg,
+                            float cfg, float dt, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float o = out[i];
+    if (neg) o = __fadd_rn(o, __fmul_rn(cfg, __fsub_rn(o, neg[i])));
+    x[i] = fmaf(dt, o, x[i]);
+  }
+}
+
 // mod [4D] = scale_msa | gate_msa | scale_mlp | gate_mlp -> 1 + s, tanh(g) in place
 // (zimage.cpp:97-112: affine_(1, 1) and tanh_).
 __global__ void k_adaln_split(float* __restrict__ mod, int D) {
@@ -319,6 +333,13 @@ void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const
   if (rows <= 0) return;
   k_post_norm_residual<<<(unsigned)rows, kRowThreads, 0, ctx().stream>>>(x, a, D, gamma, g, eps);
   check_launch("post_norm_residual");
+}
+
+void dit_flow_step(float* x, const float* out, const float* neg, float cfg, float dt, int64_t n) {
+  if (n <= 0) return;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, (int64_t)ctx().num_sms * 8);
+  k_flow_step<<<(unsigned)blocks, 256, 0, ctx().stream>>>(x, out, neg, cfg, dt, n);
+  check_launch("flow_step");
 }
 
 void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,

@@ -203,6 +203,8 @@ void dit_post_norm_residual(float* x, const float* a, int64_t rows, int D, const
                             float eps);
 // Tensor-parallel post-norm of rows [row0, row0 + rows): sums the world partial slots,
 // updates x, and (nh > 0) stores the next GEMM's bf16 input row into nh buffers.
+// x += dt * (out (+ cfg (out - neg) when neg != null)) over n values.
+void dit_flow_step(float* x, const float* out, const float* neg, float cfg, float dt, int64_t n);
 void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,
                              int D, const float* gamma2, const float* g, const float* gamma_n, const float* scale_n,
                              uint16_t* const* hdst, int nh, float eps);

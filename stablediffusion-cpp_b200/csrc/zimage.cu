@@ -121,6 +121,19 @@ void linear(const float* x, int64_t rows, int64_t in, const WRef& W, const WRef*
 
 }  // namespace
 
+// Flow-matching schedule of FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127):
+// sigma_i = shift s / (1 + (shift - 1) s), s running linearly from 1 to 1/steps, and
+// sigma_steps = 0. The denominator is one fused multiply-add: the reference is built
+// for x86-64-v3 and its compiler contracts exactly that term, so this reproduces the
+// reference's values bit for bit.
+void flow_sigmas(int steps, float shift, float* sig) {
+  for (int i = 0; i < steps; ++i) {
+    const float s = steps == 1 ? 1.0f : 1.0f - (float)i * (1.0f - 1.0f / (float)steps) / (float)(steps - 1);
+    sig[i] = shift * s / std::fma(shift - 1.0f, s, 1.0f);
+  }
+  sig[steps] = 0.0f;
+}
+
 class ZImage {
  public:
   int heads, patch;
@@ -526,6 +539,31 @@ class ZImage {
 
   static int64_t pad_to(int64_t n) { return (n + 31) / 32 * 32; }
 
+  // The sampler of the Z-Image pipeline (pipeline.cpp:229-244) with every step on the
+  // device: steps flow-matching Euler steps from the latent x (in place) under the
+  // text states cap (and cap_neg with guidance cfg > 0). Model time of step i is
+  // 1 - sigma_i; the update is x += (sigma_i - sigma_(i+1)) * prediction.
+  void sample(float* x, int64_t B, int64_t C, int64_t H, int64_t W, const float* cap, const float* cap_neg, int64_t L,
+              int64_t capdim, float cfg, int steps, float shift) {
+    if (!finalized) fail(kErrInvalidArg, "zimage: finalize() not called");
+    if (steps < 1) fail(kErrInvalidArg, "zimage_sample: steps must be >= 1");
+    const bool use_cfg = cfg > 0.0f;
+    if (use_cfg && !cap_neg) fail(kErrInvalidArg, "zimage_sample: cfg > 0 needs the negative text states");
+    std::vector<float> sig((size_t)steps + 1);
+    flow_sigmas(steps, shift, sig.data());
+    const int64_t n = B * C * H * W;
+    pred.ensure((size_t)n * 4);
+    if (use_cfg) pred_neg.ensure((size_t)n * 4);
+    for (int i = 0; i < steps; ++i) {
+      const float t = 1.0f - sig[(size_t)i];
+      forward(x, B, C, H, W, t, cap, L, capdim, pred.as<float>());
+      if (use_cfg) forward(x, B, C, H, W, t, cap_neg, L, capdim, pred_neg.as<float>());
+      dit_flow_step(x, pred.as<float>(), use_cfg ? pred_neg.as<float>() : nullptr, cfg,
+                    sig[(size_t)i] - sig[(size_t)i + 1], n);
+    }
+  }
+  DBuf pred, pred_neg;
+
   // x [B, C, H, W], cap [B, L, capdim] -> out [B, C, H, W] (zimage.cpp:138-228).
   void forward(const float* x_in, int64_t B, int64_t C, int64_t H, int64_t W, float t, const float* cap_in, int64_t L,
                int64_t capdim, float* out) {
@@ -712,6 +750,21 @@ int sdb200_zimage_set_tp(void* m, void* comm) {
     ZImage* z = static_cast<ZImage*>(m);
     z->release_tp();
     z->comm = static_cast<sdb::Comm*>(comm);
+  })
+}
+
+int sdb200_zimage_sample(void* m, float* x, int64_t B, int64_t C, int64_t H, int64_t W, const float* cap,
+                         const float* cap_neg, int64_t L, int64_t capdim, float cfg, int steps, float shift) {
+  SDB_GUARD({
+    if (!m || !x || !cap) sdb::fail(sdb::kErrInvalidArg, "zimage_sample: null pointer");
+    static_cast<ZImage*>(m)->sample(x, B, C, H, W, cap, cap_neg, L, capdim, cfg, steps, shift);
+  })
+}
+
+int sdb200_flow_sigmas(int steps, float shift, float* sigmas) {
+  SDB_GUARD({
+    if (steps < 1 || !sigmas) sdb::fail(sdb::kErrInvalidArg, "flow_sigmas: steps must be >= 1 and sigmas non-null");
+    sdb::flow_sigmas(steps, shift, sigmas);
   })
 }
 

@@ -82,6 +82,8 @@ _SIGS = {
     "sdb200_zimage_profile_read": ([_v, C.POINTER(C.c_double)], _i),
     "sdb200_zimage_set_tp": ([_v, _v], _i),
     "sdb200_zimage_set_tp_mode": ([_v, _i], _i),
+    "sdb200_zimage_sample": ([_v, _v, _i64, _i64, _i64, _i64, _v, _v, _i64, _i64, _f, _i, _f], _i),
+    "sdb200_flow_sigmas": ([_i, _f, _v], _i),
     "sdb200_comm_unique_id": ([_v], _i),
     "sdb200_comm_create": ([_v, _i, _i], _v),
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
@@ -139,3 +141,12 @@ def available() -> bool:
 
 
 from . import backend  # noqa: E402,F401  (torch-facing wrappers)
+
+
+def flow_sigmas(steps: int, shift: float = 3.0):
+    """The flow-matching schedule sigma_0..sigma_steps (scheduler.cpp:117-127), host-side."""
+    import numpy as np
+
+    out = np.zeros(steps + 1, dtype=np.float32)
+    check(lib().sdb200_flow_sigmas(int(steps), float(shift), out.ctypes.data_as(C.c_void_p)))
+    return out

@@ -154,6 +154,17 @@ class ZImageB200:
                                           cap.shape[2], out.data_ptr()))
         return out
 
+    def sample(self, x, cap, steps: int = 8, shift: float = 3.0, cap_neg=None, cfg: float = 0.0):
+        """The pipeline's flow-matching Euler sampler (pipeline.cpp:229-244) with every step
+        on the device: returns the denoised latent for the noise x [B, C, H, W] and the
+        text states cap (cap_neg and cfg > 0 add classifier-free guidance)."""
+        B, Cc, H, W = x.shape
+        y = x.clone()
+        check(lib().sdb200_zimage_sample(self._m, y.data_ptr(), B, Cc, H, W, cap.data_ptr(),
+                                         cap_neg.data_ptr() if cap_neg is not None else None, cap.shape[1],
+                                         cap.shape[2], float(cfg), int(steps), float(shift)))
+        return y
+
     def profile(self, enable: bool = True):
         """Times later forwards' GEMM and attention kernels with CUDA events."""
         check(lib().sdb200_zimage_profile(self._m, int(enable)))

@@ -8,7 +8,8 @@ bias / accumulate, causal and grouped-query attention, both RoPE conventions) pl
 sample of BASELINE config 1 (the fused-QKV bf16 GEMM, seed 0).
 
 Run in a container that has the reference tree:  python tests/golden/make_golden.py
-The fixtures it writes are committed; the tests never need the reference at run time.
+(`python tests/golden/make_golden.py flow` writes only the sampler fixture). The fixtures
+it writes are committed; the tests never need the reference at run time.
 """
 import os
 import subprocess
@@ -143,8 +144,32 @@ def main():
         cap = zr.standard_normal((1, L, cfg.cap_dim)).astype(np.float32)
         model = ref.zimage(w, bf, heads=cfg.heads)
         np.savez(os.path.join(HERE, f"{name}.npz"), x=x, cap=cap, t=np.float32(t), out=model(x, t, cap))
+    flow(ref)
     print("golden vectors written to", HERE)
 
 
+# Steps and shifts of the flow-matching schedule fixture (scheduler.cpp:117-127).
+FLOW_STEPS = tuple(range(1, 41))
+FLOW_SHIFTS = (0.5, 1.0, 2.0, 3.0, 6.0)
+
+
+def flow(ref):
+    """The reference's FlowMatchScheduler sigmas for every (steps, shift) pair, and one
+    guided sampler update (pipeline.cpp:237-243) on seeded data."""
+    sig = np.zeros((len(FLOW_STEPS), len(FLOW_SHIFTS), max(FLOW_STEPS) + 1), np.float32)
+    for i, steps in enumerate(FLOW_STEPS):
+        for j, shift in enumerate(FLOW_SHIFTS):
+            sig[i, j, :steps + 1] = ref.flow_sigmas(steps, shift)
+    rng = np.random.default_rng(77)
+    x, o, neg = rn(rng, 4096), rn(rng, 4096), rn(rng, 4096)
+    x_plain = ref.flow_step(x, o, None, 0.0, 2, 8, 3.0)
+    x_cfg = ref.flow_step(x, o, neg, 2.5, 5, 8, 3.0)
+    np.savez(os.path.join(HERE, "flow_sampler.npz"), sig=sig, steps=np.array(FLOW_STEPS), shifts=np.array(FLOW_SHIFTS),
+             x=x, out=o, neg=neg, x_plain=x_plain, x_cfg=x_cfg)
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["flow"]:  # only the sampler fixture
+        flow(RefCPU())
+    else:
+        main()

@@ -98,3 +98,39 @@ def test_zimage_cfg3_block_1024(sdb, ref):
     got = _np(m.forward(_t(x), 0.5, _t(cap)))
     want = ref.zimage(w, bf, heads=30)(x, 0.5, cap)
     assert rel_fro(got, want) <= TOL_LATENT
+
+
+@pytest.mark.parametrize("cfg_scale", [0.0, 2.0])
+def test_zimage_sampler_on_device(sdb, orc, ref, cfg_scale):
+    """sdb200_zimage_sample (the pipeline's flow-matching Euler loop run on the device)
+    against the same loop on the host over the device forward (identical up to the
+    update's rounding), and against the reference's CPU forward + FlowMatchScheduler per
+    image at the DiT latent gate."""
+    from sdb200.zimage import ZConfig
+
+    cfg = ZConfig(dim=256, heads=2, ffn=512, t_dim=256, t_hidden=512, cap_dim=128, layers=2, noise_refiners=1,
+                  context_refiners=1)
+    w, bf, m = _model(cfg, 0)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, 16, 16, 16)).astype(np.float32)
+    cap = rng.standard_normal((2, 20, 128)).astype(np.float32)
+    neg = rng.standard_normal((2, 20, 128)).astype(np.float32)
+    steps, shift = 3, 3.0
+    got = _np(m.sample(_t(x), _t(cap), steps=steps, shift=shift, cap_neg=_t(neg) if cfg_scale else None,
+                       cfg=cfg_scale))
+    assert np.isfinite(got).all()
+    sig = orc.flow_sigmas(steps, shift)
+    y = x.copy()
+    for i in range(steps):
+        o = _np(m.forward(_t(y), 1.0 - sig[i], _t(cap)))
+        n = _np(m.forward(_t(y), 1.0 - sig[i], _t(neg))) if cfg_scale else None
+        y = orc.flow_step(y, o, n, cfg_scale, sig[i] - sig[i + 1])
+    assert rel_fro(got, y) <= 1e-5
+    model = ref.zimage(w, bf, heads=cfg.heads)
+    for b in range(2):
+        yr = x[b:b + 1].copy()
+        for i in range(steps):
+            o = model(yr, 1.0 - sig[i], cap[b:b + 1])
+            n = model(yr, 1.0 - sig[i], neg[b:b + 1]) if cfg_scale else None
+            yr = ref.flow_step(yr, o, n, cfg_scale, i, steps, shift)
+        assert rel_fro(got[b:b + 1], yr) <= TOL_LATENT
