@@ -199,6 +199,21 @@ int sdb200_zimage_set_tp_mode(void* model, int mode);
  * prediction. steps >= 1; shift is the schedule's shift (3 for Z-Image). */
 int sdb200_zimage_sample(void* model, float* x, int64_t B, int64_t C, int64_t H, int64_t W, const float* cap,
                          const float* cap_neg, int64_t L, int64_t capdim, float cfg, int steps, float shift);
+/* Extension (the reference loads the whole checkpoint on every process and has no
+ * tensor parallelism): registers the weights of the checkpoint <dir>/<base> (found as
+ * Weights::load_model finds it: <base>.safetensors, the shards of
+ * <base>.safetensors.index.json, or <base>.fp16.safetensors) into device memory the
+ * model owns, read as the reference reads them (safetensors.cpp:80-168; tensors of at
+ * least bf16_min_numel elements kept as BF16, 1 << 20 when <= 0, smaller ones as F32).
+ * With world > 1 only this rank's tensor-parallel shard of every block tensor is read
+ * and uploaded (the layout sdb200_zimage_set_tp expects). Call before
+ * sdb200_zimage_finalize. */
+int sdb200_zimage_load(void* model, const char* dir, const char* base, int rank, int world, int64_t bf16_min_numel);
+/* Host only: one tensor of a .safetensors file converted as above into dst (BF16 bit
+ * patterns when *is_bf16, else F32); shape[0..*ndim) receives its shape (at most 8
+ * dims). dst may be NULL to query the shape and dtype. */
+int sdb200_safetensors_read(const char* path, const char* name, int keep_bf16, int64_t bf16_min_numel, void* dst,
+                            int64_t dst_bytes, int64_t* shape, int* ndim, int* is_bf16);
 /* FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127) on the host: sigmas[0..steps],
  * bit-identical to the reference's values. */
 int sdb200_flow_sigmas(int steps, float shift, float* sigmas);

@@ -386,6 +386,32 @@ class RefCPU(_Base):
                                         C.c_float], C.c_int)(_ptr(x), _ptr(out), negp, cfg, x.size, step, steps, shift))
         return x
 
+    # ---- checkpoints (the reference's safetensors reader) --------------------------
+    def safetensors_tensor(self, path, name, keep_bf16, min_numel, numel):
+        """Tensor `name` of `path` as Weights::load_safetensors stores it: (uint16 BF16 bits
+        or float32 array of numel values, is_bf16), or None if the reference skipped it."""
+        o32 = np.zeros(numel, np.float32)
+        o16 = np.zeros(numel, np.uint16)
+        rc = self.fn("safetensors_tensor", [C.c_char_p, C.c_char_p, C.c_int, _i64, C.c_void_p, C.c_void_p], C.c_int)(
+            path.encode(), name.encode(), int(keep_bf16), int(min_numel), _ptr(o32), _ptr(o16))
+        if rc == -1:
+            raise RuntimeError(self.last_error().decode())
+        if rc == -2:
+            return None
+        return (o16, True) if rc == 1 else (o32, False)
+
+    def zimage_load(self, dir_, base, heads=30, patch=2, norm_eps=1e-5, rope_theta=256.0, t_scale=1000.0,
+                    axes=(32, 48, 48)):
+        """The reference ZImageTransformer over a checkpoint directory, loaded as the
+        pipeline loads it; returns a callable like zimage()."""
+        wout = C.c_void_p()
+        load = self.fn("zimage_load", [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_float, C.c_float, C.c_float,
+                                       C.c_int, C.c_int, C.c_int, C.c_void_p], C.c_void_p)
+        m = load(dir_.encode(), base.encode(), heads, patch, norm_eps, rope_theta, t_scale, *axes, C.byref(wout))
+        if not m:
+            raise RuntimeError(self.last_error().decode())
+        return self._wrap_model(m, wout.value)
+
     # ---- Z-Image transformer on random-init weights ------------------------------
     def zimage(self, weights: dict, bf16_names: set, heads=30, patch=2, norm_eps=1e-5, rope_theta=256.0,
                t_scale=1000.0, axes=(32, 48, 48)):
@@ -402,6 +428,9 @@ class RefCPU(_Base):
         if not m:
             self.w_free(w)
             raise RuntimeError(self.last_error().decode())
+        return self._wrap_model(m, w)
+
+    def _wrap_model(self, m, w):
         ref = self
 
         class _Model:

@@ -189,6 +189,56 @@ int sdref_zimage_forward(void* m, const float* x, int64_t C, int64_t H, int64_t 
   });
 }
 
+// Weights::load_safetensors (safetensors.cpp:80-168) on one file; copies tensor `name`
+// out as the reference stores it: BF16 bit patterns into out16 when it kept BF16, else
+// F32 into out32. Returns 1 if BF16, 0 if F32, -1 on error (message in last_error), -2
+// if the reference did not read that tensor.
+int sdref_safetensors_tensor(const char* path, const char* name, int keep_bf16, int64_t min_numel, float* out32,
+                             uint16_t* out16) {
+  int res = -1;
+  guard([&] {
+    Weights w;
+    w.load_safetensors(path, keep_bf16 != 0, min_numel);
+    const Tensor* t = w.try_get(name);
+    if (!t) {
+      res = -2;
+      return;
+    }
+    if (t->is_bf16()) {
+      std::memcpy(out16, t->data16.data(), t->data16.size() * 2);
+      res = 1;
+    } else {
+      std::memcpy(out32, t->data.data(), t->data.size() * 4);
+      res = 0;
+    }
+  });
+  return res;
+}
+
+// A ZImageTransformer over the checkpoint <dir>/<base> as the pipeline loads it
+// (Weights::load_model with keep_bf16, pipeline.cpp:113); free with sdref_zimage_free and
+// sdref_weights_free(*weights_out).
+void* sdref_zimage_load(const char* dir, const char* base, int heads, int patch, float norm_eps, float rope_theta,
+                        float t_scale, int ax0, int ax1, int ax2, void** weights_out) {
+  void* model = nullptr;
+  guard([&] {
+    Weights* w = new Weights();
+    try {
+      w->load_model(dir, base, true);
+      model = sdref_zimage_new(w, heads, patch, norm_eps, rope_theta, t_scale, ax0, ax1, ax2);
+    } catch (...) {
+      delete w;
+      throw;
+    }
+    if (!model) {
+      delete w;
+      throw std::runtime_error(g_err);
+    }
+    *weights_out = w;
+  });
+  return model;
+}
+
 // FlowMatchScheduler (scheduler.cpp:117-135): sigmas[0..steps] and the model-facing times
 // 1 - sigma_i of a `steps`-step schedule with the given shift.
 int sdref_flow_sigmas(int steps, float shift, float* sigmas, float* model_times) {

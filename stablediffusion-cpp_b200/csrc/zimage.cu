@@ -28,6 +28,7 @@
 #include <array>
 #include <cmath>
 #include <cstring>
+#include <stdexcept>
 #include <map>
 #include <memory>
 #include <string>
@@ -36,6 +37,7 @@
 
 #include "internal.h"
 #include "sdb200.h"
+#include "weights_io.h"
 
 namespace sdb {
 
@@ -140,6 +142,7 @@ class ZImage {
   float norm_eps, rope_theta, t_scale;
   int axes[3];
   std::unordered_map<std::string, WRef> w;
+  std::vector<DBuf> owned;  // device copies made by sdb200_zimage_load
   bool finalized = false;
   int64_t D = 0, head_dim = 0, in_ch = 0, tdim = 0;
   std::vector<Block> noise, context, layers;
@@ -758,6 +761,60 @@ int sdb200_zimage_sample(void* m, float* x, int64_t B, int64_t C, int64_t H, int
   SDB_GUARD({
     if (!m || !x || !cap) sdb::fail(sdb::kErrInvalidArg, "zimage_sample: null pointer");
     static_cast<ZImage*>(m)->sample(x, B, C, H, W, cap, cap_neg, L, capdim, cfg, steps, shift);
+  })
+}
+
+int sdb200_zimage_load(void* m, const char* dir, const char* base, int rank, int world, int64_t bf16_min_numel) {
+  SDB_GUARD({
+    if (!m || !dir || !base) sdb::fail(sdb::kErrInvalidArg, "zimage_load: null argument");
+    if (world < 1 || rank < 0 || rank >= world) sdb::fail(sdb::kErrInvalidArg, "zimage_load: bad rank / world");
+    ZImage* z = static_cast<ZImage*>(m);
+    if (z->finalized) sdb::fail(sdb::kErrInvalidArg, "zimage_load: model already finalized");
+    sdb::TpShard tp;
+    tp.rank = rank;
+    tp.world = world;
+    tp.heads = z->heads;
+    try {
+      const std::vector<std::string> files = sdb::checkpoint_files(dir, base);
+      sdb::read_checkpoint(files, true, bf16_min_numel > 0 ? bf16_min_numel : ((int64_t)1 << 20),
+                           world > 1 ? &tp : nullptr, [&](sdb::HostTensor&& t) {
+                             sdb::DBuf buf;
+                             buf.ensure(t.data.size());
+                             sdb::check_cuda(cudaMemcpy(buf.p, t.data.data(), t.data.size(), cudaMemcpyHostToDevice),
+                                             "zimage_load: upload");
+                             sdb::WRef r;
+                             r.p = buf.p;
+                             r.bf16 = t.bf16;
+                             r.shape = t.shape;
+                             z->owned.push_back(std::move(buf));
+                             z->w[t.name] = r;
+                           });
+    } catch (const std::runtime_error& e) {
+      sdb::fail(sdb::kErrInvalidArg, std::string("zimage_load: ") + e.what());
+    }
+  })
+}
+
+int sdb200_safetensors_read(const char* path, const char* name, int keep_bf16, int64_t bf16_min_numel, void* dst,
+                            int64_t dst_bytes, int64_t* shape, int* ndim, int* is_bf16) {
+  SDB_GUARD({
+    if (!path || !name || !shape || !ndim || !is_bf16) sdb::fail(sdb::kErrInvalidArg, "safetensors_read: null argument");
+    sdb::HostTensor t;
+    bool ok = false;
+    try {
+      ok = sdb::read_tensor(path, name, keep_bf16 != 0, bf16_min_numel > 0 ? bf16_min_numel : ((int64_t)1 << 20), t);
+    } catch (const std::runtime_error& e) {
+      sdb::fail(sdb::kErrInvalidArg, std::string("safetensors_read: ") + e.what());
+    }
+    if (!ok) sdb::fail(sdb::kErrUnsupported, "safetensors_read: dtype not read (F32 / F16 / BF16 only)");
+    if (t.shape.size() > 8) sdb::fail(sdb::kErrUnsupported, "safetensors_read: more than 8 dimensions");
+    *ndim = (int)t.shape.size();
+    for (size_t i = 0; i < t.shape.size(); ++i) shape[i] = t.shape[i];
+    if (dst) {
+      if ((int64_t)t.data.size() > dst_bytes) sdb::fail(sdb::kErrInvalidArg, "safetensors_read: dst too small");
+      std::memcpy(dst, t.data.data(), t.data.size());
+    }
+    *is_bf16 = t.bf16 ? 1 : 0;
   })
 }
 

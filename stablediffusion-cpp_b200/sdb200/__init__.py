@@ -84,6 +84,8 @@ _SIGS = {
     "sdb200_zimage_set_tp_mode": ([_v, _i], _i),
     "sdb200_zimage_sample": ([_v, _v, _i64, _i64, _i64, _i64, _v, _v, _i64, _i64, _f, _i, _f], _i),
     "sdb200_flow_sigmas": ([_i, _f, _v], _i),
+    "sdb200_zimage_load": ([_v, C.c_char_p, C.c_char_p, _i, _i, _i64], _i),
+    "sdb200_safetensors_read": ([C.c_char_p, C.c_char_p, _i, _i64, _v, _i64, _v, _v, _v], _i),
     "sdb200_comm_unique_id": ([_v], _i),
     "sdb200_comm_create": ([_v, _i, _i], _v),
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
@@ -149,4 +151,21 @@ def flow_sigmas(steps: int, shift: float = 3.0):
 
     out = np.zeros(steps + 1, dtype=np.float32)
     check(lib().sdb200_flow_sigmas(int(steps), float(shift), out.ctypes.data_as(C.c_void_p)))
+    return out
+
+
+def safetensors_read(path: str, name: str, keep_bf16: bool = True, bf16_min_numel: int = 1 << 20):
+    """One tensor of a .safetensors file, converted as the reference converts it: a numpy
+    uint16 array of BF16 bit patterns, or float32."""
+    import numpy as np
+
+    shape = (C.c_int64 * 8)()
+    ndim, isb = C.c_int(0), C.c_int(0)
+    check(lib().sdb200_safetensors_read(path.encode(), name.encode(), int(keep_bf16), int(bf16_min_numel), None, 0,
+                                        shape, C.byref(ndim), C.byref(isb)))
+    dims = [shape[i] for i in range(ndim.value)]
+    out = np.empty(dims, dtype=np.uint16 if isb.value else np.float32)
+    check(lib().sdb200_safetensors_read(path.encode(), name.encode(), int(keep_bf16), int(bf16_min_numel),
+                                        out.ctypes.data_as(C.c_void_p), out.nbytes, shape, C.byref(ndim),
+                                        C.byref(isb)))
     return out

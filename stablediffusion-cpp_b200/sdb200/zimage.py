@@ -144,6 +144,26 @@ class ZImageB200:
             check(L.sdb200_zimage_set_weight(self._m, name.encode(), t.data_ptr(), int(is_bf16), shape, t.dim()))
         check(L.sdb200_zimage_finalize(self._m))
 
+    @classmethod
+    def from_checkpoint(cls, dir_: str, base: str = "diffusion_pytorch_model", cfg: ZConfig = Z_IMAGE, rank: int = 0,
+                        world: int = 1, bf16_min_numel: int = 0):
+        """A model over the checkpoint <dir>/<base> (.safetensors, sharded .index.json or
+        .fp16), read by the library as the reference reads it (sdb200_zimage_load); with
+        world > 1 only rank's tensor-parallel shard is read (then call set_tp)."""
+        from . import backend
+
+        backend.bind_stream()
+        self = cls.__new__(cls)
+        self.cfg = cfg
+        self._bufs = {}
+        L = lib()
+        self._m = L.sdb200_zimage_create(cfg.heads, cfg.patch, cfg.norm_eps, cfg.rope_theta, cfg.t_scale, *cfg.axes)
+        if not self._m:
+            raise RuntimeError(L.sdb200_last_error().decode())
+        check(L.sdb200_zimage_load(self._m, dir_.encode(), base.encode(), int(rank), int(world), int(bf16_min_numel)))
+        check(L.sdb200_zimage_finalize(self._m))
+        return self
+
     def forward(self, x, t: float, cap, out=None):
         """x [B, C, H, W], cap [B, L, cap_dim] (CUDA fp32) -> [B, C, H, W]."""
         import torch

@@ -134,3 +134,46 @@ def test_zimage_sampler_on_device(sdb, orc, ref, cfg_scale):
             n = model(yr, 1.0 - sig[i], neg[b:b + 1]) if cfg_scale else None
             yr = ref.flow_step(yr, o, n, cfg_scale, i, steps, shift)
         assert rel_fro(got[b:b + 1], yr) <= TOL_LATENT
+
+
+def _as_read(w, bf, min_numel):
+    """The weights as the checkpoint reader returns them from a file that holds the bf16
+    names as BF16 and the rest as F32: BF16 from min_numel elements up, F32 below."""
+    from sdb200.workloads import f32_to_bf16_bits
+
+    out, names = {}, set()
+    for n, a in w.items():
+        if a.size >= min_numel:
+            out[n] = (f32_to_bf16_bits(a).astype(np.uint32) << 16).view(np.float32)
+            names.add(n)
+        else:
+            out[n] = a
+    return out, names
+
+
+def test_zimage_load_checkpoint(sdb, ref, tmp_path):
+    """sdb200_zimage_load on a two-file checkpoint (index.json) against the same weights
+    registered one by one (bit-identical output), and against the reference loading the
+    same directory with its own reader (latent gate)."""
+    from safetensors_writer import write_checkpoint
+    from sdb200.workloads import f32_to_bf16_bits
+    from sdb200.zimage import ZConfig, ZImageB200, random_weights_numpy
+
+    cfg = ZConfig(dim=256, heads=2, ffn=512, t_dim=256, t_hidden=512, cap_dim=128, layers=2, noise_refiners=1,
+                  context_refiners=1)
+    w, bf = random_weights_numpy(cfg, 0)
+    tensors = {n: ("BF16", f32_to_bf16_bits(a)) if n in bf else ("F32", a) for n, a in w.items()}
+    base = "diffusion_pytorch_model"
+    write_checkpoint(str(tmp_path), base, tensors, shards=2)
+    mn = 32768  # every block matrix is at least this large
+    loaded = ZImageB200.from_checkpoint(str(tmp_path), base, cfg, bf16_min_numel=mn)
+    w2, bf2 = _as_read(w, bf, mn)
+    same = ZImageB200(w2, cfg, bf16_names=bf2)
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((2, 16, 16, 16)).astype(np.float32)
+    cap = rng.standard_normal((2, 20, 128)).astype(np.float32)
+    got = _np(loaded.forward(_t(x), 0.4, _t(cap)))
+    assert np.array_equal(got, _np(same.forward(_t(x), 0.4, _t(cap))))
+    rm = ref.zimage_load(str(tmp_path), base, heads=cfg.heads)
+    for b in range(2):
+        assert rel_fro(got[b:b + 1], rm(x[b:b + 1], 0.4, cap[b:b + 1])) <= TOL_LATENT

@@ -1,7 +1,8 @@
 """Worker run under torchrun by tests/test_tp_gpu.py: the Z-Image forward with tensor
 parallelism over the launched GPUs (heads 3 and FFN 528 split unevenly over 2 ranks), in
 both exchange modes (fused into the kernels over NVLink, and NCCL all-reduce), against
-the single-GPU forward and the CPU oracle. Rank 0 prints one JSON line."""
+the single-GPU forward and the CPU oracle, and the same model loaded per rank from a
+checkpoint file. Rank 0 prints one JSON line."""
 import datetime
 import json
 import os
@@ -47,6 +48,35 @@ def main():
     t = torch.tensor([max(diffs)], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     m.set_tp(None)
+    # The same model read from a checkpoint file, each rank reading only its shard
+    # (sdb200_zimage_load): identical to the shards registered from memory.
+    import tempfile
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from safetensors_writer import write_checkpoint
+    from sdb200.workloads import f32_to_bf16_bits
+
+    mn = 32768
+    box = [tempfile.mkdtemp(prefix="tpck_") if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    if rank == 0:
+        write_checkpoint(box[0], "model", {n: ("BF16", f32_to_bf16_bits(a)) if n in bf else ("F32", a)
+                                           for n, a in w.items()}, shards=2)
+    dist.barrier()
+    w_read = {n: (f32_to_bf16_bits(a).astype(np.uint32) << 16).view(np.float32) if a.size >= mn else a
+              for n, a in w.items()}
+    bf_read = {n for n, a in w.items() if a.size >= mn}
+    mf = ZImageB200.from_checkpoint(box[0], "model", cfg, rank=rank, world=world, bf16_min_numel=mn)
+    mf.set_tp(comm)
+    y_file = mf.forward(xt, 0.6, capt)
+    mm = ZImageB200(shard_weights(w_read, cfg.heads, 128, rank, world), cfg, bf16_names=bf_read)
+    mm.set_tp(comm)
+    y_mem = mm.forward(xt, 0.6, capt)
+    torch.cuda.synchronize()
+    file_diff = torch.tensor([float((y_file - y_mem).abs().max().item())], device=dev)
+    dist.all_reduce(file_diff, op=dist.ReduceOp.MAX)
+    mf.set_tp(None)
+    mm.set_tp(None)
     if rank == 0:
         from oracle import Oracle
         from zimage_oracle import ZImageOracle
@@ -58,6 +88,7 @@ def main():
         print(json.dumps({"world": world, "rel_vs_single_gpu": rel(fused, single), "rel_vs_oracle": rel(fused, want),
                           "allreduce_rel_vs_single_gpu": rel(allred, single),
                           "allreduce_rel_vs_oracle": rel(allred, want), "max_rank_diff": float(t.item()),
+                          "checkpoint_vs_memory_max_diff": float(file_diff.item()),
                           "finite": bool(np.isfinite(fused).all() and np.isfinite(allred).all()),
                           "err_word": sdb200.backend.device_error_word()}), flush=True)
     comm.close()
