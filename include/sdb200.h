@@ -133,6 +133,10 @@ int sdb200_set_gemm_tile(int bn);
  * pairs of SMs with 256 x 256 tiles (M = 256 MMAs over a cluster of two CTAs) when
  * enable != 0 (default), on single SMs with 128 x 256 tiles otherwise. */
 int sdb200_set_gemm_pair(int enable);
+/* Tuning extension (no reference counterpart): stride-1 conv2d runs as an implicit GEMM
+ * over an NHWC copy of the input when enable != 0 (default), as im2col + GEMM otherwise
+ * (the reference's lowering, backend_cuda.cu:479-510). */
+int sdb200_set_conv_implicit(int enable);
 
 /* ---- attention ------------------------------------------------------------------- */
 /* backend_cuda.h:58-59 attention(): q [N, Sq, heads*d]; k, v [N, Skv, kv_heads*d];

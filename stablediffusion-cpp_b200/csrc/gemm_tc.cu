@@ -36,6 +36,20 @@ constexpr int kBM = 128;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
 
+// Implicit-GEMM convolution, stride 1: out[img, co, oy, ox] = sum over taps (ky, kx) and
+// channels ci of w[co, ky, kx, ci] * x[img, oy - pad + ky, ox - pad + kx, ci] (+ bias[co])
+// (+ res[img, co, oy, ox]). GEMM rows are output channels; a tile's BN columns are a
+// BW x BH rectangle of output pixels of one image (column j -> (oy0 + j / BW, ox0 + j % BW)).
+// One K block is 32 channels of one tap, loaded as a 4-D TMA box of the NHWC input that the
+// hardware zero-fills outside the image (the padding).
+struct ConvGeom {
+  int Ho, Wo, BW, BH, tiles_x, tiles_y;
+  int kw, pad, cblocks;
+  int b_bytes;             // bytes of one B box (BW * BH rows of 128 B)
+  long long img_stride;    // elements between images of the output (Cout * Ho * Wo)
+  const float* res;        // residual added in the epilogue (output layout), or null
+};
+
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, num_tiles, k_blocks;
@@ -49,6 +63,7 @@ struct GemmParams {
   int* err;
   QkvRope rope;  // Epi::kQkvRope
   ScatterOut sc;  // Epi::kScatter
+  ConvGeom cv;    // implicit-GEMM convolution (k_gemm_tc<BN, true, true>)
 };
 
 constexpr int kStgPitch = 36;  // floats per staged row: 16-byte aligned, spreads banks
@@ -333,7 +348,85 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, u
   }
 }
 
-template <int BN, bool TF32>
+// Pixel tile nb of the implicit convolution -> image and top-left output pixel.
+__device__ __forceinline__ void conv_tile(const ConvGeom& g, int nb, int& img, int& oy0, int& ox0) {
+  const int tx = nb % g.tiles_x;
+  const int r = nb / g.tiles_x;
+  const int ty = r % g.tiles_y;
+  img = r / g.tiles_y;
+  oy0 = ty * g.BH;
+  ox0 = tx * g.BW;
+}
+
+// Epilogue of the implicit convolution for one warp: rows (output channels) row_base..+31,
+// this thread's channel row_base + lane. Each 32-column chunk is 32 consecutive pixels of
+// one output row (BW a multiple of 32), or of the flattened image when BW == Wo < 32. The
+// warp's 32 x 32 block goes through shared memory (stg, pitch kStgPitch) so that each
+// store instruction writes four whole 128-byte channel-row segments instead of 32 lines
+// one channel plane (Ho * Wo * 4 bytes) apart.
+template <int BN>
+__device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, uint32_t tbase, int row_base, int nb,
+                                              int lane) {
+  const ConvGeom& g = p.cv;
+  int img, oy0, ox0;
+  conv_tile(g, nb, img, oy0, ox0);
+  const long long hw = (long long)g.Ho * g.Wo;
+  const int co = row_base + lane;
+  const float bias = (co < p.M && p.bias) ? __ldg(p.bias + co) : 0.0f;
+  float* out = reinterpret_cast<float*>(p.C) + (long long)img * g.img_stride;
+  const float* res = g.res ? g.res + (long long)img * g.img_stride : nullptr;
+  const int sub = lane >> 3, c4 = (lane & 7) * 4;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int j0 = c * 32;
+    if (j0 >= g.BW * g.BH) break;  // uniform: columns past the pixel rectangle are unused
+    long long pix0;
+    int n;
+    if (g.BW >= 32) {
+      const int oy = oy0 + j0 / g.BW, ox = ox0 + j0 % g.BW;
+      pix0 = (long long)oy * g.Wo + ox;
+      n = (oy < g.Ho && ox < g.Wo) ? min(32, g.Wo - ox) : 0;
+    } else {
+      pix0 = (long long)oy0 * g.Wo + j0;
+      n = (int)min((long long)min(32, g.BW * g.BH - j0), hw - pix0);
+    }
+    if (n <= 0) continue;  // uniform over the warp
+    uint32_t r[32];
+    __syncwarp();
+    tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), r);
+    tmem_wait_ld();
+    float* mine = stg + lane * kStgPitch;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(mine + j) =
+          make_float4(__uint_as_float(r[j]) + bias, __uint_as_float(r[j + 1]) + bias,
+                      __uint_as_float(r[j + 2]) + bias, __uint_as_float(r[j + 3]) + bias);
+    __syncwarp();
+    const bool vec = n == 32 && p.vec_ok && (pix0 & 3) == 0;
+#pragma unroll
+    for (int r0 = 0; r0 < 32; r0 += 4) {
+      const int rr = r0 + sub, ch = row_base + rr;
+      if (ch >= p.M) continue;
+      const long long off = (long long)ch * hw + pix0 + c4;
+      const float* src = stg + rr * kStgPitch + c4;
+      if (vec) {
+        float4 o = *reinterpret_cast<const float4*>(src);
+        if (res) {
+          const float4 a4 = __ldg(reinterpret_cast<const float4*>(res + off));
+          o.x += a4.x; o.y += a4.y; o.z += a4.z; o.w += a4.w;
+        }
+        *reinterpret_cast<float4*>(out + off) = o;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c4 + e < n) out[off + e] = res ? src[e] + __ldg(res + off + e) : src[e];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <int BN, bool TF32, bool CONV = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   using C_ = Cfg<BN>;
@@ -396,14 +489,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
         int mb, nb;
         tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        int img = 0, oy0 = 0, ox0 = 0;
+        if constexpr (CONV) conv_tile(p.cv, nb, img, oy0, ox0);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrWaitEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
-          tma_load_2d(sA + stage * C_::A_BYTES, &tmA, &full[stage], kb * BK, mb * kBM);
-          tma_load_2d(sB + stage * C_::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          if constexpr (CONV) {
+            const int tap = kb / p.cv.cblocks, cb = kb - tap * p.cv.cblocks;
+            const int ky = tap / p.cv.kw, kx = tap - ky * p.cv.kw;
+            mbar_arrive_expect_tx(&full[stage], C_::A_BYTES + p.cv.b_bytes);
+            tma_load_2d(sA + stage * C_::A_BYTES, &tmA, &full[stage], kb * BK, mb * kBM);
+            tma_load_4d(sB + stage * C_::B_BYTES, &tmB, &full[stage], cb * 32, ox0 + kx - p.cv.pad,
+                        oy0 + ky - p.cv.pad, img);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+            tma_load_2d(sA + stage * C_::A_BYTES, &tmA, &full[stage], kb * BK, mb * kBM);
+            tma_load_2d(sB + stage * C_::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          }
           issued |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -487,7 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
+      if constexpr (CONV)
+        epilogue_conv<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
+      else
+        epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -909,6 +1016,116 @@ void launch_gemm_tc(const GemmCall& g) {
       case 128: launch_bn<128, false>(g, p, c.num_sms); break;
       default: launch_bn<64, false>(g, p, c.num_sms); break;
     }
+  }
+}
+
+namespace {
+template <int BN>
+void launch_conv_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int num_sms, int dev,
+                    cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  auto kern = k_gemm_tc<BN, true, true>;
+  static bool attr_set[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM),
+               "cudaFuncSetAttribute(conv)");
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(p.num_tiles, num_sms);
+  kern<<<grid, kThreads, C_::SMEM, stream>>>(ta, tb, p);
+  check_launch("conv_tc");
+}
+
+// Pixel rectangle of a BN-column tile: BW a power of two >= 32 (or the whole row when
+// Wo < 32), BH rows, never more rows than the image has.
+void conv_rect(int bn, int64_t Ho, int64_t Wo, int& bw, int& bh) {
+  if (Wo >= 32) {
+    bw = 32;
+    while (bw < Wo && bw < bn) bw *= 2;
+    bh = bn / bw;
+  } else {
+    bw = (int)Wo;
+    bh = std::min(bn / (int)Wo, 256);
+  }
+  bh = (int)std::min<int64_t>(bh, Ho);
+}
+}  // namespace
+
+void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                    int64_t cq, int64_t Cout, int kh, int kw, int pad, const float* bias, const float* res, float* out,
+                    int64_t Ho, int64_t Wo) {
+  DeviceContext& c = ctx();
+  if (cp % 4 != 0 || cq % 32 != 0 || cq < Cin || cp < Cin || N <= 0 || Ho <= 0 || Wo <= 0)
+    fail(kErrInvalidArg, "conv_tc: bad packed layout");
+  if (Cout > (1 << 30) || Ho * Wo > (1ll << 31) || N > 65535)
+    fail(kErrInvalidArg, "conv_tc: shape too large");
+  // Tile width by the wave-count cost model of choose_bn over the pixel rectangles.
+  const int64_t m_tiles = (Cout + kBM - 1) / kBM;
+  int bn = 256, bw = 0, bh = 0;
+  double best = 1e30;
+  for (int cand : {256, 128, 64}) {
+    int w_, h_;
+    conv_rect(cand, Ho, Wo, w_, h_);
+    const int64_t tiles = m_tiles * N * ((Ho + h_ - 1) / h_) * ((Wo + w_ - 1) / w_);
+    const double cost = (double)((tiles + c.num_sms - 1) / c.num_sms) * (cand + 48);
+    if (cost < best - 1e-9) {
+      best = cost;
+      bn = cand;
+      bw = w_;
+      bh = h_;
+    }
+  }
+  if (g_forced_bn == 256 || g_forced_bn == 128 || g_forced_bn == 64) {
+    bn = g_forced_bn;
+    conv_rect(bn, Ho, Wo, bw, bh);
+  }
+  const int64_t kk = (int64_t)kh * kw * cq;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)kk, (uint64_t)Cout};
+    const uint64_t strides[1] = {(uint64_t)kk * 4};
+    const uint32_t box[2] = {32, (uint32_t)kBM};
+    encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)N};
+    const uint64_t strides[3] = {(uint64_t)cp * 4, (uint64_t)(W * cp * 4), (uint64_t)(H * W * cp * 4)};
+    const uint32_t box[4] = {32, (uint32_t)bw, (uint32_t)bh, 1};
+    encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  GemmParams p{};
+  p.M = (int)Cout;
+  p.N = bw * bh;  // columns used per tile (informational; the conv epilogue masks by geometry)
+  p.K = (int)kk;
+  p.cv.Ho = (int)Ho;
+  p.cv.Wo = (int)Wo;
+  p.cv.BW = bw;
+  p.cv.BH = bh;
+  p.cv.tiles_x = (int)((Wo + bw - 1) / bw);
+  p.cv.tiles_y = (int)((Ho + bh - 1) / bh);
+  p.cv.kw = kw;
+  p.cv.pad = pad;
+  p.cv.cblocks = (int)(cq / 32);
+  p.cv.b_bytes = bw * bh * 128;
+  p.cv.img_stride = Cout * Ho * Wo;
+  p.cv.res = res;
+  p.m_tiles = (int)m_tiles;
+  p.n_tiles = (int)(N * p.cv.tiles_x * p.cv.tiles_y);
+  if ((int64_t)p.m_tiles * p.n_tiles > (1ll << 31) - 1) fail(kErrInvalidArg, "conv_tc: too many tiles");
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = (int)(kk / 32);
+  p.C = out;
+  p.ldc = Ho * Wo;
+  p.bias = bias;
+  p.epi = (int)Epi::kStore;
+  const bool al = (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                  (!res || (reinterpret_cast<uintptr_t>(res) & 15) == 0);
+  p.vec_ok = al && (Ho * Wo) % 4 == 0;
+  p.err = c.err_word;
+  switch (bn) {
+    case 256: launch_conv_bn<256>(ta, tb, p, c.num_sms, c.device, c.stream); break;
+    case 128: launch_conv_bn<128>(ta, tb, p, c.num_sms, c.device, c.stream); break;
+    default: launch_conv_bn<64>(ta, tb, p, c.num_sms, c.device, c.stream); break;
   }
 }
 

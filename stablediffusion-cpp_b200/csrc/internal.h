@@ -118,10 +118,23 @@ struct GemmCall {
   const ScatterOut* scatter = nullptr;  // Epi::kScatter only (C unused, ldc = row length)
 };
 void launch_gemm_tc(const GemmCall& g);
+// Implicit-GEMM convolution (stride 1) on kind::tf32: out NCHW [N, Cout, Ho, Wo] =
+// conv(x, w) (+bias[Cout]) (+res, same layout as out). xh is the input in NHWC with a
+// channel pitch cp (% 4 == 0; channels past Cin are ignored) and wp the weights as
+// [Cout, kh, kw, cq] with cq = round_up(Cin, 32), zero past Cin; both tf32-rounded.
+void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                    int64_t cq, int64_t Cout, int kh, int kw, int pad, const float* bias, const float* res, float* out,
+                    int64_t Ho, int64_t Wo);
+// NCHW fp32 [N, C, HW] -> NHWC [N, HW, cp], rounded to tf32, zero in channels C..cp-1.
+void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp);
+// Conv weights [Cout, Cin, taps] -> [Cout, taps, cq], rounded to tf32, zero past Cin.
+void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
 void set_gemm_tile(int bn);
 // Enables (default) or disables the CTA-pair kernel for bf16 GEMMs with 256-wide tiles.
 void set_gemm_pair(bool on);
+// Enables (default) or disables the implicit-GEMM path of conv2d for stride 1.
+void set_conv_implicit(bool on);
 // bf16 tcgen05 GEMM on an explicit device / stream / error word; no device context.
 void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream, int* err_word, int dev);
 // Small-M (M <= 16) GEMM through a memory-bound SIMT kernel (weights streamed once).
@@ -137,7 +150,9 @@ void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* 
 
 // Layer ops (layers.cu); arguments already validated by the caller.
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
-void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float);
+// GroupNorm over N samples of C channels x HW values (optionally followed by SiLU).
+void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float,
+                   bool silu = false);
 void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const float*, float, bool);
 void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
 void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);

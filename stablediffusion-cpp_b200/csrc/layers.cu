@@ -100,6 +100,45 @@ __global__ void k_pack_tf32(const float* __restrict__ src, int64_t ld, float* __
     dst[r * ldo + c] = round_tf32(src[r * ld + c]);
   }
 }
+// NCHW -> NHWC (channel pitch cp) through a 32-channel x 128-pixel shared-memory tile:
+// 128-byte reads along pixels (16 in flight per thread), 128-byte writes along channels;
+// tf32-rounded, zero past C.
+constexpr int kPackPx = 128;
+__global__ void __launch_bounds__(256) k_conv_pack_x(const float* __restrict__ x, float* __restrict__ xh, int64_t C,
+                                                     int64_t HW, int64_t cp) {
+  __shared__ float tile[32][kPackPx + 1];
+  const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * kPackPx, c0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  float v[4][kPackPx / 32];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t c = c0 + ty + 8 * i;
+#pragma unroll
+    for (int j = 0; j < kPackPx / 32; ++j) {
+      const int64_t p = p0 + tx + 32 * j;
+      v[i][j] = (c < C && p < HW) ? __ldg(x + (n * C + c) * HW + p) : 0.0f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < kPackPx / 32; ++j) tile[ty + 8 * i][tx + 32 * j] = round_tf32(v[i][j]);
+  __syncthreads();
+  const int64_t c = c0 + tx;
+  if (c >= cp) return;
+#pragma unroll 4
+  for (int i = 0; i < kPackPx / 8; ++i) {
+    const int64_t p = p0 + ty + 8 * i;
+    if (p < HW) xh[(n * HW + p) * cp + c] = tile[tx][ty + 8 * i];
+  }
+}
+__global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ wp, int64_t Cin, int64_t taps,
+                              int64_t cq, int64_t total) {
+  GRID_STRIDE(i, total) {
+    const int64_t ci = i % cq, r = i / cq, t = r % taps, co = r / taps;
+    wp[i] = ci < Cin ? round_tf32(__ldg(w + (co * Cin + ci) * taps + t)) : 0.0f;
+  }
+}
 __global__ void k_copy2d_16(const uint16_t* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
                             int64_t rows, int64_t cols) {
   GRID_STRIDE(i, rows * cols) {
@@ -212,28 +251,95 @@ __global__ void __launch_bounds__(256) k_gemm_skinny(int M, int N, int K, const 
 // ---------------------------------------------------------------------------------
 // Norms (tensor.cpp:588-679, :681-699)
 // ---------------------------------------------------------------------------------
-// GroupNorm: one block per (sample, group); two passes (mean, then variance), as the
-// reference CPU path does in double (tensor.cpp:603-624).
-__global__ void k_group_norm(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t HW, int groups,
-                             const float* __restrict__ gamma, const float* __restrict__ beta, float eps) {
+// GroupNorm (tensor.cpp:603-624) in three steps over the N * groups contiguous segments
+// of cg * HW values:
+//   1. k_gn_stats: one block per 8192-value chunk keeps its chunk in registers and
+//      writes the chunk's mean and sum of squared deviations (two passes, fp32);
+//   2. k_gn_finalize: one warp per segment combines its chunks in double (Chan et al.'s
+//      pairwise update: M2 = sum M2_c + n_c (mean_c - mean)^2), the counterpart of the
+//      reference's double two-pass statistics, and folds normalisation and the affine
+//      transform into a per-channel scale a = rstd * gamma and shift b = beta - mean * a;
+//   3. k_gn_apply: y = x * a + b over every (sample, channel) row, optionally SiLU.
+constexpr int kGnThreads = 256;
+constexpr int kGnPer = 32;  // values per thread per chunk
+constexpr int kGnChunk = kGnThreads * kGnPer;
+__global__ void __launch_bounds__(kGnThreads) k_gn_stats(const float* __restrict__ x, int64_t len, int chunks,
+                                                         float2* __restrict__ part) {
   __shared__ float red[32];
-  const int64_t n = blockIdx.x / groups, g = blockIdx.x % groups, cg = C / groups, len = cg * HW;
-  const float* p = x + (n * C + g * cg) * HW;
-  float* q = y + (n * C + g * cg) * HW;
+  const int64_t seg = blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * kGnChunk;
+  const float* p = x + seg * len + c0;
+  const int64_t n = (len - c0 < (int64_t)kGnChunk ? len - c0 : (int64_t)kGnChunk);
+  float v[kGnPer];
   float s = 0.0f;
-  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) s += p[i];
-  const float mean = block_sum(s, red) / (float)len;
-  float v = 0.0f;
-  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
-    const float d = p[i] - mean;
-    v += d * d;
+#pragma unroll
+  for (int j = 0; j < kGnPer; ++j) {
+    const int64_t i = (int64_t)j * kGnThreads + threadIdx.x;
+    v[j] = i < n ? __ldg(p + i) : 0.0f;
+    s += v[j];
   }
-  const float var = block_sum(v, red) / (float)len;
-  const float rstd = rsqrtf(var + eps);
-  for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
-    const int64_t ch = g * cg + i / HW;
+  const float mean = block_sum(s, red) / (float)n;
+  float m2 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kGnPer; ++j) {
+    const int64_t i = (int64_t)j * kGnThreads + threadIdx.x;
+    const float d = v[j] - mean;
+    if (i < n) m2 = fmaf(d, d, m2);
+  }
+  m2 = block_sum(m2, red);
+  if (threadIdx.x == 0) part[seg * chunks + blockIdx.x] = make_float2(mean, m2);
+}
+__global__ void k_gn_finalize(const float2* __restrict__ part, int chunks, int64_t len, int64_t C, int groups,
+                              const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+                              float2* __restrict__ ab, int64_t segs) {
+  const int64_t seg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (seg >= segs) return;
+  const float2* q = part + seg * chunks;
+  double sum = 0.0;
+  for (int c = lane; c < chunks; c += 32) {
+    const double nc = (double)(len - (int64_t)c * kGnChunk < (int64_t)kGnChunk ? len - (int64_t)c * kGnChunk : (int64_t)kGnChunk);
+    sum += nc * (double)q[c].x;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const double mean = sum / (double)len;
+  double m2 = 0.0;
+  for (int c = lane; c < chunks; c += 32) {
+    const double nc = (double)(len - (int64_t)c * kGnChunk < (int64_t)kGnChunk ? len - (int64_t)c * kGnChunk : (int64_t)kGnChunk);
+    const double d = (double)q[c].x - mean;
+    m2 += (double)q[c].y + nc * d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
+  const float rstd = (float)(1.0 / sqrt(m2 / (double)len + (double)eps));
+  const int64_t n = seg / groups, g = seg % groups, cg = C / groups;
+  for (int64_t c = lane; c < cg; c += 32) {
+    const int64_t ch = g * cg + c;
     const float a = rstd * gamma[ch];
-    q[i] = p[i] * a + (beta[ch] - mean * a);
+    ab[n * C + ch] = make_float2(a, beta[ch] - (float)mean * a);
+  }
+}
+template <bool VEC>
+__global__ void k_gn_apply(const float* __restrict__ x, float* __restrict__ y, int64_t HW,
+                           const float2* __restrict__ ab, int silu) {
+  const int64_t row = blockIdx.y;
+  const float2 t = ab[row];
+  const float* p = x + row * HW;
+  float* q = y + row * HW;
+  auto f = [&](float v) {
+    const float o = v * t.x + t.y;
+    return silu ? o / (1.0f + expf(-o)) : o;
+  };
+  if (VEC) {
+    const int64_t n4 = HW >> 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p) + i);
+      reinterpret_cast<float4*>(q)[i] = make_float4(f(v.x), f(v.y), f(v.z), f(v.w));
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < HW; i += (int64_t)gridDim.x * blockDim.x)
+      q[i] = f(__ldg(p + i));
   }
 }
 // LayerNorm / RMSNorm over rows of C (tensor.cpp:628-679).
@@ -436,6 +542,18 @@ void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, 
     k_pack_bf16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
   check_launch("pack_bf16");
 }
+void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
+  if (N <= 0 || HW <= 0) return;
+  const dim3 grid((unsigned)((HW + kPackPx - 1) / kPackPx), (unsigned)((cp + 31) / 32), (unsigned)N);
+  k_conv_pack_x<<<grid, dim3(32, 8), 0, ctx().stream>>>(x, xh, C, HW, cp);
+  check_launch("conv_pack_x");
+}
+void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq) {
+  const int64_t total = Cout * taps * cq;
+  if (total <= 0) return;
+  k_conv_pack_w<<<grid_for(total), kT, 0, ctx().stream>>>(w, wp, Cin, taps, cq, total);
+  check_launch("conv_pack_w");
+}
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return;
   k_pack_tf32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
@@ -480,10 +598,30 @@ void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 
 // Public layer ops (called from runtime.cu's C ABI after argument checks).
 void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
-                   const float* beta, float eps) {
+                   const float* beta, float eps, bool silu) {
   if (N <= 0 || C <= 0 || HW <= 0) return;
-  k_group_norm<<<(unsigned)(N * groups), 512, 0, ctx().stream>>>(x, y, C, HW, groups, gamma, beta, eps);
+  const int64_t segs = N * groups, len = (C / groups) * HW;
+  const int64_t chunks = (len + kGnChunk - 1) / kGnChunk;
+  if (segs > 65535 || N * C > 65535 || chunks > (1ll << 31) - 1)
+    fail(kErrInvalidArg, "group_norm: too many samples or channels");
+  const size_t pb = ((size_t)(segs * chunks) * sizeof(float2) + 255) & ~(size_t)255;
+  uint8_t* ws = static_cast<uint8_t*>(pool_malloc(pb + (size_t)(N * C) * sizeof(float2)));
+  float2* part = reinterpret_cast<float2*>(ws);
+  float2* ab = reinterpret_cast<float2*>(ws + pb);
+  cudaStream_t st = ctx().stream;
+  k_gn_stats<<<dim3((unsigned)chunks, (unsigned)segs), kGnThreads, 0, st>>>(x, len, (int)chunks, part);
+  k_gn_finalize<<<(unsigned)((segs + 7) / 8), 256, 0, st>>>(part, (int)chunks, len, C, groups, gamma, beta, eps, ab,
+                                                            segs);
+  const bool vec = HW % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  const int64_t per_row = vec ? HW / 4 : HW;
+  const unsigned bx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((per_row + 4 * 256 - 1) / (4 * 256), 64));
+  if (vec)
+    k_gn_apply<true><<<dim3(bx, (unsigned)(N * C)), 256, 0, st>>>(x, y, HW, ab, silu ? 1 : 0);
+  else
+    k_gn_apply<false><<<dim3(bx, (unsigned)(N * C)), 256, 0, st>>>(x, y, HW, ab, silu ? 1 : 0);
   check_launch("group_norm");
+  // Stream-ordered: the next user of this pool block is issued on the same stream.
+  pool_free(ws);
 }
 void op_row_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta, float eps,
                  bool rms) {

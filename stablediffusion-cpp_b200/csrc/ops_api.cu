@@ -204,8 +204,13 @@ void gemm_bf16_scatter_impl(int64_t M, int64_t N, int64_t K, const void* A, int6
   gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kScatter, nullptr, &so);
 }
 
-// conv2d as im2col + tf32 GEMM, writing NCHW directly (ldc = HW), as
-// backend_cuda.cu:479-510 does with cuBLAS.
+// Implicit-GEMM convolution for stride 1 (default); off: im2col for every stride.
+static bool g_conv_implicit = true;
+void set_conv_implicit(bool on) { g_conv_implicit = on; }
+
+// conv2d (backend_cuda.cu:479-510). Stride 1 runs as an implicit GEMM on tf32 tensor
+// cores (launch_conv_tc); other strides as im2col + tf32 GEMM writing NCHW directly
+// (ldc = HW), as the reference does with cuBLAS.
 void conv2d_impl(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
                  int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo) {
   const char* op = "conv2d";
@@ -216,6 +221,19 @@ void conv2d_impl(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, c
   require_ptr(out, op, "out");
   const int64_t K = Cin * kh * kw, HW = Ho * Wo;
   if (N == 0 || HW <= 0) return;
+  if (stride == 1 && g_conv_implicit) {
+    // Implicit GEMM: the input repacked once to NHWC, no im2col matrix.
+    const int64_t cp = round_up(Cin, 4), cq = round_up(Cin, 32), taps = kh * kw;
+    const size_t xb = align256((size_t)(N * H * W * cp) * 4);
+    const size_t wb = align256((size_t)(Cout * taps * cq) * 4);
+    uint8_t* ws = static_cast<uint8_t*>(workspace(xb + wb));
+    float* xh = reinterpret_cast<float*>(ws);
+    float* wp = reinterpret_cast<float*>(ws + xb);
+    launch_conv_pack_x(x, xh, N, Cin, H * W, cp);
+    launch_conv_pack_w(w, wp, Cout, Cin, taps, cq);
+    launch_conv_tc(xh, N, Cin, cp, H, W, wp, cq, Cout, (int)kh, (int)kw, pad, bias, nullptr, out, Ho, Wo);
+    return;
+  }
   const int64_t Kp = round_up(K, 4);
   const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(HW, ((int64_t)1 << 26) / Kp));
   // cols live in pool memory so that the GEMM's own workspace stays free.
@@ -270,6 +288,10 @@ int sdb200_set_gemm_tile(int bn) {
 
 int sdb200_set_gemm_pair(int enable) {
   SDB_GUARD(sdb::set_gemm_pair(enable != 0))
+}
+
+int sdb200_set_conv_implicit(int enable) {
+  SDB_GUARD(sdb::set_conv_implicit(enable != 0))
 }
 
 int sdb200_set_attention_path(int path) {

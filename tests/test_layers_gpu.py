@@ -137,6 +137,85 @@ def test_conv2d_sd15_shape(sdb, orc):
     assert rel_fro(got, want) <= 2e-3
 
 
+@pytest.fixture
+def conv_setup(sdb):
+    """Selects the conv2d lowering and GEMM tile width for one test; restores defaults."""
+    def use(implicit, bn=0):
+        sdb.check(sdb.lib().sdb200_set_conv_implicit(1 if implicit else 0))
+        sdb.check(sdb.lib().sdb200_set_gemm_tile(bn))
+    yield use
+    sdb.check(sdb.lib().sdb200_set_conv_implicit(1))
+    sdb.check(sdb.lib().sdb200_set_gemm_tile(0))
+
+
+# (N, Cin, H, W, Cout, k, pad): ragged channel counts, Wo below and above 32, batches,
+# 1x1 kernels, pad 2, a one-pixel image, and UNet / VAE channel widths.
+CONV_CASES = [
+    (1, 3, 5, 7, 8, 3, 1),
+    (2, 40, 9, 33, 130, 3, 1),
+    (1, 8, 70, 40, 5, 1, 0),
+    (2, 5, 12, 20, 7, 3, 2),
+    (1, 33, 17, 65, 129, 3, 1),
+    (1, 4, 1, 1, 2, 3, 1),
+    (1, 16, 48, 48, 512, 3, 1),
+    (1, 128, 96, 96, 128, 3, 1),
+    (2, 256, 24, 24, 128, 1, 0),
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_conv2d_implicit_gemm(sdb, orc, conv_setup, case):
+    """Stride-1 conv2d as an implicit GEMM (NHWC boxes by TMA, zero-filled halo) against the
+    oracle's im2col convolution, at every tile width, and against the im2col lowering on
+    the same tf32 tensor cores (same rounded operands: only the summation order differs)
+    where that lowering uses them."""
+    N, Cin, H, W, Cout, k, pad = case
+    rng = np.random.default_rng(sum(case))
+    x = rng.standard_normal((N, Cin, H, W)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((Cout, Cin, k, k))).astype(np.float32)
+    b = (0.05 * rng.standard_normal(Cout)).astype(np.float32)
+    want = orc.conv2d(x, w, b, 1, pad)
+    conv_setup(False)
+    lowered = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 1, pad))
+    for bn in (0, 64, 128, 256):
+        conv_setup(True, bn)
+        got = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 1, pad))
+        assert got.shape == want.shape
+        assert rel_fro(got, want) <= 2e-3, bn
+        if Cout > 16:  # the lowering's GEMM runs on tf32 tensor cores (exact SIMT for M <= 16)
+            assert rel_fro(got, lowered) <= 1e-5, bn
+
+
+def test_conv2d_strided_uses_im2col(sdb, orc):
+    """Stride 2 (the UNet's downsamplers) keeps the im2col lowering."""
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((1, 64, 33, 31)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((96, 64, 3, 3))).astype(np.float32)
+    b = (0.05 * rng.standard_normal(96)).astype(np.float32)
+    want = orc.conv2d(x, w, b, 2, 1)
+    got = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 2, 1))
+    assert rel_fro(got, want) <= 2e-3
+
+
+@pytest.mark.parametrize("shape,groups", [
+    ((1, 128, 256, 256), 32),   # VAE last-stage width: 4 channels x 65536 values per group
+    ((2, 320, 37, 29), 32),     # odd plane (no 16-byte rows), several chunks per group
+    ((1, 64, 3, 3), 32),        # groups smaller than one chunk
+    ((3, 96, 17, 16), 8),
+])
+def test_group_norm_split_statistics(sdb, orc, shape, groups):
+    """GroupNorm with chunked statistics combined in double, against the oracle's double
+    two-pass statistics (the reference's GPU-vs-CPU norm tolerance, 1e-4)."""
+    rng = np.random.default_rng(shape[1])
+    # A large common offset makes single-pass fp32 statistics fail; the split form must not.
+    x = (3.0 + rng.standard_normal(shape)).astype(np.float32)
+    gamma = (1.0 + 0.1 * rng.standard_normal(shape[1])).astype(np.float32)
+    beta = (0.1 * rng.standard_normal(shape[1])).astype(np.float32)
+    want = orc.group_norm(x, groups, gamma, beta, 1e-6)
+    got = _np(sdb.backend.group_norm(_t(x), groups, _t(gamma), _t(beta), 1e-6))
+    assert np.abs(got - want).max() <= 1e-4
+
+
 def test_elementwise_and_layout(sdb):
     import torch
 
