@@ -1,7 +1,7 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dit|dit_tp|gemm|attention]
+                    [--workload dit|dit_tp|gemm|attention|conv]
 
 Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
 random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
@@ -18,6 +18,9 @@ Workload `dit_tp`: the same DiT at batch 1, 2048x2048 (16512
 Megatron tensor parallelism over the N ranks; ms per step. The row-parallel outputs are
 combined inside the kernels (--tp-mode 1, default: GEMM epilogue stores to the owner
 rank over NVLink, sequence-sharded post-norm) or by an NCCL all-reduce (--tp-mode 0).
+
+Workload `conv`: the VAE decoder's 3x3 convolutions at the four resolution stages of a
+1024^2 decode (512@128^2, 512@256^2, 256@512^2, 128@1024^2), TFLOP/s through conv2d.
 
 Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
 128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
@@ -269,6 +272,24 @@ def run_reference(args, world, rank):
                                  "sample": f"one full-width block forward per step ({dt:.2f} s), scaled by FLOPs "
                                            f"({sample_flop / 1e12:.2f} -> {step_flop / 1e12:.0f} TFLOP)"},
                 "e2e": {"value": ms, "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    elif args.workload == "conv":
+        fn, flop, cores = ref_conv_sample()
+        for _ in range(min(args.warmup, 1)):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        v = flop / dt / 1e12
+        line = {"impl": "reference", "metric": "VAE-decoder conv2d TFLOP/s (3x3, 4 stages of a 1024^2 decode)",
+                "value": v, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": dt * 1e3 * sum(conv_flops()) / flop, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 (CPU)", "data": "synthetic N(0,1) activations, N(0,0.02) weights",
+                "config": {"workload": "conv2d 3x3 pad 1, C->C: " + ", ".join(f"{c}@{s}^2" for c, s in CONV_STAGES),
+                           "sample": "the 512-channel 128^2 stage per step"},
+                "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                                 "sample": "reference conv2d of the 512-channel 128^2 stage per step"},
+                "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     else:
         fn, flop, cores, _ = ref_gemm_sample()
         for _ in range(args.warmup):
@@ -632,14 +653,150 @@ def run_attention(args, world, rank, local, pg, dev):
             "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
 
 
+# The VAE decoder's 3x3 convolution at each resolution stage of a 1024^2 decode (channels,
+# side): 512 @ 128^2, 512 @ 256^2, 256 @ 512^2, 128 @ 1024^2 (AutoencoderKL decoder, vae.cpp).
+CONV_STAGES = [(512, 128), (512, 256), (256, 512), (128, 1024)]
+
+
+def conv_flops():
+    return [2.0 * c * c * 9 * s * s for c, s in CONV_STAGES]
+
+
+def ref_conv_sample():
+    """The reference's CPU conv2d (tensor.cpp:529-586) on the smallest stage."""
+    import numpy as np
+
+    from oracle import RefCPU
+
+    ref = RefCPU()
+    ref.set_num_threads(0)
+    c, s = CONV_STAGES[0]
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((1, c, s, s)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((c, c, 3, 3))).astype(np.float32)
+    b = (0.02 * rng.standard_normal(c)).astype(np.float32)
+    return (lambda: ref.conv2d(x, w, b, 1, 1)), conv_flops()[0], ref.num_threads()
+
+
+def run_conv(args, world, rank, local, pg, dev):
+    """One step = the four VAE-decoder stage convolutions (3x3, pad 1, C -> C, batch 1)
+    through the reference API (sdb200_conv2d: NHWC repack + implicit GEMM). value =
+    TFLOP/s over the step; roofline = the implicit-GEMM kernel alone on packed operands
+    (sdb200_conv2d_nhwc), against a cuBLAS tf32 GEMM measured in the same run."""
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+
+    global CONV_STAGES
+    if args.conv_stage >= 0:
+        CONV_STAGES = [CONV_STAGES[args.conv_stage]]
+    L = sdb200.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    bufs = []
+    for c, s in CONV_STAGES:
+        x = torch.randn((1, c, s, s), generator=g, device=dev)
+        w = 0.02 * torch.randn((c, c, 3, 3), generator=g, device=dev)
+        b = 0.02 * torch.randn((c,), generator=g, device=dev)
+        bufs.append((c, s, x, w, b, torch.empty_like(x)))
+    flops = conv_flops()
+    FLOP = sum(flops)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for c, s, x, w, b, y in bufs:
+            sdb200.check(L.sdb200_conv2d(x.data_ptr(), 1, c, s, s, w.data_ptr(), c, 3, 3, b.data_ptr(), 1, 1,
+                                         y.data_ptr(), s, s))
+
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    value = FLOP * args.steps * world / (ms * 1e-3) / 1e12
+    # the implicit-GEMM kernel alone, operands packed once
+    packed = []
+    for c, s, x, w, b, y in bufs:
+        xh = torch.empty(s * s * c, device=dev)
+        wp = torch.empty(c * 9 * c, device=dev)
+        sdb200.check(L.sdb200_conv_pack_input(x.data_ptr(), xh.data_ptr(), 1, c, s * s, c))
+        sdb200.check(L.sdb200_conv_pack_weight(w.data_ptr(), wp.data_ptr(), c, c, 9, c))
+        packed.append((c, s, xh, wp, b, y))
+    kstep = lambda: [sdb200.check(L.sdb200_conv2d_nhwc(xh.data_ptr(), 1, c, c, s, s, wp.data_ptr(), c, c, 3, 3, 1,  # noqa: E731
+                                                       b.data_ptr(), None, y.data_ptr(), s, s))
+                     for c, s, xh, wp, b, y in packed]
+    for _ in range(3):
+        kstep()
+    reps = max(args.steps, 5)
+    kms = timed_loop(kstep, reps, stream, None, dev) / reps
+    achieved = FLOP / (kms * 1e-3) / 1e12
+    # cuBLAS tf32 reference rate on the same stream (8192^3, as the bf16 peak is measured)
+    allow = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    A = torch.randn((8192, 8192), device=dev)
+    B = torch.randn((8192, 8192), device=dev)
+    for _ in range(3):
+        torch.matmul(A, B)
+    tms = min(timed_loop(lambda: torch.matmul(A, B), 5, stream, None, dev) / 5 for _ in range(2))
+    torch.backends.cuda.matmul.allow_tf32 = allow
+    tf32_peak = 2.0 * 8192 ** 3 / (tms * 1e-3) / 1e12
+    del A, B
+    # end to end: host NCHW activations in, host outputs back, per stage
+    hosts = [(c, s, x.cpu().pin_memory(), torch.empty(x.shape).pin_memory(), x, w, b, y) for c, s, x, w, b, y in bufs]
+
+    def e2e_step():
+        for c, s, xh_, yh, x, w, b, y in hosts:
+            sdb200.check(L.sdb200_upload(x.data_ptr(), xh_.data_ptr(), xh_.numel() * 4))
+            sdb200.check(L.sdb200_conv2d(x.data_ptr(), 1, c, s, s, w.data_ptr(), c, 3, 3, b.data_ptr(), 1, 1,
+                                         y.data_ptr(), s, s))
+            sdb200.check(L.sdb200_download(yh.data_ptr(), y.data_ptr(), yh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
+    io = sum(h[2].numel() * 4 for h in hosts)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            fn, f0, cores = ref_conv_sample()
+            fn()
+            t0 = time.perf_counter()
+            fn()
+            dt = time.perf_counter() - t0
+            cpu = {"value": f0 / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                   "sample": f"reference conv2d (im2col + CPU GEMM) of the 512-channel 128^2 stage ({dt:.2f} s)"}
+        except Exception as e:  # reported, never required
+            cpu = {"value": None, "unit": None, "cores": None, "kind": "reference", "sample": f"failed: {e}"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "VAE-decoder conv2d TFLOP/s (3x3, 4 stages of a 1024^2 decode)", "value": value,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations and weights, tf32 tensor cores, f32 accumulate",
+            "data": "synthetic N(0,1) activations, N(0,0.02) weights and bias",
+            "config": {"workload": "conv2d 3x3 pad 1, C->C: " + ", ".join(f"{c}@{s}^2" for c, s in CONV_STAGES),
+                       "parallelism": f"replicas x{world}", "l2": "inputs 1 GB/step > 126 MB L2, no flush"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc<256, tf32, conv> (implicit GEMM, NHWC TMA boxes)",
+                         "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
+                         "peak_kind": "cuBLAS tf32 8192^3 measured live in this run (burst)", "kernel_ms": kms,
+                         "traffic": profile_value("conv_tc_vae.md", "traffic_bytes_per_step")},
+            "e2e": {"value": FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(io), "d2h_bytes_per_step": int(io)},
+            "cpu_baseline": cpu, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention", "conv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--conv-stage", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
+                    help="conv: run only this stage of the VAE-decoder stack (-1: all four)")
     ap.add_argument("--tp-mode", type=int, default=1, choices=[0, 1],
                     help="dit_tp: 1 = exchange fused into the GEMM epilogue and post-norm over NVLink, "
                          "0 = NCCL all-reduce")
@@ -671,6 +828,8 @@ def main():
         run_attention(args, world, rank, local, pg, dev)
     elif args.workload == "dit_tp":
         run_dit_tp(args, world, rank, local, pg, dev)
+    elif args.workload == "conv":
+        run_conv(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:

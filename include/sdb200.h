@@ -129,9 +129,10 @@ int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, in
 /* Tuning extension (no reference counterpart): forces the GEMM tile width N (64, 128,
  * 192 or 256) for later calls of this process; 0 restores the automatic choice. */
 int sdb200_set_gemm_tile(int bn);
-/* Tuning extension (no reference counterpart): bf16 GEMMs with 256-wide tiles run on
- * pairs of SMs with 256 x 256 tiles (M = 256 MMAs over a cluster of two CTAs) when
- * enable != 0 (default), on single SMs with 128 x 256 tiles otherwise. */
+/* Tuning extension (no reference counterpart): bf16 GEMMs with 256-wide tiles and
+ * implicit-GEMM convolutions with >= 256 output channels may run on pairs of SMs with
+ * 256 x 256 tiles (M = 256 MMAs over a cluster of two CTAs). enable: 0 never, 1 when the
+ * wave-count cost model prefers them (default), 2 whenever the shape allows. */
 int sdb200_set_gemm_pair(int enable);
 /* Tuning extension (no reference counterpart): stride-1 conv2d runs as an implicit GEMM
  * over an NHWC copy of the input when enable != 0 (default), as im2col + GEMM otherwise
@@ -232,10 +233,26 @@ int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n);
 void sdb200_comm_destroy(void* comm);
 
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
-/* backend_cuda.h:46-47 conv2d(): im2col + tf32 tensor-core GEMM. */
+/* backend_cuda.h:46-47 conv2d(): x NCHW [N, Cin, H, W], w [Cout, Cin, kh, kw], out NCHW
+ * [N, Cout, Ho, Wo], tf32 tensor cores. Stride 1 runs as an implicit GEMM over an NHWC
+ * copy of x (workspace); other strides as im2col + GEMM. */
 int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
                   int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo);
-/* backend_cuda.h:48-49 group_norm() */
+/* Extension (no reference counterpart): the implicit-GEMM convolution on operands already
+ * in its layouts, for callers that keep activations channels-last.
+ *   conv_pack_input:  x NCHW [N, C, HW] -> xh NHWC [N, HW, cp], tf32-rounded, cp % 4 == 0,
+ *                     zero in channels C..cp-1
+ *   conv_pack_weight: w [Cout, Cin, taps] -> wp [Cout, taps, cq], tf32-rounded,
+ *                     cq = round_up(Cin, 32), zero past Cin
+ *   conv2d_nhwc:      out NCHW = conv(xh, wp) (+bias[Cout]) (+res, same layout as out),
+ *                     stride 1, zero padding pad; xh and wp 16-byte aligned. */
+int sdb200_conv_pack_input(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp);
+int sdb200_conv_pack_weight(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq);
+int sdb200_conv2d_nhwc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                       int64_t cq, int64_t Cout, int64_t kh, int64_t kw, int pad, const float* bias, const float* res,
+                       float* out, int64_t Ho, int64_t Wo);
+/* backend_cuda.h:48-49 group_norm(): split statistics (chunk mean and squared deviations
+ * combined in double per group), then y = x * a[c] + b[c]. */
 int sdb200_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
                       const float* beta, float eps);
 /* backend_cuda.h:50 layer_norm() */

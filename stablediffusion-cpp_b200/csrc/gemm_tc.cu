@@ -45,7 +45,8 @@ constexpr int kGroupM = 16;
 struct ConvGeom {
   int Ho, Wo, BW, BH, tiles_x, tiles_y;
   int kw, pad, cblocks;
-  int b_bytes;             // bytes of one B box (BW * BH rows of 128 B)
+  int b_bytes;             // bytes of one B box (BW * BH rows of 128 B; half of that on SM pairs)
+  int half_dx, half_dy;    // SM pairs: offset of the second CTA's half of the pixel rectangle
   long long img_stride;    // elements between images of the output (Cout * Ho * Wo)
   const float* res;        // residual added in the epilogue (output layout), or null
 };
@@ -636,15 +637,16 @@ struct PairCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + STG_BYTES;
 };
 
+template <bool CONV>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     k_gemm_tc_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p) {
   using C_ = PairCfg;
   constexpr int BN = C_::BN;
   constexpr int STAGES = C_::STAGES;
-  constexpr int BK = 64;
+  constexpr int BK = CONV ? 32 : 64;  // one 128-byte swizzle row of K: tf32 (conv) or bf16
   constexpr int KSTEPS = 4;
-  constexpr uint32_t IDESC = make_idesc(1u /*bf16*/, 0, 0, 2 * kBM, BN);
+  constexpr uint32_t IDESC = make_idesc(CONV ? 2u : 1u, 0, 0, 2 * kBM, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -702,15 +704,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
         int mb, nb;
         tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        int img = 0, oy0 = 0, ox0 = 0;
+        if constexpr (CONV) {
+          conv_tile(p.cv, nb, img, oy0, ox0);
+          oy0 += (int)rank * p.cv.half_dy;  // this CTA's half of the pixel rectangle
+          ox0 += (int)rank * p.cv.half_dx;
+        }
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrWaitEmpty)) {
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);
           const uint32_t fb = full0 + (uint32_t)(stage * 8);
-          tma_load_2d_pair(sA + stage * C_::A_BYTES, &tmA, fb, kb * BK, mb * 2 * kBM + (int)rank * kBM);
-          tma_load_2d_pair(sB + stage * C_::B_BYTES, &tmB, fb, kb * BK, nb * BN + (int)rank * (BN / 2));
+          if constexpr (CONV) {
+            const int tap = kb / p.cv.cblocks, cb = kb - tap * p.cv.cblocks;
+            const int ky = tap / p.cv.kw, kx = tap - ky * p.cv.kw;
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (C_::A_BYTES + p.cv.b_bytes));
+            tma_load_2d_pair(sA + stage * C_::A_BYTES, &tmA, fb, kb * BK, mb * 2 * kBM + (int)rank * kBM);
+            tma_load_4d_pair(sB + stage * C_::B_BYTES, &tmB, fb, cb * 32, ox0 + kx - p.cv.pad, oy0 + ky - p.cv.pad,
+                             img);
+          } else {
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);
+            tma_load_2d_pair(sA + stage * C_::A_BYTES, &tmA, fb, kb * BK, mb * 2 * kBM + (int)rank * kBM);
+            tma_load_2d_pair(sB + stage * C_::B_BYTES, &tmB, fb, kb * BK, nb * BN + (int)rank * (BN / 2));
+          }
           issued |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -753,8 +770,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(sA + stage * C_::A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * C_::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < KSTEPS; ++k)
-            umma_f16_ss_pair(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32), IDESC, (kb | k) != 0);
+          for (int k = 0; k < KSTEPS; ++k) {
+            if constexpr (CONV)
+              umma_tf32_ss_pair(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32), IDESC, (kb | k) != 0);
+            else
+              umma_f16_ss_pair(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32), IDESC, (kb | k) != 0);
+          }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
@@ -789,7 +810,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * 2 * kBM + (int)rank * kBM + q * 32, nb, lane);
+      if constexpr (CONV)
+        epilogue_conv<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * 2 * kBM + (int)rank * kBM + q * 32, nb, lane);
+      else
+        epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * 2 * kBM + (int)rank * kBM + q * 32, nb, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty0 + (uint32_t)(acc * 8));
@@ -813,8 +837,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 int pair_clusters(int dev) {
   static int cached[64] = {};
   if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
-  check_cuda(cudaFuncSetAttribute(k_gemm_tc_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM),
+  check_cuda(cudaFuncSetAttribute(k_gemm_tc_pair<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM),
              "cudaFuncSetAttribute(gemm pair)");
+  check_cuda(cudaFuncSetAttribute(k_gemm_tc_pair<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM),
+             "cudaFuncSetAttribute(conv pair)");
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -827,7 +853,7 @@ int pair_clusters(int dev) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  check_cuda(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc_pair, &cfg), "cudaOccupancyMaxActiveClusters");
+  check_cuda(cudaOccupancyMaxActiveClusters(&n, k_gemm_tc_pair<false>, &cfg), "cudaOccupancyMaxActiveClusters");
   if (n <= 0) fail(kErrUnsupported, "gemm pair kernel: no cluster of 2 fits");
   if (dev >= 0 && dev < 64) cached[dev] = n;
   return n;
@@ -852,7 +878,7 @@ void launch_pair(const GemmCall& g, GemmParams p, int dev, cudaStream_t stream) 
   p.n_tiles = (int)((g.N + C_::BN - 1) / C_::BN);
   p.num_tiles = p.m_tiles * p.n_tiles;
   const int clusters = std::min(pair_clusters(dev), p.num_tiles);
-  k_gemm_tc_pair<<<(unsigned)(2 * clusters), kThreads, C_::SMEM, stream>>>(ta, tb, p);
+  k_gemm_tc_pair<false><<<(unsigned)(2 * clusters), kThreads, C_::SMEM, stream>>>(ta, tb, p);
   check_launch("gemm_tc_pair");
 }
 
@@ -945,13 +971,17 @@ int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
 
 }  // namespace
 
+
+
 // Tile-width override for tuning and tests (0 = automatic choice).
 static int g_forced_bn = 0;
 void set_gemm_tile(int bn) { g_forced_bn = bn; }
 
-// 256 x 256 tiles on CTA pairs (k_gemm_tc_pair) for bf16 GEMMs with 256-column tiles.
-static bool g_gemm_pair = true;
-void set_gemm_pair(bool on) { g_gemm_pair = on; }
+// 256 x 256 tiles on CTA pairs (k_gemm_tc_pair) for bf16 GEMMs with 256-column
+// tiles and for implicit-GEMM convolutions with >= 256 output channels.
+// Mode 0: never; 1: when the cost model prefers them (default); 2: whenever eligible.
+static int g_gemm_pair = 1;
+void set_gemm_pair(int mode) { g_gemm_pair = mode; }
 
 void launch_gemm_tc(const GemmCall& g) {
   DeviceContext& c = ctx();
@@ -997,7 +1027,7 @@ void launch_gemm_tc(const GemmCall& g) {
     const int64_t pair_tiles = ((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + 255) / 256);
     const int64_t clusters = pair_clusters(c.device);
     const double pair_cost = (double)((pair_tiles + clusters - 1) / clusters) * (256 + 48) * 0.92;
-    if (pair_cost <= single_cost) {
+    if (pair_cost <= single_cost || g_gemm_pair == 2) {
       launch_pair(g, p, c.device, c.stream);
       return;
     }
@@ -1018,6 +1048,7 @@ void launch_gemm_tc(const GemmCall& g) {
     }
   }
 }
+
 
 namespace {
 template <int BN>
@@ -1075,9 +1106,29 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
       bh = h_;
     }
   }
-  if (g_forced_bn == 256 || g_forced_bn == 128 || g_forced_bn == 64) {
+  const bool forced = g_forced_bn == 256 || g_forced_bn == 128 || g_forced_bn == 64;
+  if (forced) {
     bn = g_forced_bn;
     conv_rect(bn, Ho, Wo, bw, bh);
+  }
+  // SM pairs (k_gemm_tc_pair<true>): 256 channels x 256 pixels per pair, each CTA loading
+  // 128 channels of the weights and half of the pixel rectangle; same cost model as the
+  // GEMM's pair choice. Needs a full 256-pixel rectangle that splits into two halves.
+  bool pair = false;
+  int pw = 0, ph = 0;
+  if (g_gemm_pair && !forced && Cout >= 2 * kBM) {
+    conv_rect(256, Ho, Wo, pw, ph);
+    if (pw * ph == 256 && (ph % 2 == 0 || pw == 256)) {
+      const int64_t pair_tiles = ((Cout + 2 * kBM - 1) / (2 * kBM)) * N * ((Ho + ph - 1) / ph) * ((Wo + pw - 1) / pw);
+      const int64_t clusters = pair_clusters(c.device);
+      const double pair_cost = (double)((pair_tiles + clusters - 1) / clusters) * (256 + 48) * 0.92;
+      pair = pair_cost <= best || g_gemm_pair == 2;
+    }
+  }
+  if (pair) {
+    bn = 256;
+    bw = pw;
+    bh = ph;
   }
   const int64_t kk = (int64_t)kh * kw * cq;
   CUtensorMap ta, tb;
@@ -1087,10 +1138,14 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
     const uint32_t box[2] = {32, (uint32_t)kBM};
     encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, wp, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   }
+  // On SM pairs each CTA loads half of the rectangle: the top / bottom rows, or the left /
+  // right half of a one-row rectangle.
+  const int hx = (pair && bh == 1) ? bw / 2 : 0, hy = (pair && bh > 1) ? bh / 2 : 0;
+  const int box_w = hx ? bw / 2 : bw, box_h = hy ? bh / 2 : bh;
   {
     const uint64_t dims[4] = {(uint64_t)Cin, (uint64_t)W, (uint64_t)H, (uint64_t)N};
     const uint64_t strides[3] = {(uint64_t)cp * 4, (uint64_t)(W * cp * 4), (uint64_t)(H * W * cp * 4)};
-    const uint32_t box[4] = {32, (uint32_t)bw, (uint32_t)bh, 1};
+    const uint32_t box[4] = {32, (uint32_t)box_w, (uint32_t)box_h, 1};
     encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   }
   GemmParams p{};
@@ -1106,10 +1161,12 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
   p.cv.kw = kw;
   p.cv.pad = pad;
   p.cv.cblocks = (int)(cq / 32);
-  p.cv.b_bytes = bw * bh * 128;
+  p.cv.b_bytes = box_w * box_h * 128;
+  p.cv.half_dx = hx;
+  p.cv.half_dy = hy;
   p.cv.img_stride = Cout * Ho * Wo;
   p.cv.res = res;
-  p.m_tiles = (int)m_tiles;
+  p.m_tiles = pair ? (int)((Cout + 2 * kBM - 1) / (2 * kBM)) : (int)m_tiles;
   p.n_tiles = (int)(N * p.cv.tiles_x * p.cv.tiles_y);
   if ((int64_t)p.m_tiles * p.n_tiles > (1ll << 31) - 1) fail(kErrInvalidArg, "conv_tc: too many tiles");
   p.num_tiles = p.m_tiles * p.n_tiles;
@@ -1122,6 +1179,12 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
                   (!res || (reinterpret_cast<uintptr_t>(res) & 15) == 0);
   p.vec_ok = al && (Ho * Wo) % 4 == 0;
   p.err = c.err_word;
+  if (pair) {
+    const int clusters = std::min(pair_clusters(c.device), p.num_tiles);
+    k_gemm_tc_pair<true><<<(unsigned)(2 * clusters), kThreads, PairCfg::SMEM, c.stream>>>(ta, tb, p);
+    check_launch("conv_tc_pair");
+    return;
+  }
   switch (bn) {
     case 256: launch_conv_bn<256>(ta, tb, p, c.num_sms, c.device, c.stream); break;
     case 128: launch_conv_bn<128>(ta, tb, p, c.num_sms, c.device, c.stream); break;

@@ -131,8 +131,9 @@ void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t
 void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq);
 // Forces the tile width of later launch_gemm_tc calls (0 = automatic).
 void set_gemm_tile(int bn);
-// Enables (default) or disables the CTA-pair kernel for bf16 GEMMs with 256-wide tiles.
-void set_gemm_pair(bool on);
+// CTA-pair kernel for bf16 GEMMs and implicit convolutions: 0 never, 1 by the cost model
+// (default), 2 whenever the shape allows (tests).
+void set_gemm_pair(int mode);
 // Enables (default) or disables the implicit-GEMM path of conv2d for stride 1.
 void set_conv_implicit(bool on);
 // bf16 tcgen05 GEMM on an explicit device / stream / error word; no device context.

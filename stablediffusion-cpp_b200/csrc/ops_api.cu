@@ -287,7 +287,10 @@ int sdb200_set_gemm_tile(int bn) {
 }
 
 int sdb200_set_gemm_pair(int enable) {
-  SDB_GUARD(sdb::set_gemm_pair(enable != 0))
+  SDB_GUARD({
+    require(enable >= 0 && enable <= 2, "set_gemm_pair", "mode must be 0, 1 or 2");
+    sdb::set_gemm_pair(enable);
+  })
 }
 
 int sdb200_set_conv_implicit(int enable) {
@@ -366,6 +369,42 @@ int sdb200_pack_heads_f16(const float* x, void* y, int64_t rows, int heads, int6
 int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
                   int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo) {
   SDB_GUARD(conv2d_impl(x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo))
+}
+int sdb200_conv_pack_input(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
+  SDB_GUARD({
+    const char* op = "conv_pack_input";
+    require(N >= 0 && C > 0 && HW >= 0 && cp >= C && cp % 4 == 0, op, "bad shape (cp must be >= C and % 4 == 0)");
+    require_ptr(x, op, "x");
+    require_ptr(xh, op, "xh");
+    launch_conv_pack_x(x, xh, N, C, HW, cp);
+  })
+}
+int sdb200_conv_pack_weight(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq) {
+  SDB_GUARD({
+    const char* op = "conv_pack_weight";
+    require(Cout > 0 && Cin > 0 && taps > 0 && cq >= Cin && cq % 32 == 0, op,
+            "bad shape (cq must be >= Cin and % 32 == 0)");
+    require_ptr(w, op, "w");
+    require_ptr(wp, op, "wp");
+    launch_conv_pack_w(w, wp, Cout, Cin, taps, cq);
+  })
+}
+int sdb200_conv2d_nhwc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                       int64_t cq, int64_t Cout, int64_t kh, int64_t kw, int pad, const float* bias, const float* res,
+                       float* out, int64_t Ho, int64_t Wo) {
+  SDB_GUARD({
+    const char* op = "conv2d_nhwc";
+    require(N >= 0 && Cin > 0 && H > 0 && W > 0 && Cout > 0 && kh > 0 && kw > 0 && pad >= 0 && Ho >= 0 && Wo >= 0,
+            op, "bad shape");
+    require(cp >= Cin && cp % 4 == 0 && cq >= Cin && cq % 32 == 0, op, "bad packed channel pitch");
+    require_ptr(xh, op, "xh");
+    require_ptr(wp, op, "wp");
+    require_ptr(out, op, "out");
+    require((reinterpret_cast<uintptr_t>(xh) & 15) == 0 && (reinterpret_cast<uintptr_t>(wp) & 15) == 0, op,
+            "xh and wp must be 16-byte aligned");
+    if (N > 0 && Ho > 0 && Wo > 0)
+      launch_conv_tc(xh, N, Cin, cp, H, W, wp, cq, Cout, (int)kh, (int)kw, pad, bias, res, out, Ho, Wo);
+  })
 }
 int sdb200_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
                       const float* beta, float eps) {

@@ -92,6 +92,10 @@ _SIGS = {
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
     "sdb200_comm_destroy": ([_v], None),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
+    "sdb200_conv_pack_input": ([_v, _v, _i64, _i64, _i64, _i64], _i),
+    "sdb200_conv_pack_weight": ([_v, _v, _i64, _i64, _i64, _i64], _i),
+    "sdb200_conv2d_nhwc": ([_v, _i64, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _i64, _i, _v, _v, _v, _i64,
+                            _i64], _i),
     "sdb200_group_norm": ([_v, _v, _i64, _i64, _i64, _i, _v, _v, _f], _i),
     "sdb200_layer_norm": ([_v, _v, _i64, _i64, _v, _v, _f], _i),
     "sdb200_rms_norm": ([_v, _v, _i64, _i64, _v, _f], _i),

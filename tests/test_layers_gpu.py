@@ -140,12 +140,14 @@ def test_conv2d_sd15_shape(sdb, orc):
 @pytest.fixture
 def conv_setup(sdb):
     """Selects the conv2d lowering and GEMM tile width for one test; restores defaults."""
-    def use(implicit, bn=0):
+    def use(implicit, bn=0, pair=1):
         sdb.check(sdb.lib().sdb200_set_conv_implicit(1 if implicit else 0))
         sdb.check(sdb.lib().sdb200_set_gemm_tile(bn))
+        sdb.check(sdb.lib().sdb200_set_gemm_pair(pair))
     yield use
     sdb.check(sdb.lib().sdb200_set_conv_implicit(1))
     sdb.check(sdb.lib().sdb200_set_gemm_tile(0))
+    sdb.check(sdb.lib().sdb200_set_gemm_pair(1))
 
 
 # (N, Cin, H, W, Cout, k, pad): ragged channel counts, Wo below and above 32, batches,
@@ -160,6 +162,8 @@ CONV_CASES = [
     (1, 16, 48, 48, 512, 3, 1),
     (1, 128, 96, 96, 128, 3, 1),
     (2, 256, 24, 24, 128, 1, 0),
+    (1, 64, 5, 300, 256, 3, 1),     # SM pairs: one-row 256-pixel rectangles split left / right
+    (1, 40, 20, 70, 320, 3, 1),     # SM pairs: 128 x 2 rectangles split top / bottom, ragged Cout
 ]
 
 
@@ -177,13 +181,42 @@ def test_conv2d_implicit_gemm(sdb, orc, conv_setup, case):
     want = orc.conv2d(x, w, b, 1, pad)
     conv_setup(False)
     lowered = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 1, pad))
-    for bn in (0, 64, 128, 256):
-        conv_setup(True, bn)
+    # automatic choice, each single-SM tile width, and SM pairs wherever the shape allows
+    for bn, pair in ((0, 1), (64, 1), (128, 1), (256, 1), (0, 2)):
+        conv_setup(True, bn, pair)
         got = _np(sdb.backend.conv2d(_t(x), _t(w), _t(b), 1, pad))
         assert got.shape == want.shape
-        assert rel_fro(got, want) <= 2e-3, bn
+        assert rel_fro(got, want) <= 2e-3, (bn, pair)
         if Cout > 16:  # the lowering's GEMM runs on tf32 tensor cores (exact SIMT for M <= 16)
-            assert rel_fro(got, lowered) <= 1e-5, bn
+            assert rel_fro(got, lowered) <= 1e-5, (bn, pair)
+
+
+def test_conv2d_nhwc_packed_with_residual(sdb, orc):
+    """The packed-operand entry points: pack x (channel pitch above C) and w once, then
+    out = conv + bias + res in one kernel; res is read in the output layout."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    N, Cin, H, W, Cout = 2, 37, 19, 45, 70
+    x = rng.standard_normal((N, Cin, H, W)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((Cout, Cin, 3, 3))).astype(np.float32)
+    b = (0.05 * rng.standard_normal(Cout)).astype(np.float32)
+    res = rng.standard_normal((N, Cout, H, W)).astype(np.float32)
+    want = orc.conv2d(x, w, b, 1, 1) + res
+    cp, cq = 40, 64
+    L = sdb.lib()
+    xd, wd, bd, rd = _t(x), _t(w), _t(b), _t(res)
+    xh = torch.empty(N * H * W * cp, device="cuda")
+    wp = torch.empty(Cout * 9 * cq, device="cuda")
+    out = torch.empty((N, Cout, H, W), device="cuda")
+    sdb.check(L.sdb200_conv_pack_input(xd.data_ptr(), xh.data_ptr(), N, Cin, H * W, cp))
+    sdb.check(L.sdb200_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), Cout, Cin, 9, cq))
+    sdb.check(L.sdb200_conv2d_nhwc(xh.data_ptr(), N, Cin, cp, H, W, wp.data_ptr(), cq, Cout, 3, 3, 1, bd.data_ptr(),
+                                   rd.data_ptr(), out.data_ptr(), H, W))
+    assert rel_fro(_np(out), want) <= 2e-3
+    # a channel pitch that is not a multiple of 4 is refused before any launch
+    assert L.sdb200_conv2d_nhwc(xh.data_ptr(), N, Cin, 38, H, W, wp.data_ptr(), cq, Cout, 3, 3, 1, None, None,
+                                out.data_ptr(), H, W) != 0
 
 
 def test_conv2d_strided_uses_im2col(sdb, orc):
