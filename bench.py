@@ -1,7 +1,7 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dit|dit_tp|gemm|attention|conv]
+                    [--workload dit|dit_tp|gemm|attention|conv|vae]
 
 Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
 random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
@@ -21,6 +21,9 @@ rank over NVLink, sequence-sharded post-norm) or by an NCCL all-reduce (--tp-mod
 
 Workload `conv`: the VAE decoder's 3x3 convolutions at the four resolution stages of a
 1024^2 decode (512@128^2, 512@256^2, 256@512^2, 128@1024^2), TFLOP/s through conv2d.
+
+Workload `vae`: one FLUX / Z-Image VAE decode of a 1024x1024 image on the device
+(sdb200_vae_decode), ms per decode.
 
 Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
 128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
@@ -272,6 +275,27 @@ def run_reference(args, world, rank):
                                  "sample": f"one full-width block forward per step ({dt:.2f} s), scaled by FLOPs "
                                            f"({sample_flop / 1e12:.2f} -> {step_flop / 1e12:.0f} TFLOP)"},
                 "e2e": {"value": ms, "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    elif args.workload == "vae":
+        from sdb200.vae import FLUX_VAE, decode_flops
+
+        fn, f0, cores, _keep = ref_vae_sample()
+        FLOP = decode_flops(FLUX_VAE, LAT_H, LAT_W)
+        for _ in range(min(args.warmup, 1)):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        dt = (time.perf_counter() - t0) / args.steps
+        ms = dt * 1e3 * FLOP / f0
+        line = {"impl": "reference", "metric": "VAE decode ms (1024^2 image, FLUX / Z-Image VAE)", "value": ms,
+                "unit": "ms/decode", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU)",
+                "data": "synthetic (random-init weights, N(0,1) latent)",
+                "config": {"workload": "AutoencoderKL decoder, latent 16x128x128 -> 3x1024x1024",
+                           "sample": "a 256^2 decode per step, scaled by FLOPs"},
+                "cpu_baseline": {"value": ms, "unit": "ms/decode", "cores": cores, "kind": "reference",
+                                 "sample": f"VAEDecoder::decode of a 256^2 image per step ({dt:.2f} s), FLOP-scaled"},
+                "e2e": {"value": ms, "unit": "ms/decode", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     elif args.workload == "conv":
         fn, flop, cores = ref_conv_sample()
         for _ in range(min(args.warmup, 1)):
@@ -787,13 +811,123 @@ def run_conv(args, world, rank, local, pg, dev):
             "cpu_baseline": cpu, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
 
 
+def ref_vae_sample(side=32):
+    """The reference's VAEDecoder::decode (vae.cpp:35-51) with the FLUX / Z-Image VAE's
+    widths on a side x side latent (a 8*side image), random-init weights."""
+    import numpy as np
+
+    from oracle import RefCPU
+    from sdb200.vae import FLUX_VAE, decode_flops, random_weights
+
+    ref = RefCPU()
+    ref.set_num_threads(0)
+    m = ref.vae(random_weights(FLUX_VAE, 7), FLUX_VAE.scaling_factor, FLUX_VAE.shift_factor)
+    z = np.random.default_rng(8).standard_normal((1, FLUX_VAE.latent_channels, side, side)).astype(np.float32)
+    return (lambda: m(z)), decode_flops(FLUX_VAE, side, side), ref.num_threads(), m
+
+
+def run_vae(args, world, rank, local, pg, dev):
+    """One step = one VAE decode of a 1024^2 image (latent [1, 16, 128, 128] -> [1, 3, 1024,
+    1024]) through sdb200_vae_decode, per GPU (replicas). value = ms per decode."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+    from sdb200.vae import FLUX_VAE, VAE, decode_flops, random_weights
+
+    L = sdb200.lib()
+    cfg = FLUX_VAE
+    side = LAT_H
+    FLOP = decode_flops(cfg, side, side)
+    v = VAE(cfg, random_weights(cfg, 7))
+    g = torch.Generator(device=dev)
+    g.manual_seed(9 + rank)
+    z = torch.randn((1, cfg.latent_channels, side, side), generator=g, device=dev)
+    out = torch.empty((1, 3, side * v.upscale, side * v.upscale), device=dev)
+    stream = torch.cuda.current_stream()
+    step = lambda: v.decode(z, out)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_loop(step, args.steps, stream, pg, dev)
+    launches = L.sdb200_launch_count() - n0
+    # one profiled decode: convolution kernels alone (CUDA events around each launch)
+    sdb200.check(L.sdb200_vae_profile(v.h, 1))
+    step()
+    prof = (C.c_double * 5)()
+    sdb200.check(L.sdb200_vae_profile_read(v.h, prof))
+    sdb200.check(L.sdb200_vae_profile(v.h, 0))
+    conv_ms, conv_flop, conv_n, att_ms, att_flop = list(prof)
+    # cuBLAS tf32 rate measured on the same stream as the denominator
+    allow = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    A = torch.randn((8192, 8192), device=dev)
+    B = torch.randn((8192, 8192), device=dev)
+    for _ in range(3):
+        torch.matmul(A, B)
+    tms = min(timed_loop(lambda: torch.matmul(A, B), 5, stream, None, dev) / 5 for _ in range(2))
+    torch.backends.cuda.matmul.allow_tf32 = allow
+    tf32_peak = 2.0 * 8192 ** 3 / (tms * 1e-3) / 1e12
+    del A, B
+    zh = z.cpu().pin_memory()
+    oh = torch.empty(out.shape).pin_memory()
+    zd = torch.empty_like(z)
+
+    def e2e_step():
+        sdb200.check(L.sdb200_upload(zd.data_ptr(), zh.data_ptr(), zh.numel() * 4))
+        v.decode(zd, out)
+        sdb200.check(L.sdb200_download(oh.data_ptr(), out.data_ptr(), oh.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            fn, f0, cores, _keep = ref_vae_sample()
+            t0 = time.perf_counter()
+            fn()
+            dt = time.perf_counter() - t0
+            cpu = {"value": dt * 1e3 * FLOP / f0, "unit": "ms/decode", "cores": cores, "kind": "reference",
+                   "sample": f"reference VAEDecoder::decode of a 256^2 image ({f0 / 1e12:.2f} TFLOP, {dt:.2f} s), "
+                             f"scaled by FLOPs to 1024^2 ({FLOP / 1e12:.2f} TFLOP)"}
+        except Exception as e:  # reported, never required
+            cpu = {"value": None, "unit": None, "cores": None, "kind": "reference", "sample": f"failed: {e}"}
+    if rank == 0:
+        achieved = conv_flop / (conv_ms * 1e-3) / 1e12
+        per = ms / args.steps
+        print(json.dumps({
+            "metric": "VAE decode ms (1024^2 image, FLUX / Z-Image VAE)", "value": per, "unit": "ms/decode",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "tflops": FLOP / (per * 1e-3) / 1e12,
+            "dtype": "f32 activations and weights, tf32 tensor cores, f32 accumulate",
+            "data": "synthetic (random-init weights, N(0,1) latent)",
+            "config": {"workload": "AutoencoderKL decoder (16 latent ch, widths 128/256/512/512, 3 resnets per up "
+                                   "block, 1-head mid attention), latent 16x128x128 -> 3x1024x1024",
+                       "parallelism": f"replicas x{world}", "l2": "activations up to 1 GB per layer > 126 MB L2"},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "implicit-GEMM conv (k_gemm_tc_pair<conv>, k_gemm_tc<256,tf32,conv>)",
+                         "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s", "frac": achieved / tf32_peak,
+                         "peak_kind": "cuBLAS tf32 8192^3 measured live in this run (burst)",
+                         "conv_ms": conv_ms, "conv_launches": int(conv_n), "attention_ms": att_ms,
+                         "attention_tflops": att_flop / (att_ms * 1e-3) / 1e12 if att_ms else None,
+                         "traffic": None},
+            "e2e": {"value": e2e_ms / args.steps, "unit": "ms/decode", "h2d_bytes_per_step": int(zh.numel() * 4),
+                    "d2h_bytes_per_step": int(oh.numel() * 4)},
+            "cpu_baseline": cpu, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention", "conv"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--conv-stage", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
                     help="conv: run only this stage of the VAE-decoder stack (-1: all four)")
@@ -830,6 +964,8 @@ def main():
         run_dit_tp(args, world, rank, local, pg, dev)
     elif args.workload == "conv":
         run_conv(args, world, rank, local, pg, dev)
+    elif args.workload == "vae":
+        run_vae(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:

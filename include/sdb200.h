@@ -142,7 +142,9 @@ int sdb200_set_conv_implicit(int enable);
 /* ---- attention ------------------------------------------------------------------- */
 /* backend_cuda.h:58-59 attention(): q [N, Sq, heads*d]; k, v [N, Skv, kv_heads*d];
  * out [N, Sq, heads*d]; softmax(q k^T / sqrt(d)) v per head, query head h reads kv
- * head h / (heads / kv_heads); causal keeps keys j <= query row i. */
+ * head h / (heads / kv_heads); causal keeps keys j <= query row i. Head dims <= 128 run
+ * on the flash kernel (fp16 operands), larger ones as tf32 GEMM -> softmax -> tf32 GEMM
+ * in query-row chunks (the reference GPU backend's scheme on tensor cores). */
 int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                      int heads, int kv_heads, int64_t d, int causal);
 
@@ -153,8 +155,8 @@ int sdb200_attention_f16(const void* q, const void* k, const void* v, void* out,
                          int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp, int causal);
 /* fp32 x [rows, heads*d] -> fp16 y [rows, heads, dp] (zero padded, |x| > 65504 saturates). */
 int sdb200_pack_heads_f16(const float* x, void* y, int64_t rows, int heads, int64_t d, int64_t dp);
-/* Extension (no reference counterpart): 0 = tensor-core attention (fp16 operands,
- * fp32 accumulation and softmax; head dims <= 128), 1 = exact fp32 streaming kernel.
+/* Extension (no reference counterpart): 0 = tensor-core attention (flash kernel on fp16
+ * operands for head dims <= 128, tf32 GEMMs above), 1 = exact fp32 streaming kernel.
  * Applies to later sdb200_attention calls of this process. */
 int sdb200_set_attention_path(int path);
 
@@ -222,6 +224,31 @@ int sdb200_safetensors_read(const char* path, const char* name, int keep_bf16, i
 /* FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127) on the host: sigmas[0..steps],
  * bit-identical to the reference's values. */
 int sdb200_flow_sigmas(int steps, float shift, float* sigmas);
+
+/* ---- the VAE decoder on the device (vae.cpp:13-51) ------------------------------- */
+/* Extension (no reference counterpart): AutoencoderKL decode as one device program on the
+ * implicit-GEMM convolution, with GroupNorm + SiLU, upsampling, the latent un-scaling and
+ * residual adds folded into the convolutions' operand packing and epilogues.
+ *   vae_create:     scaling_factor / shift_factor from the VAE's config.json
+ *   vae_set_weight: fp32 device tensors under the checkpoint names ("decoder.*",
+ *                   "post_quant_conv.*"); the caller keeps them alive
+ *   vae_load:       or read <dir>/<base>.safetensors (or its shards) as fp32, as
+ *                   Weights::load_model does for the VAE (pipeline.cpp:86)
+ *   vae_finalize:   binds the layers (block counts and widths from the names, as the
+ *                   VAEDecoder constructor, vae.cpp:15-32) and packs the conv weights
+ *   vae_decode:     latents [N, C, h, w] (device) -> out [N, 3, h * upscale, w * upscale]
+ * Returns NULL / a status code; the decoder owns its activation buffers. */
+void* sdb200_vae_create(float scaling_factor, float shift_factor);
+int sdb200_vae_set_weight(void* m, const char* name, const float* dev_ptr, const int64_t* shape, int ndim);
+int sdb200_vae_load(void* m, const char* dir, const char* base);
+int sdb200_vae_finalize(void* m);
+int sdb200_vae_info(void* m, int64_t* latent_channels, int64_t* out_channels, int64_t* upscale);
+int sdb200_vae_decode(void* m, const float* latents, int64_t N, int64_t C, int64_t h, int64_t w, float* out);
+/* Tuning extension: CUDA-event timing of later decodes (on != 0); profile_read returns
+ * conv ms, conv FLOPs, conv launches, attention ms, attention FLOPs and clears. */
+int sdb200_vae_profile(void* m, int on);
+int sdb200_vae_profile_read(void* m, double* out5);
+void sdb200_vae_destroy(void* m);
 
 /* ---- tensor-parallel communicator (NCCL over NVLink / NVSwitch, loaded at run time) -- */
 /* Writes a 128-byte unique id (on one rank; share it with the others out of band). */

@@ -282,6 +282,9 @@ class RefCPU(_Base):
                                             C.c_int], v)
         self.z_free = self.fn("zimage_free", [v])
         self.z_fwd = self.fn("zimage_forward", [v, v, _i64, _i64, _i64, C.c_float, v, _i64, _i64, v], C.c_int)
+        self.v_new = self.fn("vae_new", [v, C.c_float, C.c_float], v)
+        self.v_free = self.fn("vae_free", [v])
+        self.v_dec = self.fn("vae_decode", [v, v, _i64, _i64, _i64, _i64, v, _i64, v], C.c_int)
 
     def _chk(self, rc):
         if rc:
@@ -429,6 +432,40 @@ class RefCPU(_Base):
             self.w_free(w)
             raise RuntimeError(self.last_error().decode())
         return self._wrap_model(m, w)
+
+    def vae(self, weights: dict, scaling_factor: float, shift_factor: float):
+        """Builds the reference VAEDecoder (vae.cpp:15-32) over `weights` (name -> fp32
+        array). Returns a callable f(z [N,C,h,w]) -> image [N,3,H,W] running
+        VAEDecoder::decode (vae.cpp:35-51) on the CPU."""
+        w = self.w_new()
+        for name, arr in weights.items():
+            arr = np.ascontiguousarray(arr, np.float32)
+            shape = (C.c_int64 * arr.ndim)(*arr.shape)
+            self._chk(self.w_add(w, name.encode(), C.cast(shape, C.c_void_p), arr.ndim, _ptr(arr), 0))
+        m = self.v_new(w, scaling_factor, shift_factor)
+        if not m:
+            self.w_free(w)
+            raise RuntimeError(self.last_error().decode())
+        ref = self
+
+        class _Vae:
+            def __call__(self, z):
+                z = np.ascontiguousarray(z, np.float32)
+                cap = z.size * 64 * 4  # room for up to 8x upscaling to 4 channels
+                out = np.empty(cap, np.float32)
+                shp = (C.c_int64 * 4)()
+                ref._chk(ref.v_dec(m, _ptr(z), *z.shape, _ptr(out), cap, C.cast(shp, C.c_void_p)))
+                n = int(np.prod(list(shp)))
+                return out[:n].reshape(tuple(shp)).copy()
+
+            def __del__(self):
+                try:
+                    ref.v_free(m)
+                    ref.w_free(w)
+                except Exception:
+                    pass
+
+        return _Vae()
 
     def _wrap_model(self, m, w):
         ref = self

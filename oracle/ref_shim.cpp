@@ -15,6 +15,7 @@
 #include "safetensors.h"
 #include "scheduler.h"
 #include "tensor.h"
+#include "vae.h"
 #include "zimage.h"
 
 using namespace sd;
@@ -186,6 +187,27 @@ int sdref_zimage_forward(void* m, const float* x, int64_t C, int64_t H, int64_t 
     Tensor tx = make(x, {1, C, H, W});
     Tensor tc = make(cap, {1, L, capdim});
     put(static_cast<ZImageTransformer*>(m)->forward(tx, t, tc), out);
+  });
+}
+
+// ---- VAE decoder (vae.cpp) on an in-memory Weights (sdref_weights_new / _add, fp32) --
+void* sdref_vae_new(void* w, float scaling_factor, float shift_factor) {
+  try {
+    return new VAEDecoder(*static_cast<Weights*>(w), scaling_factor, shift_factor);
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void sdref_vae_free(void* m) { delete static_cast<VAEDecoder*>(m); }
+// latents [N, C, h, w] -> out (capacity out_cap floats); shape4 receives the output shape.
+int sdref_vae_decode(void* m, const float* z, int64_t N, int64_t C, int64_t h, int64_t w, float* out, int64_t out_cap,
+                     int64_t* shape4) {
+  return guard([&] {
+    Tensor y = static_cast<VAEDecoder*>(m)->decode(make(z, {N, C, h, w}));
+    if (y.ndim() != 4 || y.numel() > out_cap) throw std::runtime_error("sdref_vae_decode: output buffer too small");
+    for (int i = 0; i < 4; ++i) shape4[i] = y.dim(i);
+    put(y, out);
   });
 }
 

@@ -119,7 +119,10 @@ void launch_attention_simt(const float* q, const float* k, const float* v, float
     case 5: return launch_simt<5>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
     case 6: return launch_simt<6>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
     case 7: return launch_simt<7>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
-    default: return launch_simt<8>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 8: return launch_simt<8>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 9: case 10: case 11: case 12: return launch_simt<12>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    case 13: case 14: case 15: case 16: return launch_simt<16>(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    default: fail(kErrInvalidArg, "attention: the exact fp32 kernel takes head dims up to 512");
   }
 }
 

@@ -527,14 +527,16 @@ void launch_pack_heads_f16(const float* x, void* y, int64_t rows, int H, int64_t
 }
 
 // Drop-in attention (backend_cuda.h:58-59): fp32 q/k/v/out [N, S, heads*d].
-// Head dims up to 128 run on the tensor-core kernel (operands packed to fp16 in the
-// workspace); larger head dims use the exact fp32 streaming kernel.
+// Head dims up to 128 run on the flash kernel (operands packed to fp16 in the
+// workspace); larger head dims on tf32 GEMMs around a softmax (attention_gemm.cu).
+// set_attention_tc(false) selects the exact fp32 streaming kernel for every head dim.
 static bool g_attention_tc = true;
 void set_attention_tc(bool on) { g_attention_tc = on; }
 
 void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                       int heads, int kv_heads, int64_t d, bool causal) {
-  if (!g_attention_tc || d > 128) return launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+  if (!g_attention_tc) return launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+  if (d > 128) return launch_attention_gemm(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
   const int64_t dp = d <= 64 ? 64 : 128;
   const size_t qb = (size_t)(N * Sq * heads * dp) * 2, kb = (size_t)(N * Skv * kv_heads * dp) * 2;
   auto a256 = [](size_t b) { return (b + 255) & ~size_t(255); };

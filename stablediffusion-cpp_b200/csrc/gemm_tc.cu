@@ -38,7 +38,8 @@ constexpr int kGroupM = 16;
 
 // Implicit-GEMM convolution, stride 1: out[img, co, oy, ox] = sum over taps (ky, kx) and
 // channels ci of w[co, ky, kx, ci] * x[img, oy - pad + ky, ox - pad + kx, ci] (+ bias[co])
-// (+ res[img, co, oy, ox]). GEMM rows are output channels; a tile's BN columns are a
+// (+ res[img, co, oy, ox]; res may be the output itself: each element is read, then
+// written, by one thread). GEMM rows are output channels; a tile's BN columns are a
 // BW x BH rectangle of output pixels of one image (column j -> (oy0 + j / BW, ox0 + j % BW)).
 // One K block is 32 channels of one tap, loaded as a 4-D TMA box of the NHWC input that the
 // hardware zero-fills outside the image (the padding).
@@ -413,14 +414,14 @@ __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, u
       if (vec) {
         float4 o = *reinterpret_cast<const float4*>(src);
         if (res) {
-          const float4 a4 = __ldg(reinterpret_cast<const float4*>(res + off));
+          const float4 a4 = *reinterpret_cast<const float4*>(res + off);  // may alias out: no .nc load
           o.x += a4.x; o.y += a4.y; o.z += a4.z; o.w += a4.w;
         }
         *reinterpret_cast<float4*>(out + off) = o;
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (c4 + e < n) out[off + e] = res ? src[e] + __ldg(res + off + e) : src[e];
+          if (c4 + e < n) out[off + e] = res ? src[e] + res[off + e] : src[e];
       }
     }
     __syncwarp();

@@ -125,6 +125,15 @@ void launch_gemm_tc(const GemmCall& g);
 void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
                     int64_t cq, int64_t Cout, int kh, int kw, int pad, const float* bias, const float* res, float* out,
                     int64_t Ho, int64_t Wo);
+// NCHW [N, C, H, W] -> NHWC [N, Ho*Wo, cp] tf32, zero past C, with y = x * a + b per
+// channel (ab[n * C + c] = (a, b), or the constants a0, b0 when ab is null), then SiLU if
+// silu; with up2 the output is the nearest 2x upsampling (Ho = 2H, Wo = 2W).
+void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H, int64_t W, int64_t cp,
+                      const float2* ab, float a0, float b0, bool silu, bool up2);
+// GroupNorm statistics of x [N, C, HW] as a per-(sample, channel) scale and shift:
+// ab[n * C + c] = (rstd * gamma[c], beta[c] - mean * rstd * gamma[c]).
+void gn_scale_shift(const float* x, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                    const float* beta, float eps, float2* ab);
 // NCHW fp32 [N, C, HW] -> NHWC [N, HW, cp], rounded to tf32, zero in channels C..cp-1.
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp);
 // Conv weights [Cout, Cin, taps] -> [Cout, taps, cq], rounded to tf32, zero past Cin.
@@ -158,6 +167,22 @@ void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const flo
 void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
 void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);
 void op_softmax_rows(float*, int64_t, int64_t, float, bool, int64_t);
+// Softmax rows ld elements apart; causal row index = row0 + r % rows_per_head; with
+// round_out the probabilities are stored rounded to tf32.
+void op_softmax_rows_ex(float* x, int64_t rows, int64_t cols, int64_t ld, float scale, bool causal,
+                        int64_t rows_per_head, int64_t row0, bool round_out);
+// dst[c, r] = tf32(src[r, c]), rows x cols.
+void launch_transpose_tf32(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols);
+// tf32 tensor-core GEMM on operands already rounded to tf32, 16-byte aligned, with
+// leading dimensions that are multiples of 4: C[M,N] = A[M,K] B[N,K]^T (+bias) (+C).
+void gemm_tf32_direct(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                      float* C, int64_t ldc, const float* bias, bool acc);
+// Attention for any head dim as GEMM -> softmax -> GEMM on tf32 tensor cores. Row strides
+// (elements) default to heads * d for q / out and kv_heads * d for k / v; a sample's rows
+// are contiguous (sample stride = rows * stride).
+void launch_attention_gemm(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
+                           int64_t Skv, int heads, int kv_heads, int64_t d, bool causal, int64_t q_ld = 0,
+                           int64_t kv_ld = 0, int64_t o_ld = 0);
 void op_geglu(const float*, float*, int64_t, int64_t);
 void op_swiglu(const float*, const float*, float*, int64_t);
 void op_unary(float*, int64_t, int);  // 0 silu, 1 gelu (erf), 2 quick_gelu, 3 tanh

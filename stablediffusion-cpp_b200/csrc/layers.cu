@@ -102,11 +102,19 @@ __global__ void k_pack_tf32(const float* __restrict__ src, int64_t ld, float* __
 }
 // NCHW -> NHWC (channel pitch cp) through a 32-channel x 128-pixel shared-memory tile:
 // 128-byte reads along pixels (16 in flight per thread), 128-byte writes along channels;
-// tf32-rounded, zero past C.
+// tf32-rounded, zero past C. On the way each value may be transformed, in this order:
+//   y = x * a + b    per channel (a, b) = ab[n * C + c] (GroupNorm), or the constants
+//                    (a0, b0) when ab is null (the VAE's latent un-scaling)
+//   y = silu(y)      when silu != 0 (y / (1 + e^-y), tensor.cpp:843-849)
+// With UP, the output is the nearest-neighbour 2x upsampling of x (tensor.cpp:982-990):
+// output pixel (oy, ox) of the 2H x 2W image reads input (oy / 2, ox / 2).
 constexpr int kPackPx = 128;
-__global__ void __launch_bounds__(256) k_conv_pack_x(const float* __restrict__ x, float* __restrict__ xh, int64_t C,
-                                                     int64_t HW, int64_t cp) {
+template <bool UP>
+__global__ void __launch_bounds__(256) k_pack_nhwc(const float* __restrict__ x, float* __restrict__ xh, int64_t C,
+                                                   int64_t H, int64_t W, int64_t cp, const float2* __restrict__ ab,
+                                                   float a0, float b0, int silu) {
   __shared__ float tile[32][kPackPx + 1];
+  const int64_t Wo = UP ? 2 * W : W, HWo = (UP ? 2 * H : H) * Wo, HWs = H * W;
   const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * kPackPx, c0 = (int64_t)blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
   float v[4][kPackPx / 32];
@@ -116,20 +124,37 @@ __global__ void __launch_bounds__(256) k_conv_pack_x(const float* __restrict__ x
 #pragma unroll
     for (int j = 0; j < kPackPx / 32; ++j) {
       const int64_t p = p0 + tx + 32 * j;
-      v[i][j] = (c < C && p < HW) ? __ldg(x + (n * C + c) * HW + p) : 0.0f;
+      int64_t src = p;
+      if (UP) {
+        const int64_t oy = p / Wo, ox = p - oy * Wo;
+        src = (oy >> 1) * W + (ox >> 1);
+      }
+      v[i][j] = (c < C && p < HWo) ? __ldg(x + (n * C + c) * HWs + src) : 0.0f;
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 4; ++i) {
+    const int64_t c = c0 + ty + 8 * i;
+    float a = a0, b = b0;
+    if (ab && c < C) {
+      const float2 t = ab[n * C + c];
+      a = t.x;
+      b = t.y;
+    }
 #pragma unroll
-    for (int j = 0; j < kPackPx / 32; ++j) tile[ty + 8 * i][tx + 32 * j] = round_tf32(v[i][j]);
+    for (int j = 0; j < kPackPx / 32; ++j) {
+      float y = v[i][j] * a + b;
+      if (silu) y = y / (1.0f + expf(-y));
+      tile[ty + 8 * i][tx + 32 * j] = c < C ? round_tf32(y) : 0.0f;
+    }
+  }
   __syncthreads();
   const int64_t c = c0 + tx;
   if (c >= cp) return;
 #pragma unroll 4
   for (int i = 0; i < kPackPx / 8; ++i) {
     const int64_t p = p0 + ty + 8 * i;
-    if (p < HW) xh[(n * HW + p) * cp + c] = tile[tx][ty + 8 * i];
+    if (p < HWo) xh[(n * HWo + p) * cp + c] = tile[tx][ty + 8 * i];
   }
 }
 __global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ wp, int64_t Cin, int64_t taps,
@@ -403,12 +428,14 @@ __global__ void k_rope(float* __restrict__ x, int64_t NS, int64_t S, int64_t inn
   }
 }
 
-// Scaled, max-subtracted softmax per row; causal rows keep (r % rows_per_head) + 1
-// entries and zero the rest (tensor.cpp:752-769).
-__global__ void k_softmax_rows(float* __restrict__ x, int64_t cols, float scale, int causal, int64_t rows_per_head) {
+// Scaled, max-subtracted softmax per row; causal rows keep (row0 + r % rows_per_head) + 1
+// entries and zero the rest (tensor.cpp:752-769). Rows are ld apart; with round_out the
+// probabilities are stored rounded to tf32 (the A operand of a tf32 GEMM).
+__global__ void k_softmax_rows(float* __restrict__ x, int64_t cols, int64_t ld, float scale, int causal,
+                               int64_t rows_per_head, int64_t row0, int round_out) {
   __shared__ float red[32];
-  float* p = x + (int64_t)blockIdx.x * cols;
-  const int64_t r = (int64_t)blockIdx.x % rows_per_head;
+  float* p = x + (int64_t)blockIdx.x * ld;
+  const int64_t r = row0 + (int64_t)blockIdx.x % rows_per_head;
   const int64_t valid = causal ? min(cols, r + 1) : cols;
   float m = -INFINITY;
   for (int64_t j = threadIdx.x; j < valid; j += blockDim.x) m = fmaxf(m, p[j] * scale);
@@ -420,7 +447,29 @@ __global__ void k_softmax_rows(float* __restrict__ x, int64_t cols, float scale,
     s += e;
   }
   const float inv = 1.0f / block_sum(s, red);
-  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) p[j] = j < valid ? p[j] * inv : 0.0f;
+  for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) {
+    const float o = j < valid ? p[j] * inv : 0.0f;
+    p[j] = round_out ? round_tf32(o) : o;
+  }
+}
+// dst[c, r] = tf32(src[r, c]) for a rows x cols block (ld_src, ld_dst in elements), through
+// a 32 x 32 shared-memory tile.
+__global__ void k_transpose_tf32(const float* __restrict__ src, int64_t ld_src, float* __restrict__ dst,
+                                 int64_t ld_dst, int64_t rows, int64_t cols) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + ty + 8 * i, c = c0 + tx;
+    tile[ty + 8 * i][tx] = (r < rows && c < cols) ? round_tf32(__ldg(src + r * ld_src + c)) : 0.0f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t c = c0 + ty + 8 * i, r = r0 + tx;
+    if (c < cols && r < rows) dst[c * ld_dst + r] = tile[tx][ty + 8 * i];
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -543,10 +592,19 @@ void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, 
   check_launch("pack_bf16");
 }
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
-  if (N <= 0 || HW <= 0) return;
-  const dim3 grid((unsigned)((HW + kPackPx - 1) / kPackPx), (unsigned)((cp + 31) / 32), (unsigned)N);
-  k_conv_pack_x<<<grid, dim3(32, 8), 0, ctx().stream>>>(x, xh, C, HW, cp);
-  check_launch("conv_pack_x");
+  launch_pack_nhwc(x, xh, N, C, 1, HW, cp, nullptr, 1.0f, 0.0f, false, false);
+}
+void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H, int64_t W, int64_t cp,
+                      const float2* ab, float a0, float b0, bool silu, bool up2) {
+  if (N <= 0 || H <= 0 || W <= 0) return;
+  if (N > 65535 || (cp + 31) / 32 > 65535) fail(kErrInvalidArg, "pack_nhwc: too many samples or channels");
+  const int64_t HWo = (up2 ? 4 : 1) * H * W;
+  const dim3 grid((unsigned)((HWo + kPackPx - 1) / kPackPx), (unsigned)((cp + 31) / 32), (unsigned)N);
+  if (up2)
+    k_pack_nhwc<true><<<grid, dim3(32, 8), 0, ctx().stream>>>(x, xh, C, H, W, cp, ab, a0, b0, silu ? 1 : 0);
+  else
+    k_pack_nhwc<false><<<grid, dim3(32, 8), 0, ctx().stream>>>(x, xh, C, H, W, cp, ab, a0, b0, silu ? 1 : 0);
+  check_launch("pack_nhwc");
 }
 void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq) {
   const int64_t total = Cout * taps * cq;
@@ -597,21 +655,27 @@ void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 }
 
 // Public layer ops (called from runtime.cu's C ABI after argument checks).
-void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
-                   const float* beta, float eps, bool silu) {
-  if (N <= 0 || C <= 0 || HW <= 0) return;
+void gn_scale_shift(const float* x, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                    const float* beta, float eps, float2* ab) {
   const int64_t segs = N * groups, len = (C / groups) * HW;
   const int64_t chunks = (len + kGnChunk - 1) / kGnChunk;
-  if (segs > 65535 || N * C > 65535 || chunks > (1ll << 31) - 1)
-    fail(kErrInvalidArg, "group_norm: too many samples or channels");
-  const size_t pb = ((size_t)(segs * chunks) * sizeof(float2) + 255) & ~(size_t)255;
-  uint8_t* ws = static_cast<uint8_t*>(pool_malloc(pb + (size_t)(N * C) * sizeof(float2)));
-  float2* part = reinterpret_cast<float2*>(ws);
-  float2* ab = reinterpret_cast<float2*>(ws + pb);
+  if (segs > 65535 || chunks > (1ll << 31) - 1) fail(kErrInvalidArg, "group_norm: too many samples or groups");
+  float2* part = static_cast<float2*>(pool_malloc((size_t)(segs * chunks) * sizeof(float2)));
   cudaStream_t st = ctx().stream;
   k_gn_stats<<<dim3((unsigned)chunks, (unsigned)segs), kGnThreads, 0, st>>>(x, len, (int)chunks, part);
   k_gn_finalize<<<(unsigned)((segs + 7) / 8), 256, 0, st>>>(part, (int)chunks, len, C, groups, gamma, beta, eps, ab,
                                                             segs);
+  check_launch("group_norm_stats");
+  pool_free(part);  // stream-ordered reuse
+}
+void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
+                   const float* beta, float eps, bool silu) {
+  if (N <= 0 || C <= 0 || HW <= 0) return;
+  if (N * C > 65535) fail(kErrInvalidArg, "group_norm: too many samples x channels");
+  float2* ab = static_cast<float2*>(pool_malloc((size_t)(N * C) * sizeof(float2)));
+  uint8_t* ws = reinterpret_cast<uint8_t*>(ab);
+  cudaStream_t st = ctx().stream;
+  gn_scale_shift(x, N, C, HW, groups, gamma, beta, eps, ab);
   const bool vec = HW % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   const int64_t per_row = vec ? HW / 4 : HW;
   const unsigned bx = (unsigned)std::max<int64_t>(1, std::min<int64_t>((per_row + 4 * 256 - 1) / (4 * 256), 64));
@@ -643,9 +707,20 @@ void op_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const f
   check_launch("rope");
 }
 void op_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, bool causal, int64_t rows_per_head) {
-  if (rows <= 0) return;
-  k_softmax_rows<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, cols, scale, causal ? 1 : 0, rows_per_head);
+  op_softmax_rows_ex(x, rows, cols, cols, scale, causal, rows_per_head, 0, false);
+}
+void op_softmax_rows_ex(float* x, int64_t rows, int64_t cols, int64_t ld, float scale, bool causal,
+                        int64_t rows_per_head, int64_t row0, bool round_out) {
+  if (rows <= 0 || cols <= 0) return;
+  k_softmax_rows<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, cols, ld, scale, causal ? 1 : 0, rows_per_head, row0,
+                                                          round_out ? 1 : 0);
   check_launch("softmax_rows");
+}
+void launch_transpose_tf32(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return;
+  const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32));
+  k_transpose_tf32<<<grid, dim3(32, 8), 0, ctx().stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  check_launch("transpose_tf32");
 }
 void op_geglu(const float* x, float* y, int64_t rows, int64_t D) {
   if (rows * D <= 0) return;

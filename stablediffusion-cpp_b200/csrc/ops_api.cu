@@ -153,6 +153,30 @@ void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t l
   if (skinny_ok(M, K)) return launch_gemm_skinny(M, N, K, A, lda, B, ldb, false, C, ldc, bias, acc);
   gemm_f32_core(M, N, K, A, lda, B, ldb, C, ldc, bias, acc);
 }
+void gemm_tf32_direct(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                      float* C, int64_t ldc, const float* bias, bool acc) {
+  if (M <= 0 || N <= 0) return;
+  const bool ok = K > 0 && lda % 4 == 0 && ldb % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(B) & 15) == 0;
+  if (!ok) fail(kErrInvalidArg, "gemm_tf32_direct: operands must be 16-byte aligned rows");
+  GemmCall g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.A = A;
+  g.lda = lda;
+  g.B = B;
+  g.ldb = ldb;
+  g.C = C;
+  g.ldc = ldc;
+  g.bias = bias;
+  g.accumulate = acc;
+  g.tf32 = true;
+  g.epi = Epi::kStore;
+  g.out_bf16 = false;
+  g.bn = 0;
+  launch_gemm_tc(g);
+}
 void gemm_bf16_epilogue_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16,
                              const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, bool y_bf16, const float* bias,
                              int epi) {
@@ -330,7 +354,6 @@ int sdb200_attention(const float* q, const float* k, const float* v, float* out,
     require(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, op, "heads must be a multiple of kv_heads");
     if (N == 0 || Sq == 0) return kOk;
     require(Skv > 0, op, "Skv == 0");
-    require(d <= 256, op, "head dim > 256 is not supported");
     require_ptr(q, op, "q");
     require_ptr(k, op, "k");
     require_ptr(v, op, "v");

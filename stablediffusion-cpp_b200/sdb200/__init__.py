@@ -86,6 +86,15 @@ _SIGS = {
     "sdb200_zimage_sample": ([_v, _v, _i64, _i64, _i64, _i64, _v, _v, _i64, _i64, _f, _i, _f], _i),
     "sdb200_flow_sigmas": ([_i, _f, _v], _i),
     "sdb200_zimage_load": ([_v, C.c_char_p, C.c_char_p, _i, _i, _i64], _i),
+    "sdb200_vae_create": ([_f, _f], _v),
+    "sdb200_vae_set_weight": ([_v, C.c_char_p, _v, C.POINTER(_i64), _i], _i),
+    "sdb200_vae_load": ([_v, C.c_char_p, C.c_char_p], _i),
+    "sdb200_vae_finalize": ([_v], _i),
+    "sdb200_vae_info": ([_v, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)], _i),
+    "sdb200_vae_decode": ([_v, _v, _i64, _i64, _i64, _i64, _v], _i),
+    "sdb200_vae_destroy": ([_v], None),
+    "sdb200_vae_profile": ([_v, _i], _i),
+    "sdb200_vae_profile_read": ([_v, C.POINTER(C.c_double)], _i),
     "sdb200_safetensors_read": ([C.c_char_p, C.c_char_p, _i, _i64, _v, _i64, _v, _v, _v], _i),
     "sdb200_comm_unique_id": ([_v], _i),
     "sdb200_comm_create": ([_v, _i, _i], _v),

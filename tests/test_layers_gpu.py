@@ -81,13 +81,53 @@ def test_attention_tensor_cores_vs_oracle(sdb, orc, attention_path, N, Sq, Skv, 
     assert rel_fro(got, want) <= 2e-3
 
 
-def test_attention_d256_uses_exact_kernel(sdb, orc):
+def test_attention_d256_paths(sdb, orc, attention_path):
+    """Head dims above 128: tf32 GEMMs around a softmax by default (GEMM gate), the exact
+    fp32 kernel on path 1 (the reference's 1e-4)."""
     rng = np.random.default_rng(12)
     q = rng.standard_normal((1, 40, 2 * 256)).astype(np.float32)
     k = rng.standard_normal((1, 50, 2 * 256)).astype(np.float32)
     v = rng.standard_normal((1, 50, 2 * 256)).astype(np.float32)
+    want = orc.attention(q, k, v, 2, 2, False)
     got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), 2))
-    assert np.abs(got - orc.attention(q, k, v, 2, 2, False)).max() <= 1e-4
+    assert rel_fro(got, want) <= 2e-3
+    attention_path(1)
+    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), 2))
+    assert np.abs(got - want).max() <= 1e-4
+
+
+@pytest.mark.parametrize("N,Sq,Skv,H,KVH,d,causal", [
+    (1, 1024, 1024, 1, 1, 512, False),   # the VAE mid-block attention shape at a reduced size
+    (2, 130, 67, 4, 2, 160, True),       # GQA, causal, Skv not a multiple of 4 (padded rows)
+    (1, 7, 300, 3, 3, 200, False),       # few query rows
+])
+def test_attention_gemm_path_vs_oracle(sdb, orc, N, Sq, Skv, H, KVH, d, causal):
+    rng = np.random.default_rng(Sq + d)
+    q = rng.standard_normal((N, Sq, H * d)).astype(np.float32)
+    k = rng.standard_normal((N, Skv, KVH * d)).astype(np.float32)
+    v = rng.standard_normal((N, Skv, KVH * d)).astype(np.float32)
+    got = _np(sdb.backend.attention(_t(q), _t(k), _t(v), H, causal=causal, kv_heads=KVH))
+    want = orc.attention(q, k, v, H, KVH, causal)
+    assert rel_fro(got, want) <= 2e-3
+
+
+def test_attention_gemm_path_row_chunks(sdb, attention_path):
+    """Skv large enough that the 256 MB score block holds fewer rows than Sq: several
+    query-row chunks, with the causal mask offset per chunk; against the exact kernel."""
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    Sq, Skv, d = 1000, 70000, 136
+    q = torch.randn((1, Sq, d), generator=g, device="cuda")
+    k = torch.randn((1, Skv, d), generator=g, device="cuda")
+    v = torch.randn((1, Skv, d), generator=g, device="cuda")
+    for causal in (False, True):
+        attention_path(0)
+        got = _np(sdb.backend.attention(q, k, v, 1, causal=causal))
+        attention_path(1)
+        want = _np(sdb.backend.attention(q, k, v, 1, causal=causal))
+        assert rel_fro(got, want) <= 2e-3, causal
 
 
 def test_golden_layers(sdb):
