@@ -18,15 +18,24 @@ namespace sdb {
 
 void launch_attention_gemm(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
                            int64_t Skv, int heads, int kv_heads, int64_t d, bool causal, int64_t q_ld, int64_t kv_ld,
-                           int64_t o_ld) {
+                           int64_t o_ld, bool qk_tf32) {
   if (N <= 0 || Sq <= 0 || heads <= 0) return;
   const float scale = 1.0f / std::sqrt((float)d);
   const int group = heads / kv_heads;
   const int64_t inner = q_ld ? q_ld : (int64_t)heads * d, kv_inner = kv_ld ? kv_ld : (int64_t)kv_heads * d;
   const int64_t o_inner = o_ld ? o_ld : (int64_t)heads * d;
   const int64_t ld = (std::max<int64_t>(Skv, 1) + 3) / 4 * 4;  // 16-byte rows for the TMA operands
-  int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(Sq, ((int64_t)1 << 26) / ld));
-  if (chunk >= 128) chunk -= chunk % 128;
+  // Query rows per chunk: the score block stays within 512 MB, and where possible the
+  // output GEMM's 128-row tiles x (d / 128) column tiles fill whole waves of the SMs.
+  int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(Sq, ((int64_t)1 << 27) / ld));
+  const int64_t wave_rows = 128 * std::max<int64_t>(1, ctx().num_sms / ((d + 127) / 128));
+  if (chunk >= wave_rows && chunk < Sq)
+    chunk -= chunk % wave_rows;
+  else if (chunk >= 128 && chunk < Sq)
+    chunk -= chunk % 128;
+  const bool direct = qk_tf32 && inner % 4 == 0 && kv_inner % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+                      (d * 4) % 16 == 0;
   const size_t sb = ((size_t)(chunk * ld) * 4 + 255) & ~(size_t)255;
   const size_t vb = ((size_t)(d * ld) * 4 + 255) & ~(size_t)255;
   uint8_t* buf = static_cast<uint8_t*>(pool_malloc(sb + vb));
@@ -46,7 +55,10 @@ void launch_attention_gemm(const float* q, const float* k, const float* v, float
               launch_bias_fill(ob, o_inner, R, d, nullptr, false);
               continue;
             }
-            gemm_nt_f32_impl(R, Skv, d, qb, inner, kb, kv_inner, sc, ld, nullptr, false);
+            if (direct)  // operands already on the tf32 grid: read in place
+              gemm_tf32_direct(R, Skv, d, qb, inner, kb, kv_inner, sc, ld, nullptr, false);
+            else
+              gemm_nt_f32_impl(R, Skv, d, qb, inner, kb, kv_inner, sc, ld, nullptr, false);
             op_softmax_rows_ex(sc, R, Skv, ld, scale, causal, R, r0, true);
             gemm_tf32_direct(R, d, Skv, sc, ld, vt, ld, ob, o_inner, nullptr, false);
           }

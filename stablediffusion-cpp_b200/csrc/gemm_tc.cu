@@ -405,6 +405,29 @@ __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, u
                       __uint_as_float(r[j + 2]) + bias, __uint_as_float(r[j + 3]) + bias);
     __syncwarp();
     const bool vec = n == 32 && p.vec_ok && (pix0 & 3) == 0;
+    if (vec && res) {
+      // All eight residual loads of this lane first (eight in flight instead of one per
+      // store), then the stores. res may alias out: each element is loaded before this
+      // lane stores it, and no other lane touches it; plain loads, not the .nc path.
+      float4 a4[8];
+#pragma unroll
+      for (int r0 = 0; r0 < 32; r0 += 4) {
+        const int ch = row_base + r0 + sub;
+        a4[r0 / 4] = ch < p.M ? *reinterpret_cast<const float4*>(res + (long long)ch * hw + pix0 + c4)
+                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int r0 = 0; r0 < 32; r0 += 4) {
+        const int rr = r0 + sub, ch = row_base + rr;
+        if (ch >= p.M) continue;
+        float4 o = *reinterpret_cast<const float4*>(stg + rr * kStgPitch + c4);
+        const float4 a = a4[r0 / 4];
+        o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+        *reinterpret_cast<float4*>(out + (long long)ch * hw + pix0 + c4) = o;
+      }
+      __syncwarp();
+      continue;
+    }
 #pragma unroll
     for (int r0 = 0; r0 < 32; r0 += 4) {
       const int rr = r0 + sub, ch = row_base + rr;
@@ -412,12 +435,7 @@ __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, u
       const long long off = (long long)ch * hw + pix0 + c4;
       const float* src = stg + rr * kStgPitch + c4;
       if (vec) {
-        float4 o = *reinterpret_cast<const float4*>(src);
-        if (res) {
-          const float4 a4 = *reinterpret_cast<const float4*>(res + off);  // may alias out: no .nc load
-          o.x += a4.x; o.y += a4.y; o.z += a4.z; o.w += a4.w;
-        }
-        *reinterpret_cast<float4*>(out + off) = o;
+        *reinterpret_cast<float4*>(out + off) = *reinterpret_cast<const float4*>(src);
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e)

@@ -160,6 +160,8 @@ void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* 
 
 // Layer ops (layers.cu); arguments already validated by the caller.
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
+// x[r, c] rounded to tf32 in place (rows x cols, ld elements apart).
+void launch_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols);
 // GroupNorm over N samples of C channels x HW values (optionally followed by SiLU).
 void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const float*, const float*, float,
                    bool silu = false);
@@ -179,10 +181,11 @@ void gemm_tf32_direct(int64_t M, int64_t N, int64_t K, const float* A, int64_t l
                       float* C, int64_t ldc, const float* bias, bool acc);
 // Attention for any head dim as GEMM -> softmax -> GEMM on tf32 tensor cores. Row strides
 // (elements) default to heads * d for q / out and kv_heads * d for k / v; a sample's rows
-// are contiguous (sample stride = rows * stride).
+// are contiguous (sample stride = rows * stride). qk_tf32: q and k already hold values on
+// the tf32 grid (read in place instead of repacked).
 void launch_attention_gemm(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
                            int64_t Skv, int heads, int kv_heads, int64_t d, bool causal, int64_t q_ld = 0,
-                           int64_t kv_ld = 0, int64_t o_ld = 0);
+                           int64_t kv_ld = 0, int64_t o_ld = 0, bool qk_tf32 = false);
 void op_geglu(const float*, float*, int64_t, int64_t);
 void op_swiglu(const float*, const float*, float*, int64_t);
 void op_unary(float*, int64_t, int);  // 0 silu, 1 gelu (erf), 2 quick_gelu, 3 tanh

@@ -117,19 +117,27 @@ __global__ void __launch_bounds__(256) k_pack_nhwc(const float* __restrict__ x, 
   const int64_t Wo = UP ? 2 * W : W, HWo = (UP ? 2 * H : H) * Wo, HWs = H * W;
   const int64_t n = blockIdx.z, p0 = (int64_t)blockIdx.x * kPackPx, c0 = (int64_t)blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
+  // Source pixel of each of this thread's output pixels (the launcher keeps HWo < 2^31,
+  // so 32-bit division suffices).
+  int64_t src[kPackPx / 32];
+#pragma unroll
+  for (int j = 0; j < kPackPx / 32; ++j) {
+    const int64_t p = p0 + tx + 32 * j;
+    src[j] = p;
+    if (UP) {
+      const uint32_t oy = (uint32_t)p / (uint32_t)Wo, ox = (uint32_t)p - oy * (uint32_t)Wo;
+      src[j] = (int64_t)(oy >> 1) * W + (ox >> 1);
+    }
+  }
   float v[4][kPackPx / 32];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t c = c0 + ty + 8 * i;
+    const float* xc = x + (n * C + c) * HWs;
 #pragma unroll
     for (int j = 0; j < kPackPx / 32; ++j) {
       const int64_t p = p0 + tx + 32 * j;
-      int64_t src = p;
-      if (UP) {
-        const int64_t oy = p / Wo, ox = p - oy * Wo;
-        src = (oy >> 1) * W + (ox >> 1);
-      }
-      v[i][j] = (c < C && p < HWo) ? __ldg(x + (n * C + c) * HWs + src) : 0.0f;
+      v[i][j] = (c < C && p < HWo) ? __ldg(xc + src[j]) : 0.0f;
     }
   }
 #pragma unroll
@@ -144,7 +152,9 @@ __global__ void __launch_bounds__(256) k_pack_nhwc(const float* __restrict__ x, 
 #pragma unroll
     for (int j = 0; j < kPackPx / 32; ++j) {
       float y = v[i][j] * a + b;
-      if (silu) y = y / (1.0f + expf(-y));
+      // The result is rounded to tf32 (13 low bits dropped) next, so the fast exponential
+      // and division are exact enough: their error is below that rounding.
+      if (silu) y = __fdividef(y, 1.0f + __expf(-y));
       tile[ty + 8 * i][tx + 32 * j] = c < C ? round_tf32(y) : 0.0f;
     }
   }
@@ -162,6 +172,13 @@ __global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ w
   GRID_STRIDE(i, total) {
     const int64_t ci = i % cq, r = i / cq, t = r % taps, co = r / taps;
     wp[i] = ci < Cin ? round_tf32(__ldg(w + (co * Cin + ci) * taps + t)) : 0.0f;
+  }
+}
+// In place (no restrict): x[r * ld + c] = tf32(x[r * ld + c]).
+__global__ void k_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
+  GRID_STRIDE(i, rows * cols) {
+    const int64_t r = i / cols, c = i - r * cols;
+    x[r * ld + c] = round_tf32(x[r * ld + c]);
   }
 }
 __global__ void k_copy2d_16(const uint16_t* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
@@ -452,6 +469,41 @@ __global__ void k_softmax_rows(float* __restrict__ x, int64_t cols, int64_t ld, 
     p[j] = round_out ? round_tf32(o) : o;
   }
 }
+// The same softmax with the row held in registers (kSmxThreads x kSmxPer values): one
+// read and one write of the row instead of three passes. Rows of up to 16384 columns.
+constexpr int kSmxThreads = 512, kSmxPer = 32;
+__global__ void __launch_bounds__(kSmxThreads) k_softmax_rows_reg(float* __restrict__ x, int64_t cols, int64_t ld,
+                                                                  float scale, int causal, int64_t rows_per_head,
+                                                                  int64_t row0, int round_out) {
+  __shared__ float red[32];
+  float* p = x + (int64_t)blockIdx.x * ld;
+  const int64_t r = row0 + (int64_t)blockIdx.x % rows_per_head;
+  const int64_t valid = causal ? min(cols, r + 1) : cols;
+  float v[kSmxPer];
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kSmxPer; ++k) {
+    const int64_t j = threadIdx.x + (int64_t)k * kSmxThreads;
+    v[k] = j < valid ? p[j] * scale : -INFINITY;
+    m = fmaxf(m, v[k]);
+  }
+  m = block_max(m, red);
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kSmxPer; ++k) {
+    v[k] = v[k] == -INFINITY ? 0.0f : expf(v[k] - m);
+    s += v[k];
+  }
+  const float inv = 1.0f / block_sum(s, red);
+#pragma unroll
+  for (int k = 0; k < kSmxPer; ++k) {
+    const int64_t j = threadIdx.x + (int64_t)k * kSmxThreads;
+    if (j < cols) {
+      const float o = v[k] * inv;
+      p[j] = round_out ? round_tf32(o) : o;
+    }
+  }
+}
 // dst[c, r] = tf32(src[r, c]) for a rows x cols block (ld_src, ld_dst in elements), through
 // a 32 x 32 shared-memory tile.
 __global__ void k_transpose_tf32(const float* __restrict__ src, int64_t ld_src, float* __restrict__ dst,
@@ -599,6 +651,7 @@ void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H
   if (N <= 0 || H <= 0 || W <= 0) return;
   if (N > 65535 || (cp + 31) / 32 > 65535) fail(kErrInvalidArg, "pack_nhwc: too many samples or channels");
   const int64_t HWo = (up2 ? 4 : 1) * H * W;
+  if (HWo >= ((int64_t)1 << 31)) fail(kErrInvalidArg, "pack_nhwc: image too large");
   const dim3 grid((unsigned)((HWo + kPackPx - 1) / kPackPx), (unsigned)((cp + 31) / 32), (unsigned)N);
   if (up2)
     k_pack_nhwc<true><<<grid, dim3(32, 8), 0, ctx().stream>>>(x, xh, C, H, W, cp, ab, a0, b0, silu ? 1 : 0);
@@ -616,6 +669,11 @@ void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int
   if (rows <= 0 || cols <= 0) return;
   k_pack_tf32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
   check_launch("pack_tf32");
+}
+void launch_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return;
+  k_round_tf32_inplace<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(x, ld, rows, cols);
+  check_launch("round_tf32");
 }
 void launch_copy2d(const void* src, int64_t ld, void* dst, int64_t ldo, int64_t rows, int64_t cols, int esize) {
   if (rows <= 0 || cols <= 0) return;
@@ -712,8 +770,12 @@ void op_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, bool cau
 void op_softmax_rows_ex(float* x, int64_t rows, int64_t cols, int64_t ld, float scale, bool causal,
                         int64_t rows_per_head, int64_t row0, bool round_out) {
   if (rows <= 0 || cols <= 0) return;
-  k_softmax_rows<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, cols, ld, scale, causal ? 1 : 0, rows_per_head, row0,
-                                                          round_out ? 1 : 0);
+  if (cols <= (int64_t)kSmxThreads * kSmxPer)
+    k_softmax_rows_reg<<<(unsigned)rows, kSmxThreads, 0, ctx().stream>>>(x, cols, ld, scale, causal ? 1 : 0,
+                                                                          rows_per_head, row0, round_out ? 1 : 0);
+  else
+    k_softmax_rows<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, cols, ld, scale, causal ? 1 : 0, rows_per_head, row0,
+                                                            round_out ? 1 : 0);
   check_launch("softmax_rows");
 }
 void launch_transpose_tf32(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols) {

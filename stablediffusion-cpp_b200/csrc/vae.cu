@@ -297,8 +297,9 @@ struct Vae {
     launch_pack_nhwc(cur.f(), xh.f(), N, C, H, W, C, abp, 1.0f, 0.0f, false, false);  // tokens [N*S, C]
     timed(1, 2.0 * N * S * C * 3 * C + 4.0 * N * S * S * C, [&] {
       gemm_tf32_direct(N * S, 3 * C, C, xh.f(), C, attn.wqkv.f(), C, qkv.f(), 3 * C, attn.bqkv.f(), false);
+      launch_round_tf32_inplace(qkv.f(), 3 * C, N * S, 2 * C);  // q | k onto the tf32 grid
       const float* q = qkv.f();
-      launch_attention_gemm(q, q + C, q + 2 * C, att.f(), N, S, S, 1, 1, C, false, 3 * C, 3 * C, C);
+      launch_attention_gemm(q, q + C, q + 2 * C, att.f(), N, S, S, 1, 1, C, false, 3 * C, 3 * C, C, true);
       launch_pack_tf32(att.f(), C, xh.f(), C, N * S, C);  // the 1x1 conv's NHWC operand
     });
     conv(attn.out, N, H, W, cur.f(), cur.f());
