@@ -201,6 +201,29 @@ def ref_dit_block_sample():
     return (lambda: model(x, 0.5, cap)), dit_forward_flops(cfg)["total"], ref.num_threads(), model
 
 
+def ref_gpu(world, local):
+    """The reference's own GPU backend (src/backend_cuda.cu + cuBLAS, built from its sources
+    into oracle/_ref/libsdref_cuda.so): a comparison column timed on the same B200, one
+    process on device 0 only (the reference hard-wires device 0). Returns (RefCUDA or
+    None, reason)."""
+    if world != 1 or local != 0:
+        return None, "single-GPU runs only (the reference backend uses device 0)"
+    try:
+        from oracle import RefCUDA
+
+        if not RefCUDA.available():
+            return None, "oracle/_ref/libsdref_cuda.so not built"
+        r = RefCUDA()
+        if not r.cuda_available():
+            return None, "the reference backend found no CUDA device"
+        return r, None
+    except Exception as e:  # reported, never required
+        return None, f"failed: {e}"
+
+
+REF_GPU_KIND = "reference src/backend_cuda.cu + cuBLAS (its own GPU path), built for sm_100a, same B200"
+
+
 def ref_gemm_sample(rows=512):
     import numpy as np
 
@@ -360,6 +383,7 @@ def timed_loop(fn, steps, stream, pg, dev):
 
 
 def run_dit(args, world, rank, local, pg, dev):
+    import numpy as np
     import torch
 
     import sdb200
@@ -371,7 +395,8 @@ def run_dit(args, world, rank, local, pg, dev):
         raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} GPUs")
     B = GLOBAL_BATCH // world
     cfg = Z_IMAGE
-    model = ZImageB200(random_weights_torch(cfg, 0, dev), cfg)
+    wts = random_weights_torch(cfg, 0, dev)
+    model = ZImageB200(wts, cfg)
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     x = torch.randn((B, cfg.in_channels, LAT_H, LAT_W), generator=g, device=dev)
@@ -417,6 +442,30 @@ def run_dit(args, world, rank, local, pg, dev):
     # scheduler.cpp:117-135) on the device, once, after the per-step timing.
     sampler_ms = timed_loop(lambda: model.sample(x, cap, steps=8, shift=3.0), 1, stream, pg, dev)
     err = be.device_error_word()
+    rg = None
+    if not args.no_ref_gpu:
+        r, why = ref_gpu(world, local)
+        if r is None:
+            rg = {"value": None, "unavailable": why}
+        else:
+            # The reference's ZImageTransformer on its GPU backend, holding its own device
+            # copy of the same weights; its pipeline runs images one at a time (batch 1).
+            rm = r.zimage_cuda(wts, heads=cfg.heads)
+            x0, c0 = x[:1].cpu().numpy(), cap[:1].cpu().numpy()
+            ref_out = rm(x0, 0.5, c0)  # warm-up: allocator, cuBLAS
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ref_out = rm(x0, 0.5, c0)
+            rdt = time.perf_counter() - t0
+            model.forward(x, 0.5, cap, out)
+            ours = out[:1].cpu().numpy().astype(np.float64)
+            rel = float(np.linalg.norm(ours - ref_out) / np.linalg.norm(ref_out))
+            rg = {"value": rdt * 1e3 * GLOBAL_BATCH, "unit": "ms/step", "kind": REF_GPU_KIND,
+                  "sample": f"one batch-1 forward of the full 30-layer model on the GPU backend ({rdt * 1e3:.1f} ms, "
+                            f"wall clock with the latent in and prediction out), x {GLOBAL_BATCH} images per step",
+                  "rel_fro_this_vs_reference": rel}
+            del rm
+            torch.cuda.empty_cache()
     cpu = cpu_baseline("dit") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
         line = {
@@ -446,6 +495,7 @@ def run_dit(args, world, rank, local, pg, dev):
             "sampler_8_steps": {"ms": sampler_ms, "ms_per_step": sampler_ms / 8,
                                 "note": "sdb200_zimage_sample: 8 flow-matching Euler steps, shift 3, on the device"},
             "cpu_baseline": cpu,
+            "reference_gpu": rg,
             "clocks": clk.summary(),
             "device_error_word": err,
         }
@@ -591,6 +641,25 @@ def run_gemm(args, world, rank, local, pg, dev):
     e2e_value = FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12
     err = be.device_error_word()
     cpu = cpu_baseline("gemm") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    rg = None
+    if not args.no_ref_gpu:
+        r, why = ref_gpu(world, local)
+        if r is None:
+            rg = {"value": None, "unavailable": why}
+        else:
+            Yr = torch.empty_like(Yd)
+            rstep = lambda: r.gemm_nt_bf16_dev(M, N, K, Xd.data_ptr(), K, Wd.data_ptr(), K, Yr.data_ptr(), N,  # noqa
+                                               bd.data_ptr())
+            for _ in range(3):
+                rstep()
+            rms = timed_loop(rstep, args.steps, stream, None, dev)
+            sdb200.check(L.sdb200_gemm_nt_bf16(M, N, K, Xd.data_ptr(), K, Wd.data_ptr(), K, Yd.data_ptr(), N,
+                                               bd.data_ptr(), 0))
+            torch.cuda.synchronize()
+            rel = float((Yd.double() - Yr.double()).norm() / Yr.double().norm())
+            rg = {"value": FLOP * args.steps / (rms * 1e-3) / 1e12, "unit": "TFLOP/s", "kind": REF_GPU_KIND,
+                  "sample": "the same GEMM on the same device buffers (pack A to bf16, cublasGemmEx, bias kernel)",
+                  "rel_fro_this_vs_reference": rel}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -608,6 +677,7 @@ def run_gemm(args, world, rank, local, pg, dev):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(Xh.numel() * 4),
                     "d2h_bytes_per_step": int(Yh.numel() * 4)},
             "cpu_baseline": cpu,
+            "reference_gpu": rg,
             "clocks": clk.summary(),
             "device_error_word": err,
         }
@@ -659,6 +729,28 @@ def run_attention(args, world, rank, local, pg, dev):
     e2e_step()
     e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
     pk = peaks()
+    rg = None
+    if not args.no_ref_gpu:
+        r, why = ref_gpu(world, local)
+        if r is None:
+            rg = {"value": None, "unavailable": why}
+        else:
+            o_ref = torch.empty_like(q)
+            rstep = lambda: r.attention_dev(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_ref.data_ptr(), 1, S, S, H, H,  # noqa
+                                            d)
+            for _ in range(2):
+                rstep()
+            rms = timed_loop(rstep, args.steps, stream, None, dev)
+            api = lambda: sdb200.check(L.sdb200_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1,  # noqa
+                                                          S, S, H, H, d, 0))
+            api()
+            ams = timed_loop(api, args.steps, stream, None, dev)
+            rel = float((o.double() - o_ref.double()).norm() / o_ref.double().norm())
+            rg = {"value": FLOP * args.steps / (rms * 1e-3) / 1e12, "unit": "TFLOP/s", "kind": REF_GPU_KIND,
+                  "sample": "attention() on the same fp32 q/k/v device buffers (strided-batched SGEMM, softmax, "
+                            "SGEMM)",
+                  "this_api_tflops": FLOP * args.steps / (ams * 1e-3) / 1e12,
+                  "rel_fro_this_vs_reference": rel}
     if rank == 0:
         achieved = FLOP / (ms / args.steps * 1e-3) / 1e12
         print(json.dumps({
@@ -674,7 +766,8 @@ def run_attention(args, world, rank, local, pg, dev):
                          "peak_kind": f"{pk['kind']} bf16 burst (dense fp16 = bf16 rate)", "traffic": None},
             "e2e": {"value": FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(3 * qh.numel() * 4), "d2h_bytes_per_step": int(oh.numel() * 4)},
-            "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+            "cpu_baseline": None, "reference_gpu": rg, "clocks": clk.summary(),
+            "device_error_word": be.device_error_word()}), flush=True)
 
 
 # The VAE decoder's 3x3 convolution at each resolution stage of a 1024^2 decode (channels,
@@ -780,6 +873,28 @@ def run_conv(args, world, rank, local, pg, dev):
     e2e_step()
     e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
     io = sum(h[2].numel() * 4 for h in hosts)
+    rg = None
+    if not args.no_ref_gpu:
+        r, why = ref_gpu(world, local)
+        if r is None:
+            rg = {"value": None, "unavailable": why}
+        else:
+            outs = [torch.empty_like(y) for *_, y in bufs]
+
+            def rstep():
+                for (c, s, x, w, b, y), yr in zip(bufs, outs):
+                    r.conv2d_dev(x.data_ptr(), 1, c, s, s, w.data_ptr(), c, 3, 3, b.data_ptr(), 1, 1, yr.data_ptr(),
+                                 s, s)
+
+            rstep()
+            rms = timed_loop(rstep, 1, stream, None, dev)
+            step()
+            torch.cuda.synchronize()
+            rel = max(float((y.double() - yr.double()).norm() / yr.double().norm())
+                      for (*_, y), yr in zip(bufs, outs))
+            rg = {"value": FLOP / (rms * 1e-3) / 1e12, "unit": "TFLOP/s", "kind": REF_GPU_KIND,
+                  "sample": "conv2d() of the four stages on the same device buffers (im2col + fp32 SGEMM)",
+                  "ms_per_step": rms, "rel_fro_this_vs_reference_max": rel}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -808,7 +923,8 @@ def run_conv(args, world, rank, local, pg, dev):
                          "traffic": profile_value("conv_tc_vae.md", "traffic_bytes_per_step")},
             "e2e": {"value": FLOP * args.steps * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(io), "d2h_bytes_per_step": int(io)},
-            "cpu_baseline": cpu, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+            "cpu_baseline": cpu, "reference_gpu": rg, "clocks": clk.summary(),
+            "device_error_word": be.device_error_word()}), flush=True)
 
 
 def ref_vae_sample(side=32):
@@ -884,6 +1000,27 @@ def run_vae(args, world, rank, local, pg, dev):
 
     e2e_step()
     e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev)
+    rg = None
+    if not args.no_ref_gpu:
+        r, why = ref_gpu(world, local)
+        if r is None:
+            rg = {"value": None, "unavailable": why}
+        else:
+            rv = r.vae_cuda(random_weights(cfg, 7), cfg.scaling_factor, cfg.shift_factor)
+            zh_np = z.cpu().numpy()
+            img = rv(zh_np)  # warm-up (allocator, cuBLAS)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            img = rv(zh_np)
+            rdt = time.perf_counter() - t0
+            v.decode(z, out)
+            ours = out.cpu().numpy().astype(np.float64)
+            rel = float(np.linalg.norm(ours - img) / np.linalg.norm(img))
+            rg = {"value": rdt * 1e3, "unit": "ms/decode", "kind": REF_GPU_KIND,
+                  "sample": "VAEDecoder::decode on the GPU backend, same weights and latent (wall clock, latent in "
+                            "and image out over PCIe included)",
+                  "rel_fro_this_vs_reference": rel}
+            del rv
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -918,7 +1055,8 @@ def run_vae(args, world, rank, local, pg, dev):
                          "traffic": None},
             "e2e": {"value": e2e_ms / args.steps, "unit": "ms/decode", "h2d_bytes_per_step": int(zh.numel() * 4),
                     "d2h_bytes_per_step": int(oh.numel() * 4)},
-            "cpu_baseline": cpu, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+            "cpu_baseline": cpu, "reference_gpu": rg, "clocks": clk.summary(),
+            "device_error_word": be.device_error_word()}), flush=True)
 
 
 def main():
@@ -929,6 +1067,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip the reference GPU backend comparison (oracle/_ref/libsdref_cuda.so)")
     ap.add_argument("--conv-stage", type=int, default=-1, choices=[-1, 0, 1, 2, 3],
                     help="conv: run only this stage of the VAE-decoder stack (-1: all four)")
     ap.add_argument("--tp-mode", type=int, default=1, choices=[0, 1],

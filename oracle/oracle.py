@@ -21,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libsdref.so")
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libsdref_cuda.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
@@ -487,3 +488,116 @@ class RefCPU(_Base):
                     pass
 
         return _Model()
+
+
+class RefCUDA(RefCPU):
+    """The reference's GPU backend (src/backend_cuda.cu + cuBLAS) linked in place of the
+    stub (oracle/_ref/libsdref_cuda.so): a comparison column timed on the same B200, never
+    the product. Every RefCPU entry point is present; the extra ones take device pointers
+    or move tensors to the device as the reference pipeline does."""
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_CUDA_SO)
+
+    def __init__(self, path: str = REF_CUDA_SO):
+        super().__init__(path)
+        v = C.c_void_p
+        self.cuda_available = self.fn("cuda_available", [], C.c_int)
+        self.cuda_sync = self.fn("cuda_synchronize", [], C.c_int)
+        self._w_cuda = self.fn("weights_to_cuda", [v], C.c_int)
+        self._z_fwd_cuda = self.fn("zimage_forward_cuda", [v, v, _i64, _i64, _i64, C.c_float, v, _i64, _i64, v],
+                                   C.c_int)
+        self._gemm_cuda = self.fn("cuda_gemm_nt_bf16", [_i64, _i64, _i64, v, _i64, v, _i64, v, _i64, v, C.c_int],
+                                  C.c_int)
+        self._attn_cuda = self.fn("cuda_attention", [v, v, v, v, _i64, _i64, _i64, C.c_int, C.c_int, _i64, C.c_int],
+                                  C.c_int)
+        self._conv_cuda = self.fn("cuda_conv2d", [v, _i64, _i64, _i64, _i64, v, _i64, _i64, _i64, v, C.c_int, C.c_int,
+                                                  v, _i64, _i64], C.c_int)
+        self._w_add_dev = self.fn("weights_add_device", [v, C.c_char_p, v, C.c_int, v, C.c_int], C.c_int)
+        self._v_dec_cuda = self.fn("vae_decode_cuda", [v, v, _i64, _i64, _i64, _i64, v, _i64, v], C.c_int)
+
+    def gemm_nt_bf16_dev(self, M, N, K, A, lda, B, ldb, Cp, ldc, bias, acc=False):
+        self._chk(self._gemm_cuda(M, N, K, A, lda, B, ldb, Cp, ldc, bias, int(acc)))
+
+    def attention_dev(self, q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal=False):
+        self._chk(self._attn_cuda(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, int(causal)))
+
+    def conv2d_dev(self, x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo):
+        self._chk(self._conv_cuda(x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo))
+
+    def synchronize(self):
+        self._chk(self.cuda_sync())
+
+    def zimage_cuda(self, weights: dict, heads=30, patch=2, norm_eps=1e-5, rope_theta=256.0, t_scale=1000.0,
+                    axes=(32, 48, 48)):
+        """ZImageTransformer over `weights` (name -> torch CUDA tensor, float32 or bfloat16),
+        copied device to device into the reference's own storage; f(x, t, cap) runs its
+        forward on the GPU backend and returns the host output."""
+        import torch
+
+        w = self.w_new()
+        for name, t in weights.items():
+            t = t.contiguous()
+            shape = (C.c_int64 * t.dim())(*t.shape)
+            self._chk(self._w_add_dev(w, name.encode(), C.cast(shape, C.c_void_p), t.dim(), t.data_ptr(),
+                                      int(t.dtype == torch.bfloat16)))
+        self.synchronize()
+        m = self.z_new(w, heads, patch, norm_eps, rope_theta, t_scale, *axes)
+        if not m:
+            self.w_free(w)
+            raise RuntimeError(self.last_error().decode())
+        ref = self
+
+        class _Model:
+            def __call__(self, x, t, cap):
+                x = np.ascontiguousarray(x, np.float32)
+                cap = np.ascontiguousarray(cap, np.float32)
+                out = np.empty_like(x)
+                _, Cc, H, W = x.shape
+                ref._chk(ref._z_fwd_cuda(m, _ptr(x), Cc, H, W, float(t), _ptr(cap), cap.shape[1], cap.shape[2],
+                                         _ptr(out)))
+                return out
+
+            def __del__(self):
+                try:
+                    ref.z_free(m)
+                    ref.w_free(w)
+                except Exception:
+                    pass
+
+        return _Model()
+
+    def vae_cuda(self, weights: dict, scaling_factor: float, shift_factor: float):
+        """VAEDecoder over `weights` (name -> fp32 numpy) moved to the device; f(z) decodes on
+        the GPU backend and returns the host image."""
+        w = self.w_new()
+        for name, arr in weights.items():
+            arr = np.ascontiguousarray(arr, np.float32)
+            shape = (C.c_int64 * arr.ndim)(*arr.shape)
+            self._chk(self.w_add(w, name.encode(), C.cast(shape, C.c_void_p), arr.ndim, _ptr(arr), 0))
+        self._chk(self._w_cuda(w))
+        m = self.v_new(w, scaling_factor, shift_factor)
+        if not m:
+            self.w_free(w)
+            raise RuntimeError(self.last_error().decode())
+        ref = self
+
+        class _Vae:
+            def __call__(self, z):
+                z = np.ascontiguousarray(z, np.float32)
+                cap = z.size * 64 * 4
+                out = np.empty(cap, np.float32)
+                shp = (C.c_int64 * 4)()
+                ref._chk(ref._v_dec_cuda(m, _ptr(z), *z.shape, _ptr(out), cap, C.cast(shp, C.c_void_p)))
+                n = int(np.prod(list(shp)))
+                return out[:n].reshape(tuple(shp)).copy()
+
+            def __del__(self):
+                try:
+                    ref.v_free(m)
+                    ref.w_free(w)
+                except Exception:
+                    pass
+
+        return _Vae()

@@ -12,6 +12,7 @@
 #include <string>
 #include <vector>
 
+#include "backend_cuda.h"
 #include "safetensors.h"
 #include "scheduler.h"
 #include "tensor.h"
@@ -190,6 +191,57 @@ int sdref_zimage_forward(void* m, const float* x, int64_t C, int64_t H, int64_t 
   });
 }
 
+// ---- the reference's GPU backend (backend_cuda.cu + cuBLAS), in the build that links it
+// instead of the stub (oracle/Makefile `refgpu`): a comparison column on the same B200.
+int sdref_cuda_available() { return cuda::available() ? 1 : 0; }
+int sdref_cuda_synchronize() { return guard([&] { cuda::synchronize(); }); }
+// Weights::to_device(Device::CUDA) (safetensors.cpp:195-200): models keep their pointers.
+int sdref_weights_to_cuda(void* w) { return guard([&] { static_cast<Weights*>(w)->to_device(Device::CUDA); }); }
+// The transformer forward with its input moved to the device first and the output back.
+int sdref_zimage_forward_cuda(void* m, const float* x, int64_t C, int64_t H, int64_t W, float t, const float* cap,
+                              int64_t L, int64_t capdim, float* out) {
+  return guard([&] {
+    Tensor tx = make(x, {1, C, H, W}).to(Device::CUDA);
+    Tensor tc = make(cap, {1, L, capdim}).to(Device::CUDA);
+    put(static_cast<ZImageTransformer*>(m)->forward(tx, t, tc).to(Device::CPU), out);
+  });
+}
+// Adds tensor `name` on the device with the contents of the caller's device buffer
+// `src` (F32, or BF16 bit patterns when bf16 != 0), copied device to device. The storage
+// is the reference's own (Tensor::to(Device::CUDA) of a zero host tensor, then
+// cuda::copy), so its ops see a tensor exactly as Weights::to_device leaves one.
+int sdref_weights_add_device(void* w, const char* name, const int64_t* shape, int ndim, const void* src, int bf16) {
+  return guard([&] {
+    std::vector<int64_t> s(shape, shape + ndim);
+    Tensor host;
+    host.shape = s;
+    if (bf16) {
+      host.dtype = DType::BF16;
+      host.data16.assign((size_t)Tensor::numel_of(s), 0);
+    } else {
+      host.data.assign((size_t)Tensor::numel_of(s), 0.0f);
+    }
+    Tensor t = host.to(Device::CUDA);
+    const size_t bytes = (size_t)Tensor::numel_of(s) * (bf16 ? 2 : 4);
+    if (bytes) cuda::copy(bf16 ? (void*)t.dptr16() : (void*)t.dptr(), src, bytes);
+    static_cast<Weights*>(w)->tensors[name] = std::move(t);
+  });
+}
+// backend_cuda.h entry points on caller-owned device buffers.
+int sdref_cuda_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
+                            int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
+  return guard([&] { cuda::gemm_nt_bf16(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0); });
+}
+int sdref_cuda_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
+                         int64_t Skv, int heads, int kv_heads, int64_t d, int causal) {
+  return guard([&] { cuda::attention(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal != 0); });
+}
+int sdref_cuda_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
+                      int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho,
+                      int64_t Wo) {
+  return guard([&] { cuda::conv2d(x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo); });
+}
+
 // ---- VAE decoder (vae.cpp) on an in-memory Weights (sdref_weights_new / _add, fp32) --
 void* sdref_vae_new(void* w, float scaling_factor, float shift_factor) {
   try {
@@ -200,6 +252,17 @@ void* sdref_vae_new(void* w, float scaling_factor, float shift_factor) {
   }
 }
 void sdref_vae_free(void* m) { delete static_cast<VAEDecoder*>(m); }
+// The decode with the latent moved to the device and the image back (GPU backend build;
+// the weights must have been moved with sdref_weights_to_cuda before sdref_vae_new).
+int sdref_vae_decode_cuda(void* m, const float* z, int64_t N, int64_t C, int64_t h, int64_t w, float* out,
+                          int64_t out_cap, int64_t* shape4) {
+  return guard([&] {
+    Tensor y = static_cast<VAEDecoder*>(m)->decode(make(z, {N, C, h, w}).to(Device::CUDA)).to(Device::CPU);
+    if (y.ndim() != 4 || y.numel() > out_cap) throw std::runtime_error("sdref_vae_decode_cuda: output buffer too small");
+    for (int i = 0; i < 4; ++i) shape4[i] = y.dim(i);
+    put(y, out);
+  });
+}
 // latents [N, C, h, w] -> out (capacity out_cap floats); shape4 receives the output shape.
 int sdref_vae_decode(void* m, const float* z, int64_t N, int64_t C, int64_t h, int64_t w, float* out, int64_t out_cap,
                      int64_t* shape4) {
