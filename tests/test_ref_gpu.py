@@ -47,7 +47,9 @@ def test_gemm_bf16_vs_reference_gpu(sdb, rgpu, M, N, K):
     sdb.check(sdb.lib().sdb200_gemm_nt_bf16(M, N, K, A.data_ptr(), K, Wb.data_ptr(), K, ours.data_ptr(), N,
                                             b.data_ptr(), 0))
     rgpu.gemm_nt_bf16_dev(M, N, K, A.data_ptr(), K, Wb.data_ptr(), K, ref.data_ptr(), N, b.data_ptr())
-    assert rel_fro(_np(ours), _np(ref)) <= 1e-5
+    # M <= 16 runs the exact-fp32 skinny kernel here (A not rounded to bf16), so it differs
+    # from the reference by the reference's own A rounding: the GEMM gate applies there.
+    assert rel_fro(_np(ours), _np(ref)) <= (1e-5 if M > 16 else 2e-3)
 
 
 @pytest.mark.parametrize("N,S,H,KVH,d,causal", [(1, 4224, 30, 30, 128, False), (2, 300, 32, 8, 128, True),
