@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast(
       for (int q = 0; q < W; ++q) hd.p[q][row * D + i] = w;
     }
   }
-  // Stores into peers' memory are visible system-wide before this kernel completes.
-  __threadfence_system();
+  // Stores into peers' memory are visible system-wide before this kernel completes (with
+  // one rank every destination is local).
+  if (W > 1) __threadfence_system();
 }
 
 // Register-resident form of k_post_norm_mod_bcast for D % 4 == 0 and D <= 4096: thread t
@@ -164,7 +165,15 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
   const int D4 = D >> 2;
   const float4* src = reinterpret_cast<const float4*>(slots + lr * D);
   const long long sstride4 = (slot_rows * D) >> 2;
-  float4 a[kPnChunks];
+  float4* y = reinterpret_cast<float4*>(x + row * D);
+  // The residual row is loaded together with the partial rows, so that both are in flight
+  // before the first reduction.
+  float4 a[kPnChunks], xo[kPnChunks];
+#pragma unroll
+  for (int k = 0; k < kPnChunks; ++k) {
+    const int i4 = threadIdx.x + k * kRowThreads;
+    xo[k] = i4 < D4 ? y[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float ss = 0.0f;
 #pragma unroll
   for (int k = 0; k < kPnChunks; ++k) {
@@ -184,7 +193,6 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
     }
   }
   const float rstd = rsqrtf(block_sum256(ss, red) / (float)D + eps);
-  float4* y = reinterpret_cast<float4*>(x + row * D);
   const float4* g2 = reinterpret_cast<const float4*>(gamma2);
   const float4* gt = reinterpret_cast<const float4*>(g);
   float ss2 = 0.0f;
@@ -198,8 +206,7 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
         const float4 gg = gt[i4];
         v = make_float4(gg.x * v.x, gg.y * v.y, gg.z * v.z, gg.w * v.w);
       }
-      const float4 xo = y[i4];
-      const float4 xn = make_float4(xo.x + v.x, xo.y + v.y, xo.z + v.z, xo.w + v.w);
+      const float4 xn = make_float4(xo[k].x + v.x, xo[k].y + v.y, xo[k].z + v.z, xo[k].w + v.w);
       y[i4] = xn;
       a[k] = xn;
       ss2 += xn.x * xn.x + xn.y * xn.y + xn.z * xn.z + xn.w * xn.w;
@@ -226,8 +233,9 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
       for (int q = 0; q < W; ++q) *reinterpret_cast<uint2*>(hd.p[q] + row * D + 4 * i4) = w;
     }
   }
-  // Stores into peers' memory are visible system-wide before this kernel completes.
-  __threadfence_system();
+  // Stores into peers' memory are visible system-wide before this kernel completes (with
+  // one rank every destination is local and kernel completion orders the stores).
+  if (W > 1) __threadfence_system();
 }
 
 // One flow-matching Euler step of the sampler on the device (pipeline.cpp:237-243,
