@@ -1109,6 +1109,9 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
     fail(kErrInvalidArg, "conv_tc: bad packed layout");
   if (Cout > (1 << 30) || Ho * Wo > (1ll << 31) || N > 65535)
     fail(kErrInvalidArg, "conv_tc: shape too large");
+  // A few output channels would fill a few of a tile's 128 MMA rows: direct kernel instead.
+  if (Cout <= 8 && kh == kw && kh <= 15 && (Ho + 31) / 32 <= 65535 && H * W < (1ll << 31))
+    return launch_conv_direct(xh, N, Cin, cp, H, W, wp, cq, Cout, kh, pad, bias, res, out, Ho, Wo);
   // Tile width by the wave-count cost model of choose_bn over the pixel rectangles.
   const int64_t m_tiles = (Cout + kBM - 1) / kBM;
   int bn = 256, bw = 0, bh = 0;

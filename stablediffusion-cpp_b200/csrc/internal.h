@@ -134,6 +134,10 @@ void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H
 // ab[n * C + c] = (rstd * gamma[c], beta[c] - mean * rstd * gamma[c]).
 void gn_scale_shift(const float* x, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
                     const float* beta, float eps, float2* ab);
+// The same convolution (square kernel k) as a direct fp32 SIMT kernel, for Cout <= 8.
+void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                        int64_t cq, int64_t Cout, int k, int pad, const float* bias, const float* res, float* out,
+                        int64_t Ho, int64_t Wo);
 // NCHW fp32 [N, C, HW] -> NHWC [N, HW, cp], rounded to tf32, zero in channels C..cp-1.
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp);
 // Conv weights [Cout, Cin, taps] -> [Cout, taps, cq], rounded to tf32, zero past Cin.

@@ -174,6 +174,103 @@ __global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ w
     wp[i] = ci < Cin ? round_tf32(__ldg(w + (co * Cin + ci) * taps + t)) : 0.0f;
   }
 }
+// Direct convolution for layers with few output channels (the VAE's conv_out, 128 -> 3):
+// on the tensor cores such a layer would fill 3 of a tile's 128 rows. Operands are the
+// implicit-GEMM path's: xh NHWC (channel pitch cp, tf32 values), wp [Cout, taps, cq].
+// A block computes a 16 x 32 tile of output pixels for all CO channels, each thread two
+// pixels 16 rows apart. 8-channel slices of the input tile with its halo are staged
+// channel-major in shared memory (conflict-free reads along x), and the slice's weights
+// as [channel][tap][CO], so one 16-byte load gives four output channels' weights, used for
+// both pixels; fp32 FMA accumulation.
+constexpr int kDirTX = 16, kDirTY = 32, kDirCh = 8;
+template <int CO, int KC>  // KC: the kernel size at compile time, or 0 (runtime k)
+__global__ void __launch_bounds__(256) k_conv_direct_nhwc(
+    const float* __restrict__ xh, int64_t cp, int Cin, int H, int W, const float* __restrict__ wp, int64_t cq,
+    int Cout, int k_rt, int pad, const float* __restrict__ bias, const float* res, float* out, int Ho, int Wo) {
+  const int k = KC ? KC : k_rt;
+  extern __shared__ float4 dsm4[];
+  float* dsm = reinterpret_cast<float*>(dsm4);
+  const int TWx = kDirTX + k - 1, TWy = kDirTY + k - 1, TT = TWx * TWy, taps = k * k;
+  float* tin = dsm;                        // [kDirCh][TT]
+  float* tw = dsm + ((kDirCh * TT + 3) & ~3);  // [kDirCh][taps][CO], 16-byte aligned
+  const int n = blockIdx.z, oy0 = blockIdx.y * kDirTY, ox0 = blockIdx.x * kDirTX;
+  const int tx = threadIdx.x % kDirTX, ty = threadIdx.x / kDirTX;  // ty < 16: rows ty and ty + 16
+  float acc0[CO], acc1[CO];
+#pragma unroll
+  for (int co = 0; co < CO; ++co) acc0[co] = acc1[co] = 0.0f;
+  for (int c0 = 0; c0 < Cin; c0 += kDirCh) {
+    __syncthreads();
+    // One pixel's 8 channels per step: two 16-byte loads (cp % 4 == 0, c0 % 8 == 0), or
+    // element loads for a slice that runs past Cin.
+    const bool full = c0 + kDirCh <= Cin;
+    for (int p = threadIdx.x; p < TT; p += blockDim.x) {
+      const int py = p / TWx, iy = oy0 - pad + py, ix = ox0 - pad + (p - py * TWx);
+      float v[kDirCh];
+#pragma unroll
+      for (int c = 0; c < kDirCh; ++c) v[c] = 0.0f;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
+        const float* src = xh + (((int64_t)n * H + iy) * W + ix) * cp + c0;
+        if (full) {
+          const float4 a0 = __ldg(reinterpret_cast<const float4*>(src));
+          const float4 a1 = __ldg(reinterpret_cast<const float4*>(src + 4));
+          v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+          v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        } else {
+#pragma unroll
+          for (int c = 0; c < kDirCh; ++c)
+            if (c0 + c < Cin) v[c] = __ldg(src + c);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kDirCh; ++c) tin[c * TT + p] = v[c];
+    }
+    for (int i = threadIdx.x; i < kDirCh * taps * CO; i += blockDim.x) {
+      const int co = i % CO, r = i / CO, t = r % taps, c = r / taps;
+      tw[i] = (co < Cout && c0 + c < Cin) ? __ldg(wp + ((int64_t)co * taps + t) * cq + c0 + c) : 0.0f;
+    }
+    __syncthreads();
+    for (int c = 0; c < kDirCh; ++c) {
+      const float* tc = tin + c * TT;
+#pragma unroll
+      for (int ky = 0; ky < k; ++ky) {
+        const float* r0 = tc + (ty + ky) * TWx + tx;
+        const float* r1 = r0 + 16 * TWx;
+        const float4* wrow = reinterpret_cast<const float4*>(tw + ((c * taps) + ky * k) * CO);
+#pragma unroll
+        for (int kx = 0; kx < k; ++kx) {
+          const float v0 = r0[kx], v1 = r1[kx];
+#pragma unroll
+          for (int q = 0; q < CO / 4; ++q) {
+            const float4 w4 = wrow[kx * (CO / 4) + q];
+            acc0[4 * q] = fmaf(v0, w4.x, acc0[4 * q]);
+            acc0[4 * q + 1] = fmaf(v0, w4.y, acc0[4 * q + 1]);
+            acc0[4 * q + 2] = fmaf(v0, w4.z, acc0[4 * q + 2]);
+            acc0[4 * q + 3] = fmaf(v0, w4.w, acc0[4 * q + 3]);
+            acc1[4 * q] = fmaf(v1, w4.x, acc1[4 * q]);
+            acc1[4 * q + 1] = fmaf(v1, w4.y, acc1[4 * q + 1]);
+            acc1[4 * q + 2] = fmaf(v1, w4.z, acc1[4 * q + 2]);
+            acc1[4 * q + 3] = fmaf(v1, w4.w, acc1[4 * q + 3]);
+          }
+        }
+      }
+    }
+  }
+  const int ox = ox0 + tx;
+  if (ox >= Wo) return;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int oy = oy0 + ty + 16 * half;
+    if (oy >= Ho) break;
+#pragma unroll
+    for (int co = 0; co < CO; ++co) {
+      if (co >= Cout) break;
+      const int64_t o = (((int64_t)n * Cout + co) * Ho + oy) * Wo + ox;
+      float r = (half ? acc1[co] : acc0[co]) + (bias ? __ldg(bias + co) : 0.0f);
+      if (res) r += res[o];
+      out[o] = r;
+    }
+  }
+}
 // In place (no restrict): x[r * ld + c] = tf32(x[r * ld + c]).
 __global__ void k_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
   GRID_STRIDE(i, rows * cols) {
@@ -642,6 +739,28 @@ void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, 
   else
     k_pack_bf16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
   check_launch("pack_bf16");
+}
+void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
+                        int64_t cq, int64_t Cout, int k, int pad, const float* bias, const float* res, float* out,
+                        int64_t Ho, int64_t Wo) {
+  if (Cout > 8 || k > 15 || N > 65535 || (Ho + kDirTY - 1) / kDirTY > 65535)
+    fail(kErrInvalidArg, "conv_direct: unsupported shape");
+  const int TT = (kDirTX + k - 1) * (kDirTY + k - 1);
+  const size_t smem = (size_t)(((kDirCh * TT + 3) & ~3) + 8 * kDirCh * k * k) * sizeof(float);
+  const dim3 grid((unsigned)((Wo + kDirTX - 1) / kDirTX), (unsigned)((Ho + kDirTY - 1) / kDirTY), (unsigned)N);
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024)
+      check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "conv_direct attr");
+    kern<<<grid, 256, smem, ctx().stream>>>(xh, cp, (int)Cin, (int)H, (int)W, wp, cq, (int)Cout, k, pad,
+                                                            bias, res, out, (int)Ho, (int)Wo);
+  };
+  if (cp % 4 != 0 || (reinterpret_cast<uintptr_t>(xh) & 15) != 0)
+    fail(kErrInvalidArg, "conv_direct: NHWC input must have 16-byte pixel rows");
+  if (Cout <= 4)
+    k == 3 ? go(k_conv_direct_nhwc<4, 3>) : go(k_conv_direct_nhwc<4, 0>);
+  else
+    k == 3 ? go(k_conv_direct_nhwc<8, 3>) : go(k_conv_direct_nhwc<8, 0>);
+  check_launch("conv_direct");
 }
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
   launch_pack_nhwc(x, xh, N, C, 1, HW, cp, nullptr, 1.0f, 0.0f, false, false);

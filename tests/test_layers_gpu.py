@@ -204,6 +204,8 @@ CONV_CASES = [
     (2, 256, 24, 24, 128, 1, 0),
     (1, 64, 5, 300, 256, 3, 1),     # SM pairs: one-row 256-pixel rectangles split left / right
     (1, 40, 20, 70, 320, 3, 1),     # SM pairs: 128 x 2 rectangles split top / bottom, ragged Cout
+    (2, 128, 45, 38, 3, 3, 1),      # few output channels (the VAE's conv_out): direct fp32 kernel
+    (1, 20, 17, 19, 6, 5, 2),       # direct kernel, 5 x 5 taps
 ]
 
 
