@@ -50,6 +50,11 @@ struct ConvGeom {
   int half_dx, half_dy;    // SM pairs: offset of the second CTA's half of the pixel rectangle
   long long img_stride;    // elements between images of the output (Cout * Ho * Wo)
   const float* res;        // residual added in the epilogue (output layout), or null
+  // GroupNorm statistics of the output (null: off): per (image, group, pixel tile) the
+  // count, mean and sum of squared deviations, at gn_part[(img * groups + g) * tiles_img +
+  // tile]. Groups are gn_cg consecutive channels, gn_cg a divisor of 32.
+  float4* gn_part;
+  int gn_cg, gn_groups, tiles_img;
 };
 
 struct GemmParams {
@@ -360,6 +365,21 @@ __device__ __forceinline__ void conv_tile(const ConvGeom& g, int nb, int& img, i
   ox0 = tx * g.BW;
 }
 
+// Chan et al.'s pairwise update of (count, mean, sum of squared deviations).
+__device__ __forceinline__ void chan_merge(float& N, float& mean, float& m2, float n2, float mean2, float m22) {
+  if (n2 == 0.0f) return;
+  if (N == 0.0f) {
+    N = n2;
+    mean = mean2;
+    m2 = m22;
+    return;
+  }
+  const float n = N + n2, d = mean2 - mean;
+  mean += d * (n2 / n);
+  m2 += m22 + d * d * (N * n2 / n);
+  N = n;
+}
+
 // Epilogue of the implicit convolution for one warp: rows (output channels) row_base..+31,
 // this thread's channel row_base + lane. Each 32-column chunk is 32 consecutive pixels of
 // one output row (BW a multiple of 32), or of the flattened image when BW == Wo < 32. The
@@ -378,6 +398,8 @@ __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, u
   float* out = reinterpret_cast<float*>(p.C) + (long long)img * g.img_stride;
   const float* res = g.res ? g.res + (long long)img * g.img_stride : nullptr;
   const int sub = lane >> 3, c4 = (lane & 7) * 4;
+  const bool stats = g.gn_part != nullptr;
+  float sN = 0.0f, sMean = 0.0f, sM2 = 0.0f;  // this lane's channel over the tile's pixels
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     const int j0 = c * 32;
@@ -424,25 +446,65 @@ __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, u
         const float4 a = a4[r0 / 4];
         o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
         *reinterpret_cast<float4*>(out + (long long)ch * hw + pix0 + c4) = o;
+        if (stats) *reinterpret_cast<float4*>(stg + rr * kStgPitch + c4) = o;  // final values, for the statistics
       }
-      __syncwarp();
-      continue;
-    }
+    } else {
 #pragma unroll
-    for (int r0 = 0; r0 < 32; r0 += 4) {
-      const int rr = r0 + sub, ch = row_base + rr;
-      if (ch >= p.M) continue;
-      const long long off = (long long)ch * hw + pix0 + c4;
-      const float* src = stg + rr * kStgPitch + c4;
-      if (vec) {
-        *reinterpret_cast<float4*>(out + off) = *reinterpret_cast<const float4*>(src);
-      } else {
+      for (int r0 = 0; r0 < 32; r0 += 4) {
+        const int rr = r0 + sub, ch = row_base + rr;
+        if (ch >= p.M) continue;
+        const long long off = (long long)ch * hw + pix0 + c4;
+        float* src = stg + rr * kStgPitch + c4;
+        if (vec) {
+          *reinterpret_cast<float4*>(out + off) = *reinterpret_cast<const float4*>(src);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (c4 + e < n) out[off + e] = res ? src[e] + res[off + e] : src[e];
+          for (int e = 0; e < 4; ++e)
+            if (c4 + e < n) {
+              const float o = res ? src[e] + res[off + e] : src[e];
+              out[off + e] = o;
+              if (stats) src[e] = o;
+            }
+        }
       }
     }
     __syncwarp();
+    if (stats) {
+      // This lane's channel over the chunk's n pixels (two passes over registers), merged
+      // into the tile's running statistics.
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(mine + j);
+        v[j] = t.x; v[j + 1] = t.y; v[j + 2] = t.z; v[j + 3] = t.w;
+      }
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) s += j < n ? v[j] : 0.0f;
+      const float mc = s / (float)n;
+      float q = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float d = v[j] - mc;
+        q += j < n ? d * d : 0.0f;
+      }
+      chan_merge(sN, sMean, sM2, (float)n, mc, q);
+      __syncwarp();
+    }
+  }
+  if (stats) {
+    // The group's channels are consecutive lanes (gn_cg divides 32): combine them, and the
+    // group's first lane writes the tile's partial.
+    for (int off = 1; off < g.gn_cg; off <<= 1) {
+      const float n2 = __shfl_xor_sync(0xffffffffu, sN, off);
+      const float mean2 = __shfl_xor_sync(0xffffffffu, sMean, off);
+      const float m22 = __shfl_xor_sync(0xffffffffu, sM2, off);
+      chan_merge(sN, sMean, sM2, n2, mean2, m22);
+    }
+    if (co < p.M && lane % g.gn_cg == 0) {
+      const int tile = nb - img * g.tiles_x * g.tiles_y;
+      g.gn_part[((long long)img * g.gn_groups + co / g.gn_cg) * g.tiles_img + tile] = make_float4(sN, sMean, sM2, 0.0f);
+    }
   }
 }
 
@@ -1103,14 +1165,19 @@ void conv_rect(int bn, int64_t Ho, int64_t Wo, int& bw, int& bh) {
 
 void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
                     int64_t cq, int64_t Cout, int kh, int kw, int pad, const float* bias, const float* res, float* out,
-                    int64_t Ho, int64_t Wo) {
+                    int64_t Ho, int64_t Wo, ConvStats* stats) {
   DeviceContext& c = ctx();
+  if (stats) {
+    const int cg = stats->groups > 0 ? (int)(Cout / stats->groups) : 0;
+    if (cg <= 0 || Cout % stats->groups != 0 || 32 % cg != 0 || Cout % 32 != 0)
+      fail(kErrInvalidArg, "conv_tc: GroupNorm statistics need groups of a divisor of 32 channels and Cout % 32 == 0");
+  }
   if (cp % 4 != 0 || cq % 32 != 0 || cq < Cin || cp < Cin || N <= 0 || Ho <= 0 || Wo <= 0)
     fail(kErrInvalidArg, "conv_tc: bad packed layout");
   if (Cout > (1 << 30) || Ho * Wo > (1ll << 31) || N > 65535)
     fail(kErrInvalidArg, "conv_tc: shape too large");
   // A few output channels would fill a few of a tile's 128 MMA rows: direct kernel instead.
-  if (Cout <= 8 && kh == kw && kh <= 15 && (Ho + 31) / 32 <= 65535 && H * W < (1ll << 31))
+  if (!stats && Cout <= 8 && kh == kw && kh <= 15 && (Ho + 31) / 32 <= 65535 && H * W < (1ll << 31))
     return launch_conv_direct(xh, N, Cin, cp, H, W, wp, cq, Cout, kh, pad, bias, res, out, Ho, Wo);
   // Tile width by the wave-count cost model of choose_bn over the pixel rectangles.
   const int64_t m_tiles = (Cout + kBM - 1) / kBM;
@@ -1188,6 +1255,15 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
   p.cv.half_dy = hy;
   p.cv.img_stride = Cout * Ho * Wo;
   p.cv.res = res;
+  if (stats) {
+    const int64_t tiles_img = (int64_t)p.cv.tiles_x * p.cv.tiles_y;
+    if (N * stats->groups * tiles_img > stats->cap) fail(kErrInvalidArg, "conv_tc: statistics buffer too small");
+    p.cv.gn_part = stats->part;
+    p.cv.gn_groups = stats->groups;
+    p.cv.gn_cg = (int)(Cout / stats->groups);
+    p.cv.tiles_img = (int)tiles_img;
+    stats->tiles_img = tiles_img;
+  }
   p.m_tiles = pair ? (int)((Cout + 2 * kBM - 1) / (2 * kBM)) : (int)m_tiles;
   p.n_tiles = (int)(N * p.cv.tiles_x * p.cv.tiles_y);
   if ((int64_t)p.m_tiles * p.n_tiles > (1ll << 31) - 1) fail(kErrInvalidArg, "conv_tc: too many tiles");

@@ -122,9 +122,24 @@ void launch_gemm_tc(const GemmCall& g);
 // conv(x, w) (+bias[Cout]) (+res, same layout as out). xh is the input in NHWC with a
 // channel pitch cp (% 4 == 0; channels past Cin are ignored) and wp the weights as
 // [Cout, kh, kw, cq] with cq = round_up(Cin, 32), zero past Cin; both tf32-rounded.
+// With stats, the epilogue also writes the output's GroupNorm partial statistics
+// (groups of Cout / groups channels, a divisor of 32; Cout % 32 == 0): per (image, group,
+// pixel tile) float4 {count, mean, sum of squared deviations, 0} at
+// part[(img * groups + g) * tiles_img + tile]; tiles_img is returned. cap is the buffer's
+// capacity in float4; N * groups * Ho * ceil(Wo / 32) always suffices.
+struct ConvStats {
+  float4* part;
+  int64_t cap;
+  int groups;
+  int64_t tiles_img;  // out
+};
 void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
                     int64_t cq, int64_t Cout, int kh, int kw, int pad, const float* bias, const float* res, float* out,
-                    int64_t Ho, int64_t Wo);
+                    int64_t Ho, int64_t Wo, ConvStats* stats = nullptr);
+// GroupNorm scale / shift from a convolution's partial statistics (ConvStats):
+// ab[n * C + c] = (rstd * gamma[c], beta[c] - mean * rstd * gamma[c]).
+void gn_scale_shift_parts(const float4* part, int64_t tiles_img, int64_t N, int64_t C, int groups,
+                          const float* gamma, const float* beta, float eps, float2* ab);
 // NCHW [N, C, H, W] -> NHWC [N, Ho*Wo, cp] tf32, zero past C, with y = x * a + b per
 // channel (ab[n * C + c] = (a, b), or the constants a0, b0 when ab is null), then SiLU if
 // silu; with up2 the output is the nearest 2x upsampling (Ho = 2H, Wo = 2W).

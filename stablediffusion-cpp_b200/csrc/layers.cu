@@ -459,6 +459,57 @@ __global__ void k_gn_finalize(const float2* __restrict__ part, int chunks, int64
     ab[n * C + ch] = make_float2(a, beta[ch] - (float)mean * a);
   }
 }
+// The same from a convolution epilogue's per-tile partials: one block per (sample, group)
+// merges its tiles' (count, mean, M2) in double, pairwise, then writes the affine of the
+// group's channels.
+__global__ void __launch_bounds__(256) k_gn_finalize_parts(const float4* __restrict__ part, int64_t tiles, int64_t C,
+                                                           int groups, const float* __restrict__ gamma,
+                                                           const float* __restrict__ beta, float eps,
+                                                           float2* __restrict__ ab) {
+  __shared__ double sn[256], smean[256], sm2[256];
+  const int64_t seg = blockIdx.x;
+  const float4* q = part + seg * tiles;
+  double N = 0.0, mean = 0.0, m2 = 0.0;
+  auto merge = [](double& Na, double& ma, double& qa, double Nb, double mb, double qb) {
+    if (Nb == 0.0) return;
+    if (Na == 0.0) {
+      Na = Nb;
+      ma = mb;
+      qa = qb;
+      return;
+    }
+    const double n = Na + Nb, d = mb - ma;
+    ma += d * (Nb / n);
+    qa += qb + d * d * (Na * Nb / n);
+    Na = n;
+  };
+  for (int64_t t = threadIdx.x; t < tiles; t += blockDim.x) {
+    const float4 v = q[t];
+    merge(N, mean, m2, (double)v.x, (double)v.y, (double)v.z);
+  }
+  sn[threadIdx.x] = N;
+  smean[threadIdx.x] = mean;
+  sm2[threadIdx.x] = m2;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) {
+      double a = sn[threadIdx.x], b = smean[threadIdx.x], c = sm2[threadIdx.x];
+      merge(a, b, c, sn[threadIdx.x + s], smean[threadIdx.x + s], sm2[threadIdx.x + s]);
+      sn[threadIdx.x] = a;
+      smean[threadIdx.x] = b;
+      sm2[threadIdx.x] = c;
+    }
+    __syncthreads();
+  }
+  const double tot = sn[0], mu = smean[0];
+  const float rstd = (float)(1.0 / sqrt(sm2[0] / (tot > 0.0 ? tot : 1.0) + (double)eps));
+  const int64_t n = seg / groups, g = seg % groups, cg = C / groups;
+  for (int64_t c = threadIdx.x; c < cg; c += blockDim.x) {
+    const int64_t ch = g * cg + c;
+    const float a = rstd * gamma[ch];
+    ab[n * C + ch] = make_float2(a, beta[ch] - (float)mu * a);
+  }
+}
 template <bool VEC>
 __global__ void k_gn_apply(const float* __restrict__ x, float* __restrict__ y, int64_t HW,
                            const float2* __restrict__ ab, int silu) {
@@ -844,6 +895,13 @@ void gn_scale_shift(const float* x, int64_t N, int64_t C, int64_t HW, int groups
                                                             segs);
   check_launch("group_norm_stats");
   pool_free(part);  // stream-ordered reuse
+}
+void gn_scale_shift_parts(const float4* part, int64_t tiles_img, int64_t N, int64_t C, int groups,
+                          const float* gamma, const float* beta, float eps, float2* ab) {
+  if (N * groups > (1ll << 31) - 1) fail(kErrInvalidArg, "group_norm: too many groups");
+  k_gn_finalize_parts<<<(unsigned)(N * groups), 256, 0, ctx().stream>>>(part, tiles_img, C, groups, gamma, beta, eps,
+                                                                        ab);
+  check_launch("group_norm_parts");
 }
 void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
                    const float* beta, float eps, bool silu) {

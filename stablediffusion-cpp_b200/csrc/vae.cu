@@ -114,6 +114,10 @@ struct Vae {
   int64_t latent_ch = 0;
   // activations
   Buf cur, tmp, sc, xh, ab, qkv, att;
+  // GroupNorm partial statistics of cur / tmp written by the convolution that produced them
+  // (tiles per image, or -1 when the producer did not write them)
+  Buf part_cur, part_tmp;
+  int64_t part_cap = 0, cur_tiles = -1, tmp_tiles = -1;
 
   // Optional timing of the tensor-core work (CUDA events on the stream): category 0 the
   // convolutions, 1 the attention (projections, scores, softmax, output); FLOPs are
@@ -263,18 +267,28 @@ struct Vae {
   }
 
   // ---- layers ----------------------------------------------------------------------
-  // conv over an NHWC input already in xh (channel pitch cp_of(c.cin)), NCHW output.
-  void conv(const Conv& c, int64_t N, int64_t H, int64_t W, const float* res, float* out) {
+  // conv over an NHWC input already in xh (channel pitch cp_of(c.cin)), NCHW output. With
+  // part, the epilogue also writes the output's GroupNorm statistics there; returns the
+  // tiles per image, or -1 when it did not (widths the epilogue form does not take).
+  int64_t conv(const Conv& c, int64_t N, int64_t H, int64_t W, const float* res, float* out, Buf* part = nullptr) {
     const int pad = (int)(c.k - 1) / 2;
+    ConvStats st{nullptr, part_cap, kGroups, -1};
+    const bool stats = part && c.cout % 32 == 0 && 32 % (c.cout / kGroups) == 0;
+    if (stats) st.part = static_cast<float4*>(part->p);
     timed(0, 2.0 * N * c.cout * c.cin * c.k * c.k * H * W, [&] {
       launch_conv_tc(xh.f(), N, c.cin, cp_of(c.cin), H, W, c.wp.f(), c.cq, c.cout, (int)c.k, (int)c.k, pad, c.bias,
-                     res, out, H, W);
+                     res, out, H, W, stats ? &st : nullptr);
     });
+    return stats ? st.tiles_img : -1;
   }
-  // xh = pack(silu?(norm(x)))
-  void norm_pack(const Norm& n, const float* x, int64_t N, int64_t C, int64_t H, int64_t W, bool silu) {
+  // xh = pack(silu?(norm(x))); the statistics from the producer's partials when it wrote them
+  void norm_pack(const Norm& n, const float* x, int64_t N, int64_t C, int64_t H, int64_t W, bool silu,
+                 const Buf* part = nullptr, int64_t tiles = -1) {
     float2* abp = static_cast<float2*>(ab.p);
-    gn_scale_shift(x, N, C, H * W, kGroups, n.g, n.b, kVaeEps, abp);
+    if (part && tiles >= 0)
+      gn_scale_shift_parts(static_cast<const float4*>(part->p), tiles, N, C, kGroups, n.g, n.b, kVaeEps, abp);
+    else
+      gn_scale_shift(x, N, C, H * W, kGroups, n.g, n.b, kVaeEps, abp);
     launch_pack_nhwc(x, xh.f(), N, C, H, W, cp_of(C), abp, 1.0f, 0.0f, silu, false);
   }
   // cur [N, cin, H, W] -> cur [N, cout, H, W]
@@ -285,15 +299,20 @@ struct Vae {
       conv(r.sc, N, H, W, nullptr, sc.f());
       res = sc.f();
     }
-    norm_pack(r.n1, cur.f(), N, r.c1.cin, H, W, true);
-    conv(r.c1, N, H, W, nullptr, tmp.f());
-    norm_pack(r.n2, tmp.f(), N, r.c2.cin, H, W, true);
-    conv(r.c2, N, H, W, res, cur.f());  // in place when res == cur: each element read, then written
+    norm_pack(r.n1, cur.f(), N, r.c1.cin, H, W, true, &part_cur, cur_tiles);
+    tmp_tiles = conv(r.c1, N, H, W, nullptr, tmp.f(), &part_tmp);
+    norm_pack(r.n2, tmp.f(), N, r.c2.cin, H, W, true, &part_tmp, tmp_tiles);
+    // in place when res == cur: each element read, then written
+    cur_tiles = conv(r.c2, N, H, W, res, cur.f(), &part_cur);
   }
   void attention(int64_t N, int64_t H, int64_t W) {
     const int64_t C = attn.C, S = H * W;
     float2* abp = static_cast<float2*>(ab.p);
-    gn_scale_shift(cur.f(), N, C, S, kGroups, attn.n.g, attn.n.b, kVaeEps, abp);
+    if (cur_tiles >= 0)
+      gn_scale_shift_parts(static_cast<const float4*>(part_cur.p), cur_tiles, N, C, kGroups, attn.n.g, attn.n.b,
+                           kVaeEps, abp);
+    else
+      gn_scale_shift(cur.f(), N, C, S, kGroups, attn.n.g, attn.n.b, kVaeEps, abp);
     launch_pack_nhwc(cur.f(), xh.f(), N, C, H, W, C, abp, 1.0f, 0.0f, false, false);  // tokens [N*S, C]
     timed(1, 2.0 * N * S * C * 3 * C + 4.0 * N * S * S * C, [&] {
       gemm_tf32_direct(N * S, 3 * C, C, xh.f(), C, attn.wqkv.f(), C, qkv.f(), 3 * C, attn.bqkv.f(), false);
@@ -302,7 +321,7 @@ struct Vae {
       launch_attention_gemm(q, q + C, q + 2 * C, att.f(), N, S, S, 1, 1, C, false, 3 * C, 3 * C, C, true);
       launch_pack_tf32(att.f(), C, xh.f(), C, N * S, C);  // the 1x1 conv's NHWC operand
     });
-    conv(attn.out, N, H, W, cur.f(), cur.f());
+    cur_tiles = conv(attn.out, N, H, W, cur.f(), cur.f(), &part_cur);
   }
 
   // Largest NCHW activation and NHWC convolution input over the decode (elements).
@@ -354,6 +373,14 @@ struct Vae {
     sc.ensure(nchw * 4);
     xh.ensure(nhwc * 4);
     ab.ensure(chs * sizeof(float2));
+    {
+      // the largest statistics buffer: N x 32 groups x Ho x ceil(Wo / 32) tiles bounds every layer
+      const int64_t f = upscale();
+      part_cap = N * kGroups * (h * f) * ((w * f + 31) / 32);
+      part_cur.ensure((size_t)part_cap * sizeof(float4));
+      part_tmp.ensure((size_t)part_cap * sizeof(float4));
+      cur_tiles = tmp_tiles = -1;
+    }
     const int64_t S = h * w;
     qkv.ensure((size_t)(N * S * 3 * attn.C) * 4);
     att.ensure((size_t)(N * S * attn.C) * 4);
@@ -365,7 +392,7 @@ struct Vae {
       launch_pack_nhwc(tmp.f(), xh.f(), N, post_quant.cout, H, W, cp_of(post_quant.cout), nullptr, 1.0f, 0.0f, false,
                        false);
     }
-    conv(conv_in, N, H, W, nullptr, cur.f());
+    cur_tiles = conv(conv_in, N, H, W, nullptr, cur.f(), &part_cur);
     resnet(mid0, N, H, W);
     attention(N, H, W);
     resnet(mid1, N, H, W);
@@ -375,10 +402,10 @@ struct Vae {
         launch_pack_nhwc(cur.f(), xh.f(), N, u.up.cin, H, W, cp_of(u.up.cin), nullptr, 1.0f, 0.0f, false, true);
         H *= 2;
         W *= 2;
-        conv(u.up, N, H, W, nullptr, cur.f());
+        cur_tiles = conv(u.up, N, H, W, nullptr, cur.f(), &part_cur);
       }
     }
-    norm_pack(norm_out, cur.f(), N, conv_out.cin, H, W, true);
+    norm_pack(norm_out, cur.f(), N, conv_out.cin, H, W, true, &part_cur, cur_tiles);
     conv(conv_out, N, H, W, nullptr, out);
   }
   int64_t upscale() const {
