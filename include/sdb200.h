@@ -262,7 +262,8 @@ void sdb200_comm_destroy(void* comm);
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */
 /* backend_cuda.h:46-47 conv2d(): x NCHW [N, Cin, H, W], w [Cout, Cin, kh, kw], out NCHW
  * [N, Cout, Ho, Wo], tf32 tensor cores. Stride 1 runs as an implicit GEMM over an NHWC
- * copy of x (workspace); other strides as im2col + GEMM. */
+ * copy of x (workspace), or for Cout <= 8 as a direct fp32 kernel over the same copy;
+ * other strides as im2col + GEMM. */
 int sdb200_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, const float* w, int64_t Cout,
                   int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho, int64_t Wo);
 /* Extension (no reference counterpart): the implicit-GEMM convolution on operands already
