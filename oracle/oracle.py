@@ -22,6 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libsdref.so")
 REF_CUDA_SO = os.path.join(HERE, "_ref", "libsdref_cuda.so")
+REF_B200_SO = os.path.join(HERE, "_ref", "libsdref_b200.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
@@ -283,6 +284,10 @@ class RefCPU(_Base):
                                             C.c_int], v)
         self.z_free = self.fn("zimage_free", [v])
         self.z_fwd = self.fn("zimage_forward", [v, v, _i64, _i64, _i64, C.c_float, v, _i64, _i64, v], C.c_int)
+        self.u_new = self.fn("unet_new", [v, C.c_int], v)
+        self.u_free = self.fn("unet_free", [v])
+        self.u_fwd = self.fn("unet_forward", [v, v, _i64, _i64, _i64, _i64, C.c_float, v, _i64, _i64, v, C.c_int],
+                             C.c_int)
         self.v_new = self.fn("vae_new", [v, C.c_float, C.c_float], v)
         self.v_free = self.fn("vae_free", [v])
         self.v_dec = self.fn("vae_decode", [v, v, _i64, _i64, _i64, _i64, v, _i64, v], C.c_int)
@@ -433,6 +438,42 @@ class RefCPU(_Base):
             self.w_free(w)
             raise RuntimeError(self.last_error().decode())
         return self._wrap_model(m, w)
+
+    def unet(self, weights: dict, heads: int = 8, on_device: bool = False):
+        """Builds the reference UNet (unet.cpp:18-56) over `weights` (name -> fp32 array);
+        returns f(x [N,C,H,W], t, ctx [N,L,D]) -> out [N,C,H,W] running UNet::forward. With
+        on_device the weights are moved with Weights::to_device and the inputs with
+        Tensor::to (a library with a GPU backend)."""
+        w = self.w_new()
+        for name, arr in weights.items():
+            arr = np.ascontiguousarray(arr, np.float32)
+            shape = (C.c_int64 * arr.ndim)(*arr.shape)
+            self._chk(self.w_add(w, name.encode(), C.cast(shape, C.c_void_p), arr.ndim, _ptr(arr), 0))
+        if on_device:
+            self._chk(self.fn("weights_to_cuda", [C.c_void_p], C.c_int)(w))
+        m = self.u_new(w, heads)
+        if not m:
+            self.w_free(w)
+            raise RuntimeError(self.last_error().decode())
+        ref = self
+
+        class _UNet:
+            def __call__(self, x, t, ctx):
+                x = np.ascontiguousarray(x, np.float32)
+                ctx = np.ascontiguousarray(ctx, np.float32)
+                out = np.empty_like(x)
+                ref._chk(ref.u_fwd(m, _ptr(x), *x.shape, float(t), _ptr(ctx), ctx.shape[1], ctx.shape[2], _ptr(out),
+                                   int(on_device)))
+                return out
+
+            def __del__(self):
+                try:
+                    ref.u_free(m)
+                    ref.w_free(w)
+                except Exception:
+                    pass
+
+        return _UNet()
 
     def vae(self, weights: dict, scaling_factor: float, shift_factor: float):
         """Builds the reference VAEDecoder (vae.cpp:15-32) over `weights` (name -> fp32
@@ -601,3 +642,17 @@ class RefCUDA(RefCPU):
                     pass
 
         return _Vae()
+
+
+class RefOnB200(RefCUDA):
+    """The reference's own model code (tensor.cpp, modules.cpp, unet.cpp, zimage.cpp, vae.cpp)
+    linked against libsdb200.so in place of its backend (oracle/_ref/libsdref_b200.so): the
+    maintainer's drop-in link. Its Device::CUDA paths call this library's sd::cuda
+    functions. Test infrastructure: it checks the boundary, it is not the product."""
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_B200_SO)
+
+    def __init__(self, path: str = REF_B200_SO):
+        super().__init__(path)

@@ -16,6 +16,7 @@
 #include "safetensors.h"
 #include "scheduler.h"
 #include "tensor.h"
+#include "unet.h"
 #include "vae.h"
 #include "zimage.h"
 
@@ -240,6 +241,31 @@ int sdref_cuda_conv2d(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t
                       int64_t kh, int64_t kw, const float* bias, int stride, int pad, float* out, int64_t Ho,
                       int64_t Wo) {
   return guard([&] { cuda::conv2d(x, N, Cin, H, W, w, Cout, kh, kw, bias, stride, pad, out, Ho, Wo); });
+}
+
+// ---- SD 1.x UNet (unet.cpp) on an in-memory Weights ----------------------------------
+void* sdref_unet_new(void* w, int heads) {
+  try {
+    return new UNet(*static_cast<Weights*>(w), heads);
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+void sdref_unet_free(void* m) { delete static_cast<UNet*>(m); }
+// x [N, C, H, W], context [N, L, D] -> out [N, C, H, W]; on_device moves the inputs to the
+// device first (weights already moved with sdref_weights_to_cuda) and the output back.
+int sdref_unet_forward(void* m, const float* x, int64_t N, int64_t C, int64_t H, int64_t W, float t, const float* ctx,
+                       int64_t L, int64_t D, float* out, int on_device) {
+  return guard([&] {
+    Tensor tx = make(x, {N, C, H, W}), tc = make(ctx, {N, L, D});
+    if (on_device) {
+      tx = tx.to(Device::CUDA);
+      tc = tc.to(Device::CUDA);
+    }
+    Tensor y = static_cast<UNet*>(m)->forward(tx, t, tc);
+    put(on_device ? y.to(Device::CPU) : y, out);
+  });
 }
 
 // ---- VAE decoder (vae.cpp) on an in-memory Weights (sdref_weights_new / _add, fp32) --
