@@ -104,3 +104,25 @@ def test_dit_forward_vs_reference_gpu(sdb, rgpu):
     want = ref(x, 0.3, cap)
     got = _np(model.forward(torch.from_numpy(x).cuda(), 0.3, torch.from_numpy(cap).cuda()))
     assert rel_fro(got, want) <= 1e-2
+
+
+def test_dit_full_model_vs_reference_gpu(sdb, rgpu):
+    """BASELINE config 4's model at full size (30 layers + 2 + 2 refiners, 6.15 B parameters)
+    at 1024^2 for one image, against the reference's GPU forward over the same weights: the
+    full-depth parity check the CPU reference is too slow for."""
+    import torch
+
+    from sdb200.zimage import Z_IMAGE, ZImageB200, random_weights_torch
+
+    wts = random_weights_torch(Z_IMAGE, 0, "cuda")
+    model = ZImageB200(wts, Z_IMAGE)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1000)
+    x = torch.randn((1, 16, 128, 128), generator=g, device="cuda")
+    cap = torch.randn((1, 128, Z_IMAGE.cap_dim), generator=g, device="cuda")
+    got = _np(model.forward(x, 0.5, cap))
+    ref = rgpu.zimage_cuda(wts, heads=Z_IMAGE.heads)
+    want = ref(x.cpu().numpy(), 0.5, cap.cpu().numpy())
+    del ref, model, wts
+    torch.cuda.empty_cache()
+    assert rel_fro(got, want) <= 1e-2
