@@ -40,7 +40,9 @@ Printed on rank 0 as one JSON line:
   cpu_baseline the reference's own CPU forward (oracle/_ref, compiled from its sources) on
                a bounded sample: one full-width block at 1024^2, scaled by FLOPs to the step
   gpu_launches kernels this library launched inside the timed region (counted by the library)
---impl reference times the reference's CPU implementation of the same workload (rank 0).
+--impl reference times the reference's CPU implementation of the same workload (rank 0); its line
+also reports the reference's own GPU backend (src/backend_cuda.cu + cuBLAS, built for sm_100a) on
+the same seeded inputs as `reference_gpu` (--no-ref-gpu skips it).
 """
 from __future__ import annotations
 
