@@ -536,7 +536,14 @@ void set_attention_tc(bool on) { g_attention_tc = on; }
 void launch_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                       int heads, int kv_heads, int64_t d, bool causal) {
   if (!g_attention_tc) return launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
-  if (d > 128) return launch_attention_gemm(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+  if (d > 128) {
+    // The GEMM form launches about five kernels per (sample, head) and query chunk; with
+    // small score matrices (the UNet's 64-256 tokens at its deepest levels) the exact
+    // streaming kernel covers all heads in one launch and is faster.
+    if (d <= 512 && (double)N * heads * Sq * (double)Skv <= (double)(1 << 24))
+      return launch_attention_simt(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+    return launch_attention_gemm(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal);
+  }
   const int64_t dp = d <= 64 ? 64 : 128;
   const size_t qb = (size_t)(N * Sq * heads * dp) * 2, kb = (size_t)(N * Skv * kv_heads * dp) * 2;
   auto a256 = [](size_t b) { return (b + 255) & ~size_t(255); };

@@ -71,7 +71,27 @@ struct GemmParams {
   QkvRope rope;  // Epi::kQkvRope
   ScatterOut sc;  // Epi::kScatter
   ConvGeom cv;    // implicit-GEMM convolution (k_gemm_tc<BN, true, true>)
+  // Split-K (convolution only): work item t is split t / base_tiles of tile t % base_tiles,
+  // K blocks [split * kb_split, +kb_split); the epilogue stores split s's partial tile at
+  // C + s * split_stride (no bias or residual; a reduction kernel adds them).
+  int splits, base_tiles, kb_split;
+  long long split_stride;
 };
+
+// Work item t -> tile index and K-block range.
+__device__ __forceinline__ void split_item(const GemmParams& p, int t, int& tile, int& kb0, int& kb1, int& split) {
+  if (p.splits > 1) {
+    split = t / p.base_tiles;
+    tile = t - split * p.base_tiles;
+    kb0 = split * p.kb_split;
+    kb1 = min(p.k_blocks, kb0 + p.kb_split);
+  } else {
+    split = 0;
+    tile = t;
+    kb0 = 0;
+    kb1 = p.k_blocks;
+  }
+}
 
 constexpr int kStgPitch = 36;  // floats per staged row: 16-byte aligned, spreads banks
 
@@ -388,14 +408,14 @@ __device__ __forceinline__ void chan_merge(float& N, float& mean, float& m2, flo
 // one channel plane (Ho * Wo * 4 bytes) apart.
 template <int BN>
 __device__ __forceinline__ void epilogue_conv(const GemmParams& p, float* stg, uint32_t tbase, int row_base, int nb,
-                                              int lane) {
+                                              int lane, int split = 0) {
   const ConvGeom& g = p.cv;
   int img, oy0, ox0;
   conv_tile(g, nb, img, oy0, ox0);
   const long long hw = (long long)g.Ho * g.Wo;
   const int co = row_base + lane;
   const float bias = (co < p.M && p.bias) ? __ldg(p.bias + co) : 0.0f;
-  float* out = reinterpret_cast<float*>(p.C) + (long long)img * g.img_stride;
+  float* out = reinterpret_cast<float*>(p.C) + (long long)split * p.split_stride + (long long)img * g.img_stride;
   const float* res = g.res ? g.res + (long long)img * g.img_stride : nullptr;
   const int sub = lane >> 3, c4 = (lane & 7) * 4;
   const bool stats = g.gn_part != nullptr;
@@ -569,11 +589,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t last_par = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int mb, nb;
-        tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+        int mb, nb, tile, kb0, kb1, split;
+        split_item(p, t, tile, kb0, kb1, split);
+        tile_coords(tile, p.m_tiles, p.n_tiles, mb, nb);
         int img = 0, oy0 = 0, ox0 = 0;
         if constexpr (CONV) conv_tile(p.cv, nb, img, oy0, ox0);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -623,7 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        int tile, kb0, kb1, split;
+        split_item(p, t, tile, kb0, kb1, split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) {
             ok = false;
             break;
@@ -636,9 +659,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t ad = sdesc_k_sw128(a0 + k * 32);
             const uint64_t bd = sdesc_k_sw128(b0 + k * 32);
             if (TF32)
-              umma_tf32_ss(d, ad, bd, IDESC, (kb | k) != 0);
+              umma_tf32_ss(d, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
             else
-              umma_f16_ss(d, ad, bd, IDESC, (kb | k) != 0);
+              umma_f16_ss(d, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -668,13 +691,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int mb, nb;
-      tile_coords(t, p.m_tiles, p.n_tiles, mb, nb);
+      int mb, nb, tile, kb0, kb1, split;
+      split_item(p, t, tile, kb0, kb1, split);
+      tile_coords(tile, p.m_tiles, p.n_tiles, mb, nb);
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       if constexpr (CONV)
-        epilogue_conv<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
+        epilogue_conv<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane, split);
       else
         epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
       tc_fence_before();
@@ -1283,10 +1307,36 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
     check_launch("conv_tc_pair");
     return;
   }
+  // Split-K when the output has few tiles for the SMs and K is long (the UNet's deepest 3x3
+  // convolutions: 8 x 8 or 16 x 16 pixels at 1280 channels, K up to 23040): the splits'
+  // partial outputs go to a workspace and one pass adds them with the bias and residual.
+  float* part = nullptr;
+  if (!stats && p.num_tiles * 2 <= c.num_sms && p.k_blocks >= 32) {
+    const int want = std::min(c.num_sms / p.num_tiles, p.k_blocks / 16);
+    if (want >= 2) {
+      const int kb_split = (p.k_blocks + want - 1) / want;
+      const int used = (p.k_blocks + kb_split - 1) / kb_split;
+      const long long total = N * Cout * Ho * Wo;
+      part = static_cast<float*>(pool_malloc((size_t)(used * total) * sizeof(float)));
+      p.splits = used;
+      p.base_tiles = p.num_tiles;
+      p.kb_split = kb_split;
+      p.split_stride = total;
+      p.num_tiles = p.num_tiles * used;
+      p.C = part;
+      p.bias = nullptr;
+      p.cv.res = nullptr;
+      p.vec_ok = (Ho * Wo) % 4 == 0;
+    }
+  }
   switch (bn) {
     case 256: launch_conv_bn<256>(ta, tb, p, c.num_sms, c.device, c.stream); break;
     case 128: launch_conv_bn<128>(ta, tb, p, c.num_sms, c.device, c.stream); break;
     default: launch_conv_bn<64>(ta, tb, p, c.num_sms, c.device, c.stream); break;
+  }
+  if (part) {
+    launch_split_reduce(part, p.splits, N * Cout * Ho * Wo, Cout, Ho * Wo, bias, res, out);
+    pool_free(part);  // stream-ordered reuse
   }
 }
 

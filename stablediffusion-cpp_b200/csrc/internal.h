@@ -149,6 +149,10 @@ void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H
 // ab[n * C + c] = (rstd * gamma[c], beta[c] - mean * rstd * gamma[c]).
 void gn_scale_shift(const float* x, int64_t N, int64_t C, int64_t HW, int groups, const float* gamma,
                     const float* beta, float eps, float2* ab);
+// out[i] = sum over s < splits of part[s * total + i] (+ bias[(i / hw) % C]) (+ res[i]):
+// the reduction of a split-K convolution (res may alias out).
+void launch_split_reduce(const float* part, int splits, int64_t total, int64_t C, int64_t hw, const float* bias,
+                         const float* res, float* out);
 // The same convolution (square kernel k) as a direct fp32 SIMT kernel, for Cout <= 8.
 void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
                         int64_t cq, int64_t Cout, int k, int pad, const float* bias, const float* res, float* out,

@@ -271,6 +271,17 @@ __global__ void __launch_bounds__(256) k_conv_direct_nhwc(
     }
   }
 }
+// Split-K reduction (deterministic: the splits are summed in order).
+__global__ void k_split_reduce(const float* __restrict__ part, int splits, int64_t total, int64_t C, int64_t hw,
+                               const float* __restrict__ bias, const float* res, float* out) {
+  GRID_STRIDE(i, total) {
+    float s = part[i];
+    for (int k = 1; k < splits; ++k) s += part[k * total + i];
+    if (bias) s += __ldg(bias + (i / hw) % C);
+    if (res) s += res[i];
+    out[i] = s;
+  }
+}
 // In place (no restrict): x[r * ld + c] = tf32(x[r * ld + c]).
 __global__ void k_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
   GRID_STRIDE(i, rows * cols) {
@@ -812,6 +823,12 @@ void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int
   else
     k == 3 ? go(k_conv_direct_nhwc<8, 3>) : go(k_conv_direct_nhwc<8, 0>);
   check_launch("conv_direct");
+}
+void launch_split_reduce(const float* part, int splits, int64_t total, int64_t C, int64_t hw, const float* bias,
+                         const float* res, float* out) {
+  if (total <= 0) return;
+  k_split_reduce<<<grid_for(total), kT, 0, ctx().stream>>>(part, splits, total, C, hw, bias, res, out);
+  check_launch("split_reduce");
 }
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
   launch_pack_nhwc(x, xh, N, C, 1, HW, cp, nullptr, 1.0f, 0.0f, false, false);

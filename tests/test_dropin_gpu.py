@@ -73,3 +73,38 @@ def test_vae_on_this_library(sdb, ref, dropin):
     want = ref.vae(w, cfg.scaling_factor, cfg.shift_factor)(z)
     got = dropin.vae_cuda(w, cfg.scaling_factor, cfg.shift_factor)(z)
     assert rel_fro(got, want) <= TOL_OUT
+
+
+def test_sd15_unet_step_through_both_backends(sdb, dropin, capsys):
+    """BASELINE config 2 in full: the reference's own UNet (SD 1.5 widths 320/640/1280/1280, 2
+    layers per block, 8 heads, 77 x 768 text states) at 512^2 with a batch of 2, as its CFG
+    pipeline runs it, once through its own GPU backend (backend_cuda.cu + cuBLAS) and once
+    through this library (the drop-in link), same weights and inputs. The outputs agree at
+    the output gate; the step times are printed (-s) as the relink speed-up."""
+    import time
+
+    from oracle import RefCUDA
+    from unet_weights import unet_weights
+
+    if not RefCUDA.available():
+        pytest.skip("oracle/_ref/libsdref_cuda.so not built here")
+    cfg = dict(channels=(320, 640, 1280, 1280), layers=2, in_ch=4, ctx_dim=768, attn=(True, True, True, False))
+    w = unet_weights(seed=3, device="cuda", **cfg)
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((2, 4, 64, 64)).astype(np.float32)
+    ctx = rng.standard_normal((2, 77, 768)).astype(np.float32)
+    times, outs = {}, {}
+    for name, lib in (("reference backend", RefCUDA()), ("this library", dropin)):
+        m = lib.unet(w, heads=8, on_device=True)
+        m(x, 500.0, ctx)  # warm-up: allocator caches, cuBLAS / tensor maps
+        t0 = time.perf_counter()
+        for _ in range(3):
+            outs[name] = m(x, 500.0, ctx)
+        times[name] = (time.perf_counter() - t0) / 3 * 1e3
+        del m
+    err = rel_fro(outs["this library"], outs["reference backend"])
+    with capsys.disabled():
+        print(f"\nSD 1.5 UNet step @512^2, batch 2 (ms, wall clock incl. latent in / out): "
+              f"reference backend {times['reference backend']:.1f}, this library {times['this library']:.1f}, "
+              f"outputs agree to {err:.2e}")
+    assert err <= TOL_OUT

@@ -83,17 +83,36 @@ def unet_specs(channels=(64, 128), layers=1, in_ch=4, ctx_dim=96, attn=(True, Fa
     return s
 
 
-def unet_weights(seed=0, **cfg):
+def unet_weights(seed=0, device=None, **cfg):
+    """name -> fp32 numpy array. With device (a torch CUDA device) the numbers are drawn
+    there (a full-size UNet's 860 M parameters in a second) and copied to the host."""
+    if device is not None:
+        import torch
+
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        out = {}
+        for name, shape in unet_specs(**cfg):
+            leaf = name.rsplit(".", 1)[0]
+            t = torch.randn(shape, generator=g, device=device)
+            if name.endswith(".weight") and len(shape) >= 2:
+                t *= 1.0 / float(np.sqrt(np.prod(shape[1:])))
+            elif name.endswith(".bias"):
+                t *= 0.1 if "norm" in leaf.rsplit(".", 1)[-1] else 0.02
+            else:
+                t = 1.0 + 0.1 * t
+            out[name] = t.cpu().numpy()
+        return out
     rng = np.random.default_rng(seed)
     out = {}
     for name, shape in unet_specs(**cfg):
         leaf = name.rsplit(".", 1)[0]
+        a = rng.standard_normal(shape, dtype=np.float32)
         if name.endswith(".weight") and len(shape) >= 2:
-            a = rng.standard_normal(shape) / np.sqrt(np.prod(shape[1:]))
+            a *= np.float32(1.0 / np.sqrt(np.prod(shape[1:])))
         elif name.endswith(".bias"):
-            is_norm = any(k in leaf.rsplit(".", 1)[-1] for k in ("norm",))
-            a = (0.1 if is_norm else 0.02) * rng.standard_normal(shape)
+            a *= np.float32(0.1 if "norm" in leaf.rsplit(".", 1)[-1] else 0.02)
         else:  # norm gamma
-            a = 1.0 + 0.1 * rng.standard_normal(shape)
-        out[name] = a.astype(np.float32)
+            a = np.float32(1.0) + np.float32(0.1) * a
+        out[name] = a
     return out
