@@ -447,6 +447,36 @@ __global__ void k_pack_heads_f16(const float* __restrict__ x, __half* __restrict
   }
 }
 
+// q, k and v packed by one launch: segment 0 has qn = rows_q * Hq * dp elements, segments
+// 1 and 2 kn = rows_kv * Hkv * dp each.
+__global__ void k_pack_qkv_f16(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                               __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16,
+                               int64_t qn, int64_t kn, int d, int dp) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < qn + 2 * kn;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float* x = q;
+    __half* y = q16;
+    int64_t j = i;
+    if (j >= qn) {
+      j -= qn;
+      x = k;
+      y = k16;
+      if (j >= kn) {
+        j -= kn;
+        x = v;
+        y = v16;
+      }
+    }
+    const int c = (int)(j % dp);
+    float val = 0.0f;
+    if (c < d) {
+      val = x[(j / dp) * d + c];
+      if (!isnan(val)) val = fminf(fmaxf(val, -65504.0f), 65504.0f);
+    }
+    y[j] = __float2half_rn(val);
+  }
+}
+
 template <int DP>
 void launch_tc(const __half* q, const __half* k, const __half* v, void* out, long long out_row, long long out_batch,
                bool out_bf16, int64_t N, int64_t Sq, int64_t Skv, int heads, int kv_heads, int64_t d, bool causal,
@@ -551,9 +581,13 @@ void launch_attention(const float* q, const float* k, const float* v, float* out
   void* q16 = ws;
   void* k16 = ws + a256(qb);
   void* v16 = ws + a256(qb) + a256(kb);
-  launch_pack_heads_f16(q, q16, N * Sq, heads, d, dp);
-  launch_pack_heads_f16(k, k16, N * Skv, kv_heads, d, dp);
-  launch_pack_heads_f16(v, v16, N * Skv, kv_heads, d, dp);
+  {
+    const int64_t qn = N * Sq * heads * dp, kn = N * Skv * kv_heads * dp;
+    const int64_t blocks = std::min<int64_t>((qn + 2 * kn + 255) / 256, (int64_t)ctx().num_sms * 16);
+    k_pack_qkv_f16<<<(unsigned)blocks, 256, 0, ctx().stream>>>(q, k, v, (__half*)q16, (__half*)k16, (__half*)v16, qn,
+                                                               kn, (int)d, (int)dp);
+    check_launch("pack_qkv_f16");
+  }
   launch_attention_f16(q16, k16, v16, out, (long long)heads * d, (long long)Sq * heads * d, false, N, Sq, Skv, heads,
                        kv_heads, d, dp, causal);
 }

@@ -183,6 +183,9 @@ void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* 
 
 // Layer ops (layers.cu); arguments already validated by the caller.
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols);
+// launch_pack_tf32 of two matrices with the same column count, in one launch.
+void launch_pack_tf32_pair(const float* s0, int64_t ld0, float* d0, int64_t ldo0, int64_t r0, const float* s1,
+                           int64_t ld1, float* d1, int64_t ldo1, int64_t r1, int64_t cols);
 // x[r, c] rounded to tf32 in place (rows x cols, ld elements apart).
 void launch_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols);
 // GroupNorm over N samples of C channels x HW values (optionally followed by SiLU).

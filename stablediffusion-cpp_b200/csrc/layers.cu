@@ -282,6 +282,21 @@ __global__ void k_split_reduce(const float* __restrict__ part, int splits, int64
     out[i] = s;
   }
 }
+// Two matrices packed to the tf32 grid by one launch (the A and B operands of one GEMM).
+__global__ void k_pack_tf32_pair(const float* __restrict__ s0, int64_t ld0, float* __restrict__ d0, int64_t ldo0,
+                                 int64_t r0, const float* __restrict__ s1, int64_t ld1, float* __restrict__ d1,
+                                 int64_t ldo1, int64_t r1, int64_t cols) {
+  const int64_t n0 = r0 * cols;
+  GRID_STRIDE(i, n0 + r1 * cols) {
+    if (i < n0) {
+      const int64_t r = i / cols, c = i - r * cols;
+      d0[r * ldo0 + c] = round_tf32(s0[r * ld0 + c]);
+    } else {
+      const int64_t j = i - n0, r = j / cols, c = j - r * cols;
+      d1[r * ldo1 + c] = round_tf32(s1[r * ld1 + c]);
+    }
+  }
+}
 // In place (no restrict): x[r * ld + c] = tf32(x[r * ld + c]).
 __global__ void k_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
   GRID_STRIDE(i, rows * cols) {
@@ -856,6 +871,13 @@ void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int
   if (rows <= 0 || cols <= 0) return;
   k_pack_tf32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
   check_launch("pack_tf32");
+}
+void launch_pack_tf32_pair(const float* s0, int64_t ld0, float* d0, int64_t ldo0, int64_t r0, const float* s1,
+                           int64_t ld1, float* d1, int64_t ldo1, int64_t r1, int64_t cols) {
+  if (cols <= 0 || r0 + r1 <= 0) return;
+  k_pack_tf32_pair<<<grid_for((r0 + r1) * cols), kT, 0, ctx().stream>>>(s0, ld0, d0, ldo0, r0, s1, ld1, d1, ldo1, r1,
+                                                                        cols);
+  check_launch("pack_tf32_pair");
 }
 void launch_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return;

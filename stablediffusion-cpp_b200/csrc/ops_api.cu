@@ -104,8 +104,7 @@ void gemm_f32_core(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
   uint8_t* ws = static_cast<uint8_t*>(workspace(a_bytes + b_bytes));
   float* pa = reinterpret_cast<float*>(ws);
   float* pb = reinterpret_cast<float*>(ws + a_bytes);
-  launch_pack_tf32(A, lda, pa, Kp, M, K);
-  launch_pack_tf32(B, ldb, pb, Kp, N, K);
+  launch_pack_tf32_pair(A, lda, pa, Kp, M, B, ldb, pb, Kp, N, K);
   GemmCall g{};
   g.M = M;
   g.N = N;
