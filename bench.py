@@ -602,6 +602,7 @@ def run_dit_tp(args, world, rank, local, pg, dev):
     torch.cuda.empty_cache()
     model = ZImageB200(shards, cfg)
     comm = Comm(rank, world, None)
+    comm.set_barrier(args.tp_barrier == "flags")
     model.set_tp(comm, mode=args.tp_mode)
     g = torch.Generator(device=dev)
     g.manual_seed(2000)  # every rank holds the same image and text states
@@ -649,7 +650,8 @@ def run_dit_tp(args, world, rank, local, pg, dev):
                        "(column QKV/w1/w3, row to_out/w2; " + (
                            "partial rows scattered to their owner rank from the GEMM epilogue over NVLink, "
                            "sequence-sharded post-norm broadcasting the next bf16 input)" if args.tp_mode == 1 else
-                           "NCCL all-reduce fp32)")},
+                           "NCCL all-reduce fp32)"),
+                       "tp_barrier": args.tp_barrier if args.tp_mode == 1 else None},
             "step_tflops": fl["total"] / (ms_step * 1e-3) / 1e12,
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc_pair / k_gemm_tc (all GEMMs of one step, rank 0)", "achieved": gemm_tf,
@@ -1067,6 +1069,9 @@ def main():
     ap.add_argument("--tp-mode", type=int, default=1, choices=[0, 1],
                     help="dit_tp: 1 = exchange fused into the GEMM epilogue and post-norm over NVLink, "
                          "0 = NCCL all-reduce")
+    ap.add_argument("--tp-barrier", default="flags", choices=["flags", "nccl"],
+                    help="dit_tp --tp-mode 1: barrier between the fused kernels, a flag exchange over "
+                         "NVLink or a 4-byte NCCL all-reduce")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()

@@ -257,6 +257,10 @@ int sdb200_comm_unique_id(void* out128);
 void* sdb200_comm_create(const void* unique_id128, int rank, int world);
 /* In-place sum all-reduce of n fp32 values on the current device's stream. */
 int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n);
+/* Extension: the stream-ordered barrier between the fused tensor-parallel kernels is a
+ * flag exchange over NVLink (flags != 0, default) or a 4-byte NCCL all-reduce (0). Every
+ * rank of the group sets the same. */
+int sdb200_comm_set_barrier(void* comm, int flags);
 void sdb200_comm_destroy(void* comm);
 
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */

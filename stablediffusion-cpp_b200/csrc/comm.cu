@@ -13,9 +13,12 @@
 // all-gather), so kernels can store straight into a peer's memory over NVLink. The
 // fused tensor-parallel path uses them: the row-parallel GEMMs scatter their partial
 // tiles into the owner rank's slots from the epilogue, and the post-norm kernel
-// broadcasts the next GEMM's bf16 input rows. comm_barrier (a 4-byte all-reduce on the
-// stream) orders those kernels across ranks; kernels that store to peers end with a
-// system-scope fence.
+// broadcasts the next GEMM's bf16 input rows. comm_barrier orders those kernels across
+// ranks; kernels that store to peers end with a system-scope fence. The barrier is a flag
+// exchange through a symmetric buffer (k_flag_barrier: each rank stores its epoch into
+// every peer's flag word with a system-scope release, then waits, bounded, until every
+// peer's epoch has arrived in its own), a few microseconds where a 4-byte NCCL all-reduce
+// takes tens; the all-reduce form stays selectable (sdb200_comm_set_barrier).
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -25,6 +28,7 @@
 #include <vector>
 
 #include "internal.h"
+#include "ptx.cuh"
 #include "sdb200.h"
 
 namespace sdb {
@@ -74,9 +78,38 @@ void check_nccl(ncclResult_t r, const char* what) {
 struct Comm {
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1, device = -1;
-  float* bar = nullptr;     // device word of comm_barrier
+  float* bar = nullptr;     // device word of the all-reduce barrier
   uint8_t* hbuf = nullptr;  // device staging of the IPC handle exchange (world x 64 bytes)
+  SymBuf flags;             // uint32 per peer: the last barrier epoch that peer reached
+  uint32_t epoch = 0;
+  bool flag_barrier = true;
 };
+
+namespace {
+struct FlagPtrs {
+  uint32_t* p[kMaxTpRanks];
+};
+// One warp: lane i < world stores this rank's epoch into peer i's flag word `rank`
+// (release, system scope: the stores of earlier kernels on this stream, fenced system-wide
+// by those kernels, are visible to the peer first), then waits until peer i's epoch is in
+// this rank's flag word i (acquire, system scope). Bounded: after kWaitLimitNs it records
+// kErrTpBarrier and returns.
+__global__ void k_flag_barrier(FlagPtrs peers, const uint32_t* mine, int rank, int world, uint32_t epoch, int* err) {
+  const int i = threadIdx.x;
+  if (i >= world) return;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.p[i] + rank), "r"(epoch) : "memory");
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + i) : "memory");
+    if ((int32_t)(v - epoch) >= 0) break;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(err, kErrTpBarrier);
+      break;
+    }
+  }
+}
+}  // namespace
 
 // Sum all-reduce of n fp32 values in place on the calling context's stream.
 void comm_allreduce_sum(Comm* c, float* buf, size_t n) {
@@ -90,7 +123,23 @@ int comm_rank(const Comm* c) { return c ? c->rank : 0; }
 // work after it sees what every rank's earlier kernels stored into its memory.
 void comm_barrier(Comm* c) {
   if (!c || c->world <= 1) return;
+  if (c->flag_barrier && c->flags.local) {
+    FlagPtrs fp{};
+    for (int r = 0; r < c->world; ++r) fp.p[r] = static_cast<uint32_t*>(c->flags.peer[r]);
+    ++c->epoch;
+    k_flag_barrier<<<1, 32, 0, ctx().stream>>>(fp, static_cast<const uint32_t*>(c->flags.local), c->rank, c->world,
+                                               c->epoch, ctx().err_word);
+    check_launch("flag_barrier");
+    return;
+  }
   check_nccl(nccl().AllReduce(c->bar, c->bar, 1, ncclFloat32, ncclSum, c->comm, ctx().stream), "ncclAllReduce(barrier)");
+}
+
+// The all-reduce barrier followed by a stream synchronize (set-up only).
+void comm_barrier_nccl_sync(Comm* c) {
+  if (!c || c->world <= 1) return;
+  check_nccl(nccl().AllReduce(c->bar, c->bar, 1, ncclFloat32, ncclSum, c->comm, ctx().stream), "ncclAllReduce(barrier)");
+  check_cuda(cudaStreamSynchronize(ctx().stream), "comm: set-up barrier");
 }
 
 // recv[r * bytes ...] = rank r's send (in place when send == recv + rank * bytes).
@@ -173,7 +222,13 @@ void* sdb200_comm_create(const void* unique_id, int rank, int world) {
         sdb::check_cuda(cudaMalloc(&c->bar, 256), "comm: barrier word");
         sdb::check_cuda(cudaMemset(c->bar, 0, 256), "comm: barrier word");
         sdb::check_cuda(cudaMalloc(&c->hbuf, (size_t)world * 64), "comm: handle staging");
+        // The flag words start at zero on every rank before any peer can reach them: the
+        // handle exchange inside comm_sym_alloc follows the memset on every rank's stream.
+        sdb::comm_sym_alloc(c, c->flags, 256);
+        sdb::check_cuda(cudaMemsetAsync(c->flags.local, 0, 256, sdb::ctx().stream), "comm: flag words");
+        sdb::comm_barrier_nccl_sync(c);
       } catch (...) {
+        sdb::comm_sym_free(c, c->flags);
         if (c->comm) sdb::nccl().CommDestroy(c->comm);
         cudaFree(c->bar);
         cudaFree(c->hbuf);
@@ -199,9 +254,24 @@ int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n) {
   }
 }
 
+int sdb200_comm_set_barrier(void* comm, int flags) {
+  try {
+    if (!comm) sdb::fail(sdb::kErrInvalidArg, "comm_set_barrier: null communicator");
+    static_cast<Comm*>(comm)->flag_barrier = flags != 0;
+    return sdb::kOk;
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return e.code;
+  }
+}
+
 void sdb200_comm_destroy(void* comm) {
   Comm* c = static_cast<Comm*>(comm);
   if (!c) return;
+  try {
+    sdb::comm_sym_free(c, c->flags);
+  } catch (...) {
+  }
   if (c->comm) {
     try {
       sdb::nccl().CommDestroy(c->comm);

@@ -245,6 +245,7 @@ void comm_allreduce_sum(Comm* c, float* buf, size_t n);
 int comm_world(const Comm* c);
 int comm_rank(const Comm* c);
 void comm_barrier(Comm* c);
+void comm_barrier_nccl_sync(Comm* c);
 void comm_allgather(Comm* c, const void* send, void* recv, size_t bytes);
 void comm_sym_alloc(Comm* c, SymBuf& b, size_t bytes);
 void comm_sym_free(Comm* c, SymBuf& b);

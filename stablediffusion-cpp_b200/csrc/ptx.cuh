@@ -27,6 +27,7 @@ enum : int {
   kErrWaitAccEmpty = 8,   // MMA issuer waited too long for a drained accumulator
   kErrWaitDrain = 16,     // teardown waited too long for in-flight copies
   kErrAttnWait = 32,      // attention pipeline wait timed out
+  kErrTpBarrier = 64,     // tensor-parallel flag barrier: a peer did not arrive in time
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -104,6 +104,13 @@ class Comm:
             raise RuntimeError(L.sdb200_last_error().decode())
         self.rank, self.world = rank, world
 
+    def set_barrier(self, flags: bool):
+        """Barrier between the fused tensor-parallel kernels: a flag exchange over NVLink
+        (True, the default) or a 4-byte NCCL all-reduce (False). Same on every rank."""
+        from . import check, lib
+
+        check(lib().sdb200_comm_set_barrier(self.handle, 1 if flags else 0))
+
     def allreduce_sum_(self, t):
         """In-place sum over the group of a CUDA float32 tensor."""
         from . import backend, check, lib

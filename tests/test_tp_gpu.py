@@ -2,7 +2,8 @@
 (relative Frobenius <= 1e-3, only the order of the fp32 partial sums differs) and the CPU
 oracle (<= 1e-2), with all ranks holding identical outputs. Both exchange modes: the
 row-parallel partial outputs scattered to their owner rank from the GEMM epilogue and
-reduced in the sequence-sharded post-norm (default), and an NCCL all-reduce. Also each
+reduced in the sequence-sharded post-norm (default; ordered by a flag barrier over NVLink,
+bit-identical to the same with an NCCL all-reduce as the barrier), and an NCCL all-reduce. Also each
 rank reading only its shard from a checkpoint file (sdb200_zimage_load) against the
 same shards registered from memory (identical outputs). Skipped where fewer than 2 GPUs
 are visible."""
@@ -42,3 +43,4 @@ def test_tensor_parallel_forward_two_gpus():
     assert r["allreduce_rel_vs_single_gpu"] <= 1e-3, r
     assert r["allreduce_rel_vs_oracle"] <= 1e-2, r
     assert r["checkpoint_vs_memory_max_diff"] == 0.0, r
+    assert r["barrier_flags_vs_nccl_max_diff"] == 0.0, r

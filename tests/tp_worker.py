@@ -1,6 +1,7 @@
 """Worker run under torchrun by tests/test_tp_gpu.py: the Z-Image forward with tensor
 parallelism over the launched GPUs (heads 3 and FFN 528 split unevenly over 2 ranks), in
-both exchange modes (fused into the kernels over NVLink, and NCCL all-reduce), against
+both exchange modes (fused into the kernels over NVLink - ordered by the flag barrier and
+by the NCCL barrier - and NCCL all-reduce), against
 the single-GPU forward and the CPU oracle, and the same model loaded per rank from a
 checkpoint file. Rank 0 prints one JSON line."""
 import datetime
@@ -36,8 +37,11 @@ def main():
     m = ZImageB200(shard_weights(w, cfg.heads, 128, rank, world), cfg, bf16_names=bf)
     ys = {}
     diffs = []
-    for mode in (1, 0):  # 1: exchange fused into the GEMM epilogue / post-norm, 0: NCCL all-reduce
-        m.set_tp(comm, mode=mode)
+    # 1: exchange fused into the GEMM epilogue / post-norm, ordered by the flag barrier over
+    # NVLink; "1n": the same with the NCCL all-reduce barrier; 0: NCCL all-reduce of the outputs
+    for mode in (1, "1n", 0):
+        comm.set_barrier(mode != "1n")
+        m.set_tp(comm, mode=1 if mode == "1n" else mode)
         y = m.forward(xt, 0.6, capt)
         y = m.forward(xt, 0.6, capt)  # second call reuses the peer mappings
         torch.cuda.synchronize()
@@ -89,6 +93,7 @@ def main():
                           "allreduce_rel_vs_single_gpu": rel(allred, single),
                           "allreduce_rel_vs_oracle": rel(allred, want), "max_rank_diff": float(t.item()),
                           "checkpoint_vs_memory_max_diff": float(file_diff.item()),
+                          "barrier_flags_vs_nccl_max_diff": float(np.abs(fused - ys["1n"].cpu().numpy()).max()),
                           "finite": bool(np.isfinite(fused).all() and np.isfinite(allred).all()),
                           "err_word": sdb200.backend.device_error_word()}), flush=True)
     comm.close()
