@@ -174,6 +174,59 @@ __global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ w
     wp[i] = ci < Cin ? round_tf32(__ldg(w + (co * Cin + ci) * taps + t)) : 0.0f;
   }
 }
+// The same pack, one block per output channel: the channel's [Cin, taps] slab is read
+// contiguously into shared memory, then written as [taps, cq] with contiguous stores (the
+// gather above reads with a stride of `taps` floats and re-reads each line once per tap).
+// Shared-memory reads at stride taps are conflict-free for odd taps. Each thread keeps 8
+// loads in flight (16-byte loads when the slab is 16-byte aligned).
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_conv_pack_w_slab(const float* __restrict__ w, float* __restrict__ wp,
+                                                          int Cin, int taps, int cq) {
+  extern __shared__ float4 slab4[];
+  float* slab = reinterpret_cast<float*>(slab4);
+  const int64_t co = blockIdx.x;
+  const int n = Cin * taps;
+  const float* src = w + co * n;
+  constexpr int kU = 8;
+  if (VEC) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    const int n4 = n >> 2;
+    for (int j0 = threadIdx.x; j0 < n4; j0 += kU * 256) {
+      float4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + u * 256;
+        if (j < n4) v[u] = __ldg(s4 + j);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + u * 256;
+        if (j < n4) slab4[j] = v[u];
+      }
+    }
+  } else {
+    for (int j0 = threadIdx.x; j0 < n; j0 += kU * 256) {
+      float v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + u * 256;
+        if (j < n) v[u] = __ldg(src + j);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + u * 256;
+        if (j < n) slab[j] = v[u];
+      }
+    }
+  }
+  __syncthreads();
+  float* dst = wp + co * (int64_t)taps * cq;
+  const int m = taps * cq;
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    const int t = i / cq, ci = i - t * cq;
+    dst[i] = ci < Cin ? round_tf32(slab[ci * taps + t]) : 0.0f;
+  }
+}
 // Direct convolution for layers with few output channels (the VAE's conv_out, 128 -> 3):
 // on the tensor cores such a layer would fill 3 of a tile's 128 rows. Operands are the
 // implicit-GEMM path's: xh NHWC (channel pitch cp, tf32 values), wp [Cout, taps, cq].
@@ -864,7 +917,22 @@ void launch_pack_nhwc(const float* x, float* xh, int64_t N, int64_t C, int64_t H
 void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq) {
   const int64_t total = Cout * taps * cq;
   if (total <= 0) return;
-  k_conv_pack_w<<<grid_for(total), kT, 0, ctx().stream>>>(w, wp, Cin, taps, cq, total);
+  const size_t slab = (size_t)(Cin * taps) * sizeof(float);
+  constexpr size_t kSlabMax = 128 * 1024;
+  if (slab <= kSlabMax && Cout <= 0x7fffffff && taps * cq < ((int64_t)1 << 31)) {
+    auto go = [&](auto kern) {
+      if (slab > 48 * 1024)
+        check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSlabMax),
+                   "conv_pack_w attr");
+      kern<<<(unsigned)Cout, 256, slab, ctx().stream>>>(w, wp, (int)Cin, (int)taps, (int)cq);
+    };
+    if ((Cin * taps) % 4 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0)
+      go(k_conv_pack_w_slab<true>);
+    else
+      go(k_conv_pack_w_slab<false>);
+  } else {
+    k_conv_pack_w<<<grid_for(total), kT, 0, ctx().stream>>>(w, wp, Cin, taps, cq, total);
+  }
   check_launch("conv_pack_w");
 }
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols) {

@@ -268,6 +268,32 @@ def test_conv2d_nhwc_packed_with_residual(sdb, orc):
                                 out.data_ptr(), H, W) != 0
 
 
+@pytest.mark.parametrize("Cout,Cin,taps,cq", [
+    (70, 37, 9, 64),     # channel pitch above Cin: zero columns
+    (64, 320, 1, 320),   # 1 x 1
+    (16, 2560, 9, 2560),  # 92 KB slab (opt-in shared memory)
+    (8, 4000, 9, 4000),  # slab above the kernel's shared-memory bound: the gather form
+])
+def test_conv_pack_weight_layout(sdb, Cout, Cin, taps, cq):
+    """w [Cout, Cin, taps] -> wp [Cout, taps, cq] rounded to tf32 (nearest even, low 13 bits
+    cleared), zero for channels Cin..cq-1: bit-exact against numpy."""
+    import torch
+
+    rng = np.random.default_rng(Cin)
+    w = rng.standard_normal((Cout, Cin, taps)).astype(np.float32)
+    w.reshape(-1)[:4] = [np.inf, -np.inf, 1.0 + 2.0 ** -11, 1.0 + 3 * 2.0 ** -11]  # ties to even
+    u = w.view(np.uint32)
+    r = ((u + np.uint32(0xFFF) + ((u >> 13) & 1)) & np.uint32(0xFFFFE000)).view(np.float32)
+    r = np.where(np.isinf(w), w, r)
+    want = np.zeros((Cout, taps, cq), np.float32)
+    want[:, :, :Cin] = r.transpose(0, 2, 1)
+    wd = _t(w)
+    wp = torch.full((Cout * taps * cq,), 7.0, device="cuda")
+    sdb.check(sdb.lib().sdb200_conv_pack_weight(wd.data_ptr(), wp.data_ptr(), Cout, Cin, taps, cq))
+    got = _np(wp).reshape(Cout, taps, cq)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_conv2d_nhwc_split_k_with_residual(sdb, orc):
     """A convolution with few output tiles and a long K runs as split-K; the reduction adds
     the bias and the residual (here the output buffer itself, in place)."""
