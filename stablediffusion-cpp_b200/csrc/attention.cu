@@ -6,7 +6,8 @@
 // This file holds the exact-fp32 streaming kernel (online softmax, no score matrix in
 // memory): K/V tiles of 32 keys are staged in shared memory and shared by the query
 // rows of a block; each warp owns one query row and keeps its running max, sum and
-// output accumulator in registers. It serves head dims above 128, which the
+// output accumulator in registers. Lane r scores key r, so key rows sit at an odd stride
+// (d | 1) in shared memory: the 32 lanes then read 32 different banks. It serves head dims above 128, which the
 // tensor-core kernel (attention_tc.cu) does not take, and is the exact reference the
 // tensor-core path can be compared with on the device.
 #include <algorithm>
@@ -27,8 +28,9 @@ __global__ void __launch_bounds__(kRows * 32)
                      float* __restrict__ out, int64_t Sq, int64_t Skv, int heads, int kv_heads, int d, int causal,
                      float scale) {
   extern __shared__ float sm[];
-  float* sk = sm;                   // [kKeys][d]
-  float* sv = sk + kKeys * d;       // [kKeys][d]
+  const int dk = d | 1;             // odd key-row stride: conflict-free score loop
+  float* sk = sm;                   // [kKeys][dk]
+  float* sv = sk + kKeys * dk;      // [kKeys][d]
   float* sq = sv + kKeys * d;       // [kRows][d]
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int h = blockIdx.y, n = blockIdx.z;
@@ -50,14 +52,14 @@ __global__ void __launch_bounds__(kRows * 32)
     for (int e = threadIdx.x; e < kKeys * d; e += blockDim.x) {
       const int r = e / d, t = e - r * d;
       const int64_t j = j0 + r;
-      sk[e] = j < Skv ? kb[j * kv_inner + t] : 0.0f;
+      sk[r * dk + t] = j < Skv ? kb[j * kv_inner + t] : 0.0f;
       sv[e] = j < Skv ? vb[j * kv_inner + t] : 0.0f;
     }
     __syncthreads();
     // lane r scores key j0 + r
     const int64_t j = j0 + lane;
     float s = 0.0f;
-    for (int t = 0; t < d; ++t) s = fmaf(sq[w * d + t], sk[lane * d + t], s);
+    for (int t = 0; t < d; ++t) s = fmaf(sq[w * d + t], sk[lane * dk + t], s);
     const bool valid = (j < Skv) && (!causal || j <= i);
     s = valid ? s : -INFINITY;
     float mx = s;
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(kRows * 32)
 template <int DV>
 void launch_simt(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                  int heads, int kv_heads, int64_t d, bool causal) {
-  const size_t smem = (size_t)(2 * kKeys + kRows) * d * sizeof(float);
+  const size_t smem = (size_t)(kKeys * (d | 1) + (kKeys + kRows) * d) * sizeof(float);
   if (smem > 48 * 1024)
     check_cuda(cudaFuncSetAttribute(k_attention_simt<DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                "attention attr");
