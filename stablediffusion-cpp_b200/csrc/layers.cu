@@ -93,13 +93,6 @@ __device__ __forceinline__ float round_tf32(float f) {
   b += 0xFFFu + ((b >> 13) & 1u);
   return __uint_as_float(b & 0xFFFFE000u);
 }
-__global__ void k_pack_tf32(const float* __restrict__ src, int64_t ld, float* __restrict__ dst, int64_t ldo,
-                            int64_t rows, int64_t cols) {
-  GRID_STRIDE(i, rows * cols) {
-    const int64_t r = i / cols, c = i - r * cols;
-    dst[r * ldo + c] = round_tf32(src[r * ld + c]);
-  }
-}
 // NCHW -> NHWC (channel pitch cp) through a 32-channel x 128-pixel shared-memory tile:
 // 128-byte reads along pixels (16 in flight per thread), 128-byte writes along channels;
 // tf32-rounded, zero past C. On the way each value may be transformed, in this order:
@@ -336,17 +329,48 @@ __global__ void k_split_reduce(const float* __restrict__ part, int splits, int64
   }
 }
 // Two matrices packed to the tf32 grid by one launch (the A and B operands of one GEMM).
-__global__ void k_pack_tf32_pair(const float* __restrict__ s0, int64_t ld0, float* __restrict__ d0, int64_t ldo0,
-                                 int64_t r0, const float* __restrict__ s1, int64_t ld1, float* __restrict__ d1,
-                                 int64_t ldo1, int64_t r1, int64_t cols) {
-  const int64_t n0 = r0 * cols;
-  GRID_STRIDE(i, n0 + r1 * cols) {
-    if (i < n0) {
-      const int64_t r = i / cols, c = i - r * cols;
-      d0[r * ldo0 + c] = round_tf32(s0[r * ld0 + c]);
+// dst = tf32(src) for one matrix ([r0, cols], strides ld0 / ldo0) or two at once (the
+// second [r1, cols]): the fp32 GEMM's A and B operands in one launch. One warp per row: no
+// per-element 64-bit division, and with VEC (16-byte rows, strides and bases) 16-byte
+// accesses, four in flight per lane.
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_pack_tf32_rows(const float* __restrict__ s0, int64_t ld0,
+                                                        float* __restrict__ d0, int64_t ldo0, int64_t r0,
+                                                        const float* __restrict__ s1, int64_t ld1,
+                                                        float* __restrict__ d1, int64_t ldo1, int64_t r1,
+                                                        int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = r0 + r1;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+    const bool first = row < r0;
+    const int64_t r = first ? row : row - r0;
+    const float* s = first ? s0 + r * ld0 : s1 + r * ld1;
+    float* d = first ? d0 + r * ldo0 : d1 + r * ldo1;
+    if (VEC) {
+      const int64_t c4 = cols >> 2;
+      const float4* s4 = reinterpret_cast<const float4*>(s);
+      float4* d4 = reinterpret_cast<float4*>(d);
+      for (int64_t c0 = lane; c0 < c4; c0 += 4 * 32) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < c4) v[u] = __ldg(s4 + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < c4)
+            d4[c0 + 32 * u] = make_float4(round_tf32(v[u].x), round_tf32(v[u].y), round_tf32(v[u].z),
+                                          round_tf32(v[u].w));
+      }
     } else {
-      const int64_t j = i - n0, r = j / cols, c = j - r * cols;
-      d1[r * ldo1 + c] = round_tf32(s1[r * ld1 + c]);
+      for (int64_t c0 = lane; c0 < cols; c0 += 4 * 32) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < cols) v[u] = __ldg(s + c0 + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c0 + 32 * u < cols) d[c0 + 32 * u] = round_tf32(v[u]);
+      }
     }
   }
 }
@@ -937,13 +961,20 @@ void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, in
 }
 void launch_pack_tf32(const float* src, int64_t ld, float* dst, int64_t ldo, int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return;
-  k_pack_tf32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
-  check_launch("pack_tf32");
+  launch_pack_tf32_pair(src, ld, dst, ldo, rows, nullptr, 0, nullptr, 0, 0, cols);
 }
 void launch_pack_tf32_pair(const float* s0, int64_t ld0, float* d0, int64_t ldo0, int64_t r0, const float* s1,
                            int64_t ld1, float* d1, int64_t ldo1, int64_t r1, int64_t cols) {
   if (cols <= 0 || r0 + r1 <= 0) return;
-  k_pack_tf32_pair<<<grid_for((r0 + r1) * cols), kT, 0, ctx().stream>>>(s0, ld0, d0, ldo0, r0, s1, ld1, d1, ldo1, r1,
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = cols % 4 == 0 && ld0 % 4 == 0 && ldo0 % 4 == 0 && a16(s0) && a16(d0) &&
+                   (r1 == 0 || (ld1 % 4 == 0 && ldo1 % 4 == 0 && a16(s1) && a16(d1)));
+  const int64_t blocks = std::min<int64_t>((r0 + r1 + 7) / 8, (int64_t)std::max(1, ctx().num_sms) * 16);
+  if (vec)
+    k_pack_tf32_rows<true><<<(unsigned)blocks, 256, 0, ctx().stream>>>(s0, ld0, d0, ldo0, r0, s1, ld1, d1, ldo1, r1,
+                                                                       cols);
+  else
+    k_pack_tf32_rows<false><<<(unsigned)blocks, 256, 0, ctx().stream>>>(s0, ld0, d0, ldo0, r0, s1, ld1, d1, ldo1, r1,
                                                                         cols);
   check_launch("pack_tf32_pair");
 }
