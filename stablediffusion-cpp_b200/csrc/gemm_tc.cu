@@ -1244,6 +1244,49 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
     bh = ph;
   }
   const int64_t kk = (int64_t)kh * kw * cq;
+  // Split-K for outputs with fewer tiles than SMs and a long K (the UNet's 1280-channel 3x3
+  // convolutions at 16 x 16 and 8 x 8 pixels, K up to 23040): the splits' partial outputs
+  // go to a workspace and one pass adds them with the bias and residual. With few tiles each
+  // SM is bound by its L2 -> SM load rate, about 64 bytes per clock: a K block (32 channels)
+  // of a 128 x BN tile loads (128 + BN) x 128 bytes, so t_kb = 2 (128 + BN) clocks (a
+  // 256 x 256 pair tile: 512 per SM). Cost of a choice = waves x K blocks per item x t_kb,
+  // plus the reduction: (2 splits + 2) x the output's bytes at about 3400 bytes per clock and
+  // a fixed 6000 clocks (the extra launch). The split is taken when it beats the plain
+  // choice by 20%; the tile width is then chosen with it (kept when the width is forced).
+  int splits = 1;
+  {
+    const int64_t kb = kk / 32;
+    int w0, h0;
+    conv_rect(bn, Ho, Wo, w0, h0);
+    const int64_t tiles0 = pair ? ((Cout + 2 * kBM - 1) / (2 * kBM)) * N * ((Ho + h0 - 1) / h0) * ((Wo + w0 - 1) / w0)
+                                : m_tiles * N * ((Ho + h0 - 1) / h0) * ((Wo + w0 - 1) / w0);
+    const int64_t units0 = pair ? pair_clusters(c.device) : c.num_sms;
+    if (!stats && !(pair && g_gemm_pair == 2) && tiles0 < units0 && kb >= 32) {
+      const double out_bytes = (double)N * Cout * Ho * Wo * 4.0;
+      const double base = (double)((tiles0 + units0 - 1) / units0) * (double)kb * (pair ? 512.0 : 2.0 * (128 + bn));
+      double best_split = 0.8 * base;
+      for (int cand : {256, 128, 64}) {
+        if (forced && cand != bn) continue;
+        int w_, h_;
+        conv_rect(cand, Ho, Wo, w_, h_);
+        const int64_t tiles = m_tiles * N * ((Ho + h_ - 1) / h_) * ((Wo + w_ - 1) / w_);
+        for (int s = 2; s <= 16 && s * 8 <= kb; ++s) {
+          const int64_t kbs = (kb + s - 1) / s;
+          const int64_t used = (kb + kbs - 1) / kbs;
+          const double cost = (double)((tiles * used + c.num_sms - 1) / c.num_sms) * (double)kbs * 2.0 * (128 + cand) +
+                              (2.0 * used + 2.0) * out_bytes / 3400.0 + 6000.0;
+          if (cost < best_split) {
+            best_split = cost;
+            splits = s;
+            bn = cand;
+            bw = w_;
+            bh = h_;
+          }
+        }
+      }
+      if (splits > 1) pair = false;
+    }
+  }
   CUtensorMap ta, tb;
   {
     const uint64_t dims[2] = {(uint64_t)kk, (uint64_t)Cout};
@@ -1307,13 +1350,11 @@ void launch_conv_tc(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t
     check_launch("conv_tc_pair");
     return;
   }
-  // Split-K when the output has few tiles for the SMs and K is long (the UNet's deepest 3x3
-  // convolutions: 8 x 8 or 16 x 16 pixels at 1280 channels, K up to 23040): the splits'
-  // partial outputs go to a workspace and one pass adds them with the bias and residual.
+  // Split-K as chosen above.
   float* part = nullptr;
-  if (!stats && p.num_tiles * 2 <= c.num_sms && p.k_blocks >= 32) {
-    const int want = std::min(c.num_sms / p.num_tiles, p.k_blocks / 16);
-    if (want >= 2) {
+  if (splits > 1) {
+    const int want = splits;
+    {
       const int kb_split = (p.k_blocks + want - 1) / want;
       const int used = (p.k_blocks + kb_split - 1) / kb_split;
       const long long total = N * Cout * Ho * Wo;
