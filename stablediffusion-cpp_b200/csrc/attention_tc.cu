@@ -447,33 +447,34 @@ __global__ void k_pack_heads_f16(const float* __restrict__ x, __half* __restrict
   }
 }
 
-// q, k and v packed by one launch: segment 0 has qn = rows_q * Hq * dp elements, segments
-// 1 and 2 kn = rows_kv * Hkv * dp each.
+// q, k and v packed by one launch, two values per thread (one half2 store): segment 0 has
+// qn2 = rows_q * Hq * dp / 2 pairs, segments 1 and 2 kn2 = rows_kv * Hkv * dp / 2 each.
+// dp / 2 = 1 << sh (dp is 64 or 128), so a pair's row and column come from a shift and a
+// mask. Columns d..dp-1 are zero; finite values saturate at the fp16 range.
+__device__ __forceinline__ float f16_sat(float v) { return isnan(v) ? v : fminf(fmaxf(v, -65504.0f), 65504.0f); }
 __global__ void k_pack_qkv_f16(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                                __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ v16,
-                               int64_t qn, int64_t kn, int d, int dp) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < qn + 2 * kn;
+                               int64_t qn2, int64_t kn2, int d, int sh) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < qn2 + 2 * kn2;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float* x = q;
     __half* y = q16;
     int64_t j = i;
-    if (j >= qn) {
-      j -= qn;
+    if (j >= qn2) {
+      j -= qn2;
       x = k;
       y = k16;
-      if (j >= kn) {
-        j -= kn;
+      if (j >= kn2) {
+        j -= kn2;
         x = v;
         y = v16;
       }
     }
-    const int c = (int)(j % dp);
-    float val = 0.0f;
-    if (c < d) {
-      val = x[(j / dp) * d + c];
-      if (!isnan(val)) val = fminf(fmaxf(val, -65504.0f), 65504.0f);
-    }
-    y[j] = __float2half_rn(val);
+    const int c = (int)(j & ((1 << sh) - 1)) * 2;
+    const float* src = x + (j >> sh) * d + c;
+    const float a = c < d ? f16_sat(src[0]) : 0.0f;
+    const float b = c + 1 < d ? f16_sat(src[1]) : 0.0f;
+    reinterpret_cast<__half2*>(y)[j] = __floats2half2_rn(a, b);
   }
 }
 
@@ -582,10 +583,11 @@ void launch_attention(const float* q, const float* k, const float* v, float* out
   void* k16 = ws + a256(qb);
   void* v16 = ws + a256(qb) + a256(kb);
   {
-    const int64_t qn = N * Sq * heads * dp, kn = N * Skv * kv_heads * dp;
-    const int64_t blocks = std::min<int64_t>((qn + 2 * kn + 255) / 256, (int64_t)ctx().num_sms * 16);
-    k_pack_qkv_f16<<<(unsigned)blocks, 256, 0, ctx().stream>>>(q, k, v, (__half*)q16, (__half*)k16, (__half*)v16, qn,
-                                                               kn, (int)d, (int)dp);
+    const int64_t qn2 = N * Sq * heads * dp / 2, kn2 = N * Skv * kv_heads * dp / 2;
+    const int sh = dp == 64 ? 5 : 6;  // log2(dp / 2)
+    const int64_t blocks = std::min<int64_t>((qn2 + 2 * kn2 + 255) / 256, (int64_t)ctx().num_sms * 16);
+    k_pack_qkv_f16<<<(unsigned)blocks, 256, 0, ctx().stream>>>(q, k, v, (__half*)q16, (__half*)k16, (__half*)v16, qn2,
+                                                               kn2, (int)d, sh);
     check_launch("pack_qkv_f16");
   }
   launch_attention_f16(q16, k16, v16, out, (long long)heads * d, (long long)Sq * heads * d, false, N, Sq, Skv, heads,

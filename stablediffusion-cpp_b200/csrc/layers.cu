@@ -660,6 +660,57 @@ __global__ void k_row_norm(const float* __restrict__ x, float* __restrict__ y, i
     q[i] = o;
   }
 }
+// The same for rows of C <= 128 NV floats (C % 4 == 0, 16-byte rows): one warp per row,
+// the row held in registers as NV float4 per lane, so it is read once and the two
+// reductions are warp shuffles (the UNet's LayerNorms: C = 320 ... 1280).
+template <int NV>
+__global__ void __launch_bounds__(256) k_row_norm_warp(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
+                                                       int C, const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, float eps, int rms) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int C4 = C >> 2;
+  const float4* p = reinterpret_cast<const float4*>(x + row * C);
+  float4 v[NV];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < C4 ? p[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  const float mean = rms ? 0.0f : warp_sum(s) / (float)C;
+  float q = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (lane + 32 * j < C4) {
+      const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / (float)C + eps);
+  float4* o = reinterpret_cast<float4*>(y + row * C);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = lane + 32 * j;
+    if (c < C4) {
+      float4 r = make_float4((v[j].x - mean) * rstd, (v[j].y - mean) * rstd, (v[j].z - mean) * rstd,
+                             (v[j].w - mean) * rstd);
+      if (gamma) {
+        const float4 g = __ldg(g4 + c);
+        r = make_float4(r.x * g.x, r.y * g.y, r.z * g.z, r.w * g.w);
+      }
+      if (beta) {
+        const float4 b = __ldg(b4 + c);
+        r = make_float4(r.x + b.x, r.y + b.y, r.z + b.z, r.w + b.w);
+      }
+      o[c] = r;
+    }
+  }
+}
 // Per-head RMSNorm in place: one warp per group of `dim` values (tensor.cpp:681-699).
 __global__ void k_rms_norm_heads(float* __restrict__ x, int64_t groups, int64_t dim, const float* __restrict__ gamma,
                                  float eps) {
@@ -1063,7 +1114,22 @@ void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, i
 void op_row_norm(const float* x, float* y, int64_t rows, int64_t C, const float* gamma, const float* beta, float eps,
                  bool rms) {
   if (rows <= 0) return;
-  k_row_norm<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, y, C, gamma, beta, eps, rms ? 1 : 0);
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const int nv = (int)((C + 127) / 128);
+  if (C % 4 == 0 && nv <= 16 && a16(x) && a16(y) && a16(gamma) && a16(beta) && (rows + 7) / 8 < (1ll << 31)) {
+    const unsigned blocks = (unsigned)((rows + 7) / 8);
+    const int r = rms ? 1 : 0;
+    cudaStream_t st = ctx().stream;
+    switch (nv) {
+#define SDB_RN(V) \
+  case V: k_row_norm_warp<V><<<blocks, 256, 0, st>>>(x, y, rows, (int)C, gamma, beta, eps, r); break;
+      SDB_RN(1) SDB_RN(2) SDB_RN(3) SDB_RN(4) SDB_RN(5) SDB_RN(6) SDB_RN(7) SDB_RN(8)
+      SDB_RN(9) SDB_RN(10) SDB_RN(11) SDB_RN(12) SDB_RN(13) SDB_RN(14) SDB_RN(15) SDB_RN(16)
+#undef SDB_RN
+    }
+  } else {
+    k_row_norm<<<(unsigned)rows, kT, 0, ctx().stream>>>(x, y, C, gamma, beta, eps, rms ? 1 : 0);
+  }
   check_launch(rms ? "rms_norm" : "layer_norm");
 }
 void op_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma, float eps) {

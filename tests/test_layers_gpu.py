@@ -133,6 +133,23 @@ def test_attention_gemm_path_row_chunks(sdb, attention_path):
         assert rel_fro(got, want) <= 2e-3, causal
 
 
+@pytest.mark.parametrize("rows,C", [(1000, 320), (77, 1280), (40, 2048), (40, 2052), (33, 322)])
+def test_row_norms_widths(sdb, rows, C):
+    """LayerNorm / RMSNorm at the UNet's widths (one warp per row, the row in registers) and
+    at widths that take the block-per-row kernel (C > 2048, C % 4 != 0), against float64."""
+    be = sdb.backend
+    rng = np.random.default_rng(C)
+    x = (3.0 + 2.0 * rng.standard_normal((rows, C))).astype(np.float32)
+    g = rng.standard_normal(C).astype(np.float32)
+    b = rng.standard_normal(C).astype(np.float32)
+    xd = x.astype(np.float64)
+    mu = xd.mean(1, keepdims=True)
+    ln = (xd - mu) / np.sqrt(((xd - mu) ** 2).mean(1, keepdims=True) + 1e-5) * g + b
+    rms = xd / np.sqrt((xd ** 2).mean(1, keepdims=True) + 1e-6) * g
+    assert np.abs(_np(be.layer_norm(_t(x), _t(g), _t(b), 1e-5)) - ln).max() <= 1e-4
+    assert np.abs(_np(be.rms_norm(_t(x), _t(g), 1e-6)) - rms).max() <= 1e-4
+
+
 def test_golden_layers(sdb):
     g = load_golden("layers")
     be = sdb.backend
