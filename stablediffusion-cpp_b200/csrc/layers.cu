@@ -613,6 +613,57 @@ __global__ void __launch_bounds__(256) k_gn_finalize_parts(const float4* __restr
     ab[n * C + ch] = make_float2(a, beta[ch] - (float)mu * a);
   }
 }
+// GroupNorm in one launch for groups that fit in shared memory (cg x HW <= kGnFusedMax
+// values; every group of the SD 1.x UNet at 512^2): one 1024-thread block per (group,
+// sample) reads the group's values (contiguous in NCHW) once into shared memory, eight
+// 16-byte loads in flight per thread; mean, then the mean of squared deviations, are fp32
+// block reductions over shared memory; y = (x - mean) * rstd * gamma[c] + beta[c], then
+// SiLU when asked. Groups too large for it use the split statistics below.
+constexpr int kGnFusedMax = 48 * 1024;
+__global__ void __launch_bounds__(1024) k_gn_fused(const float* __restrict__ x, float* __restrict__ y, int64_t C,
+                                                   int HW, int cg, const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta, float eps, int silu) {
+  extern __shared__ float4 gsm4[];
+  __shared__ float red[32];
+  const int g = blockIdx.x, n = blockIdx.y, cnt = cg * HW, c4n = cnt >> 2;
+  const int64_t base = ((int64_t)n * C + (int64_t)g * cg) * HW;
+  const float4* src = reinterpret_cast<const float4*>(x + base);
+  constexpr int kU = 8;
+  float s = 0.0f;
+  for (int i0 = threadIdx.x; i0 < c4n; i0 += kU * 1024) {
+    float4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i0 + u * 1024 < c4n) v[u] = __ldg(src + i0 + u * 1024);
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i0 + u * 1024 < c4n) {
+        gsm4[i0 + u * 1024] = v[u];
+        s += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+      }
+  }
+  const float mean = block_sum(s, red) / (float)cnt;
+  float q = 0.0f;
+  for (int i = threadIdx.x; i < c4n; i += 1024) {
+    const float4 v = gsm4[i];
+    const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  const float rstd = rsqrtf(block_sum(q, red) / (float)cnt + eps);
+  float4* dst = reinterpret_cast<float4*>(y + base);
+  for (int i = threadIdx.x; i < c4n; i += 1024) {
+    const int c = g * cg + (4 * i) / HW;  // HW % 4 == 0: the four values share a channel
+    const float ga = gamma ? __ldg(gamma + c) : 1.0f, be = beta ? __ldg(beta + c) : 0.0f;
+    const float4 v = gsm4[i];
+    float o[4] = {(v.x - mean) * rstd * ga + be, (v.y - mean) * rstd * ga + be, (v.z - mean) * rstd * ga + be,
+                  (v.w - mean) * rstd * ga + be};
+    if (silu) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = o[e] / (1.0f + expf(-o[e]));
+    }
+    dst[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
 template <bool VEC>
 __global__ void k_gn_apply(const float* __restrict__ x, float* __restrict__ y, int64_t HW,
                            const float2* __restrict__ ab, int silu) {
@@ -1096,6 +1147,23 @@ void op_group_norm(const float* x, float* y, int64_t N, int64_t C, int64_t HW, i
                    const float* beta, float eps, bool silu) {
   if (N <= 0 || C <= 0 || HW <= 0) return;
   if (N * C > 65535) fail(kErrInvalidArg, "group_norm: too many samples x channels");
+  if (groups > 0 && C % groups == 0 && HW % 4 == 0 && (C / groups) * HW <= kGnFusedMax &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int cg = (int)(C / groups);
+    const size_t smem = (size_t)cg * HW * sizeof(float);
+    static bool attr_set[64] = {};  // per device ordinal (ctx() keeps ordinals below 64)
+    DeviceContext& c = ctx();
+    if (smem > 48 * 1024 && !attr_set[c.device]) {
+      check_cuda(cudaFuncSetAttribute(k_gn_fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)(kGnFusedMax * sizeof(float))),
+                 "group_norm attr");
+      attr_set[c.device] = true;
+    }
+    k_gn_fused<<<dim3((unsigned)groups, (unsigned)N), 1024, smem, c.stream>>>(x, y, C, (int)HW, cg, gamma, beta, eps,
+                                                                             silu ? 1 : 0);
+    check_launch("group_norm");
+    return;
+  }
   float2* ab = static_cast<float2*>(pool_malloc((size_t)(N * C) * sizeof(float2)));
   uint8_t* ws = reinterpret_cast<uint8_t*>(ab);
   cudaStream_t st = ctx().stream;

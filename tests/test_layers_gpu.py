@@ -350,11 +350,16 @@ def test_conv2d_strided_uses_im2col(sdb, orc):
     ((1, 128, 256, 256), 32),   # VAE last-stage width: 4 channels x 65536 values per group
     ((2, 320, 37, 29), 32),     # odd plane (no 16-byte rows), several chunks per group
     ((1, 64, 3, 3), 32),        # groups smaller than one chunk
-    ((3, 96, 17, 16), 8),
+    ((3, 96, 17, 16), 8),       # one launch: the group in shared memory
+    ((2, 320, 64, 64), 32),     # SD 1.x UNet groups at 512^2, one launch (160 KB group)
+    ((2, 640, 32, 32), 32),
+    ((2, 1280, 8, 8), 32),
 ])
 def test_group_norm_split_statistics(sdb, orc, shape, groups):
-    """GroupNorm with chunked statistics combined in double, against the oracle's double
-    two-pass statistics (the reference's GPU-vs-CPU norm tolerance, 1e-4)."""
+    """GroupNorm with chunked statistics combined in double (large groups), or in one launch
+    with the group in shared memory and two-pass fp32 statistics (groups up to 48K values),
+    against the oracle's double two-pass statistics (the reference's GPU-vs-CPU norm
+    tolerance, 1e-4)."""
     rng = np.random.default_rng(shape[1])
     # A large common offset makes single-pass fp32 statistics fail; the split form must not.
     x = (3.0 + rng.standard_normal(shape)).astype(np.float32)
