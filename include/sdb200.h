@@ -64,7 +64,9 @@ int sdb200_set_device(int device);
 int sdb200_set_stream(void* stream);
 void* sdb200_get_stream(void);
 /* Synchronises the stream, then reads the device error word that kernels set when a
- * bounded wait expires (0 = none) without clearing it. */
+ * bounded wait expires (0 = none) without clearing it. Bits: 1-16 GEMM / convolution
+ * pipeline waits, 32 attention pipeline, 64 tensor-parallel barrier (a peer rank did not
+ * arrive). */
 int sdb200_device_error_word(int* out);
 
 /* ---- memory (backend_cuda.h:29-36) --------------------------------------------- */
