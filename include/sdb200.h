@@ -263,6 +263,12 @@ int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n);
  * flag exchange over NVLink (flags != 0, default) or a 4-byte NCCL all-reduce (0). Every
  * rank of the group sets the same. */
 int sdb200_comm_set_barrier(void* comm, int flags);
+/* Extension, self-test of that barrier on one device: `flags` is a device array of `world`
+ * uint32 words standing for every rank's flag words at once. The kernel stores `epoch` into
+ * word `rank` and waits until every word is >= epoch. A word that never gets there makes
+ * the wait run out after its 2 s bound: the device error word then holds bit 64 and the
+ * next sdb200_synchronize returns SDB200_ERR_DEVICE_WAIT. Stream-ordered. */
+int sdb200_comm_barrier_selftest(uint32_t* flags, int world, int rank, uint32_t epoch);
 void sdb200_comm_destroy(void* comm);
 
 /* ---- layers (backend_cuda.h:45-61) ---------------------------------------------- */

@@ -254,6 +254,22 @@ int sdb200_comm_allreduce_sum_f32(void* comm, float* buf, size_t n) {
   }
 }
 
+int sdb200_comm_barrier_selftest(uint32_t* flags, int world, int rank, uint32_t epoch) {
+  try {
+    if (!flags || world < 1 || world > sdb::kMaxTpRanks || rank < 0 || rank >= world)
+      sdb::fail(sdb::kErrInvalidArg, "comm_barrier_selftest: bad flag array, world or rank");
+    if ((reinterpret_cast<uintptr_t>(flags) & 3) != 0) sdb::fail(sdb::kErrInvalidArg, "comm_barrier_selftest: unaligned");
+    sdb::FlagPtrs fp{};
+    for (int r = 0; r < world; ++r) fp.p[r] = flags;  // every peer's flag array is this one
+    sdb::k_flag_barrier<<<1, 32, 0, sdb::ctx().stream>>>(fp, flags, rank, world, epoch, sdb::ctx().err_word);
+    sdb::check_launch("flag_barrier_selftest");
+    return sdb::kOk;
+  } catch (const sdb::Error& e) {
+    sdb::set_last_error(e.msg);
+    return e.code;
+  }
+}
+
 int sdb200_comm_set_barrier(void* comm, int flags) {
   try {
     if (!comm) sdb::fail(sdb::kErrInvalidArg, "comm_set_barrier: null communicator");

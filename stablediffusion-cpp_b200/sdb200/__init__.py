@@ -100,6 +100,7 @@ _SIGS = {
     "sdb200_comm_create": ([_v, _i, _i], _v),
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
     "sdb200_comm_set_barrier": ([_v, _i], _i),
+    "sdb200_comm_barrier_selftest": ([_v, _i, _i, C.c_uint32], _i),
     "sdb200_comm_destroy": ([_v], None),
     "sdb200_conv2d": ([_v, _i64, _i64, _i64, _i64, _v, _i64, _i64, _i64, _v, _i, _i, _v, _i64, _i64], _i),
     "sdb200_conv_pack_input": ([_v, _v, _i64, _i64, _i64, _i64], _i),
