@@ -84,6 +84,14 @@ def test_host_validation_rejects_bad_args():
     assert L.sdb200_attention(1, 1, 1, 1, 1, 4, 4, 3, 2, 8, 0) == sdb200.ERR_INVALID_ARG
     # M <= 0 is a no-op success, as in the reference (backend_cuda.cu:464)
     assert f(0, 8, 16, None, 16, None, 16, 1, 8, None, 0) == sdb200.OK
+    # tensor-parallel barrier self-test: null flags, more than 8 ranks, rank outside the group,
+    # and a misaligned flag array are refused before any device work
+    assert L.sdb200_comm_barrier_selftest(None, 2, 0, 1) == sdb200.ERR_INVALID_ARG
+    assert L.sdb200_comm_barrier_selftest(16, 9, 0, 1) == sdb200.ERR_INVALID_ARG
+    assert L.sdb200_comm_barrier_selftest(16, 2, 2, 1) == sdb200.ERR_INVALID_ARG
+    assert L.sdb200_comm_barrier_selftest(18, 2, 0, 1) == sdb200.ERR_INVALID_ARG
+    # barrier choice on a null communicator
+    assert L.sdb200_comm_set_barrier(None, 1) == sdb200.ERR_INVALID_ARG
 
 
 def test_no_device_reports_unavailable():
