@@ -184,3 +184,39 @@ def test_oracle_matches_reference_library(orc, ref):
     k = rng.standard_normal((1, 80, 2 * 32)).astype(np.float32)
     v = rng.standard_normal((1, 80, 2 * 32)).astype(np.float32)
     assert_ulp_close(orc.attention(q, k, v, 4, 2, False), ref.attention(q, k, v, 4, 2, False))
+
+
+def test_oracle_layers_match_reference_library(orc, ref):
+    """The layer ops of the C restatement against the reference's own CPU code on fresh
+    inputs: norms, RoPE (both layouts), SwiGLU, GEGLU, GroupNorm and conv2d (stride 1 and 2,
+    padding, bias)."""
+    rng = np.random.default_rng(123)
+    x = (2.0 + rng.standard_normal((37, 96))).astype(np.float32)
+    g = rng.standard_normal(96).astype(np.float32)
+    b = rng.standard_normal(96).astype(np.float32)
+    assert_ulp_close(orc.rms_norm(x, g, 1e-6), ref.rms_norm(x, g, 1e-6), "rms_norm")
+    assert_ulp_close(orc.layer_norm(x, g, b, 1e-5), ref.layer_norm(x, g, b, 1e-5), "layer_norm")
+    assert_ulp_close(orc.layer_norm(x, None, None, 1e-6), ref.layer_norm(x, None, None, 1e-6), "layer_norm")
+    assert_ulp_close(orc.rms_norm_heads(x, 32, g[:32], 1e-6), ref.rms_norm_heads(x, 32, g[:32], 1e-6),
+                     "rms_norm_heads")
+    r = rng.standard_normal((2, 7, 4 * 16)).astype(np.float32)
+    ang = rng.uniform(-3, 3, (7, 8)).astype(np.float32)
+    cos = np.repeat(np.cos(ang), 2, axis=1).astype(np.float32)
+    sin = np.repeat(np.sin(ang), 2, axis=1).astype(np.float32)
+    for inter in (False, True):
+        assert_ulp_close(orc.rope(r, 16, cos, sin, inter), ref.rope(r, 16, cos, sin, inter), f"rope {inter}")
+    gt = rng.standard_normal(500).astype(np.float32)
+    ut = rng.standard_normal(500).astype(np.float32)
+    assert_ulp_close(orc.swiglu(gt, ut), ref.swiglu(gt, ut), "swiglu")
+    gx = rng.standard_normal((9, 2 * 40)).astype(np.float32)
+    assert_ulp_close(orc.geglu(gx), ref.geglu(gx), "geglu")
+    gn = (3.0 + rng.standard_normal((2, 64, 9, 11))).astype(np.float32)
+    gg = (1.0 + 0.1 * rng.standard_normal(64)).astype(np.float32)
+    gb = (0.1 * rng.standard_normal(64)).astype(np.float32)
+    assert_ulp_close(orc.group_norm(gn, 32, gg, gb, 1e-6), ref.group_norm(gn, 32, gg, gb, 1e-6), "group_norm")
+    cx = rng.standard_normal((2, 5, 13, 17)).astype(np.float32)
+    cw = (0.1 * rng.standard_normal((6, 5, 3, 3))).astype(np.float32)
+    cb = rng.standard_normal(6).astype(np.float32)
+    for stride, pad in ((1, 1), (2, 1), (1, 0)):
+        assert_ulp_close(orc.conv2d(cx, cw, cb, stride, pad), ref.conv2d(cx, cw, cb, stride, pad),
+                         f"conv2d s{stride} p{pad}")
