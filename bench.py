@@ -1,7 +1,7 @@
 """Benchmark of StableDiffusion-cpp's dense-contraction hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dit|dit_tp|gemm|attention|conv|vae]
+                    [--workload dit|dit_tp|gemm|attention|conv|vae|unet]
 
 Workload `dit` (default): the full 30-layer Z-Image-shaped DiT (6.15 B
 random-init bf16 parameters) at 1024x1024 (16-channel 128x128 latent, 128 text tokens of
@@ -24,6 +24,12 @@ Workload `conv`: the VAE decoder's 3x3 convolutions at the four resolution stage
 
 Workload `vae`: one FLUX / Z-Image VAE decode of a 1024x1024 image on the device
 (sdb200_vae_decode), ms per decode.
+
+Workload `unet`: the SD 1.5 UNet's contraction shapes at 512^2 - one
+transformer block (self- and cross-attention projections, 8 heads of 40, 77 text tokens,
+GEGLU feed-forward) and one 3x3 convolution 320 -> 320 on 64x64 - through the C ABI with
+fp32 weights, ms per pass. The reference arm adds the full SD 1.5 UNet step through the
+drop-in link (`reference_code_on_sdb200`).
 
 Workload `attention`: the DiT's joint attention at 1024^2 alone (4224 tokens, 30 heads of
 128), TFLOP/s of the tensor-core kernel (for profiling the second hot kernel).
@@ -338,6 +344,16 @@ def reference_gpu_line(args, world, local):
             ms = timed_loop(fn, 1, stream, None, dev)
             return {"value": sum(conv_flops()) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "kind": REF_GPU_KIND,
                     "ms_per_step": ms, "sample": "conv2d() of the four stages (im2col + fp32 SGEMM)"}
+        if args.workload == "unet":
+            t = cfg2_tensors(dev)
+            ops = cfg2_ops_refgpu(r, t)
+            flush_buf = torch.empty(64 << 20, device=dev)
+            step = lambda: [o[3]() for o in ops]  # noqa: E731
+            step()
+            ms = timed_steps_flushed(step, args.steps, stream, None, dev, flush_buf.zero_) / args.steps
+            return {"value": ms, "unit": "ms/step", "kind": REF_GPU_KIND,
+                    "sample": "the config-2 op set on device buffers (cublasSgemm, batched SGEMM attention, "
+                              "im2col conv), L2 flushed before each step"}
         if args.workload == "vae":
             import numpy as np
 
@@ -368,6 +384,316 @@ def reference_gpu_line(args, world, local):
             return {"value": dt * 1e3 * GLOBAL_BATCH, "unit": "ms/step", "kind": REF_GPU_KIND,
                     "sample": f"one batch-1 forward of the full 30-layer model on the GPU backend ({dt * 1e3:.1f} ms, "
                               f"wall clock with latent in and prediction out) x {GLOBAL_BATCH} images per step"}
+        return {"value": None, "unavailable": f"not measured for workload {args.workload}"}
+    except Exception as e:  # reported, never required
+        return {"value": None, "unavailable": f"failed: {e}"}
+
+
+# ---------------------------------------------------------------------------------------
+# BASELINE config 2: the SD 1.5 UNet's contraction shapes at 512^2 (64x64 latent = 4096
+# tokens of 320 channels), fp32 weights ~N(0, 0.02), activations ~N(0, 1): one transformer
+# block's self-attention (q/k/v/out projections, 8 heads of 40), cross-attention (77 text
+# tokens of width 768), GEGLU feed-forward (320 -> 2560 -> GEGLU -> 1280 -> 320), and one
+# 3x3 convolution 320 -> 320 on 64x64 (modules.cpp:55-80, unet.cpp; shapes from the SD 1.5
+# layout). One step = one pass over these ops.
+# ---------------------------------------------------------------------------------------
+CFG2 = dict(T=4096, C=320, heads=8, L=77, E=768, F=1280, side=64)
+
+
+def cfg2_tensors(dev, seed=55):
+    import torch
+
+    c = CFG2
+    T, C, L, E, F, side = c["T"], c["C"], c["L"], c["E"], c["F"], c["side"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    rn = lambda *shape, s=1.0: s * torch.randn(shape, generator=g, device=dev)  # noqa: E731
+    t = {"x": rn(T, C), "ctx": rn(L, E), "img": rn(1, C, side, side)}
+    for n in ("q1", "k1", "v1", "o1", "q2", "o2"):
+        t["W" + n] = rn(C, C, s=0.02)
+    t["Wk2"], t["Wv2"] = rn(C, E, s=0.02), rn(C, E, s=0.02)
+    t["Wf1"], t["Wf2"] = rn(2 * F, C, s=0.02), rn(C, F, s=0.02)
+    t["Wc"] = rn(C, C, 3, 3, s=0.02)
+    for n in ("bo1", "bo2", "bf2", "bc"):
+        t[n] = rn(C, s=0.02)
+    t["bf1"] = rn(2 * F, s=0.02)
+    for n, shape in (("q1", (T, C)), ("k1", (T, C)), ("v1", (T, C)), ("a1", (T, C)), ("o1", (T, C)), ("q2", (T, C)),
+                     ("k2", (L, C)), ("v2", (L, C)), ("a2", (T, C)), ("o2", (T, C)), ("f1", (T, 2 * F)),
+                     ("g", (T, F)), ("f2", (T, C)), ("y", (1, C, side, side))):
+        t[n] = torch.empty(shape, device=dev)
+    return t
+
+
+def cfg2_ops(t, gemm, attention, geglu, conv):
+    """[(name, FLOP, minimum bytes, call)] of one cfg2 pass over tensors t, with the four
+    backend entry points given as callables taking device pointers:
+    gemm(M, N, K, A, B, C, bias), attention(q, k, v, out, Sq, Skv), geglu(x, y, rows, D),
+    conv(x, w, bias, out)."""
+    c = CFG2
+    T, C, L, E, F, side, H = c["T"], c["C"], c["L"], c["E"], c["F"], c["side"], c["heads"]
+    p = lambda n: t[n].data_ptr() if n else None  # noqa: E731
+
+    def lin(name, M, N, K, a, w, out, bias=None):
+        return (name, 2.0 * M * N * K, 4.0 * (M * K + N * K + M * N), lambda: gemm(M, N, K, p(a), p(w), p(out), p(bias)))
+
+    def att(name, q, k, v, o, Sq, Skv):
+        return (name, 4.0 * Sq * Skv * C, 4.0 * (2 * Sq * C + 2 * Skv * C),
+                lambda: attention(p(q), p(k), p(v), p(o), Sq, Skv))
+
+    return [
+        lin("self_q", T, C, C, "x", "Wq1", "q1"), lin("self_k", T, C, C, "x", "Wk1", "k1"),
+        lin("self_v", T, C, C, "x", "Wv1", "v1"), att("self_attention", "q1", "k1", "v1", "a1", T, T),
+        lin("self_out", T, C, C, "a1", "Wo1", "o1", "bo1"),
+        lin("cross_q", T, C, C, "x", "Wq2", "q2"), lin("cross_k", L, C, E, "ctx", "Wk2", "k2"),
+        lin("cross_v", L, C, E, "ctx", "Wv2", "v2"), att("cross_attention", "q2", "k2", "v2", "a2", T, L),
+        lin("cross_out", T, C, C, "a2", "Wo2", "o2", "bo2"),
+        lin("ffn_proj", T, 2 * F, C, "x", "Wf1", "f1", "bf1"),
+        ("ffn_geglu", 0.0, 4.0 * (T * 2 * F + T * F), lambda: geglu(p("f1"), p("g"), T, F)),
+        lin("ffn_out", T, C, F, "g", "Wf2", "f2", "bf2"),
+        ("conv3x3", 2.0 * C * C * 9 * side * side, 4.0 * (2 * C * side * side + 9 * C * C),
+         lambda: conv(p("img"), p("Wc"), p("bc"), p("y"))),
+    ]
+
+
+def cfg2_ops_sdb(t):
+    import sdb200
+
+    L = sdb200.lib()
+    c = CFG2
+    C, H, side = c["C"], c["heads"], c["side"]
+    ck = sdb200.check
+    return cfg2_ops(
+        t,
+        lambda M, N, K, a, w, o, b: ck(L.sdb200_gemm_nt_f32(M, N, K, a, K, w, K, o, N, b, 0)),
+        lambda q, k, v, o, Sq, Skv: ck(L.sdb200_attention(q, k, v, o, 1, Sq, Skv, H, H, C // H, 0)),
+        lambda x, y, rows, D: ck(L.sdb200_geglu(x, y, rows, D)),
+        lambda x, w, b, o: ck(L.sdb200_conv2d(x, 1, C, side, side, w, C, 3, 3, b, 1, 1, o, side, side)))
+
+
+def cfg2_ops_refgpu(r, t):
+    c = CFG2
+    C, H, side = c["C"], c["heads"], c["side"]
+    return cfg2_ops(
+        t,
+        lambda M, N, K, a, w, o, b: r.gemm_nt_f32_dev(M, N, K, a, K, w, K, o, N, b),
+        lambda q, k, v, o, Sq, Skv: r.attention_dev(q, k, v, o, 1, Sq, Skv, H, H, C // H),
+        lambda x, y, rows, D: r.geglu_dev(x, y, rows, D),
+        lambda x, w, b, o: r.conv2d_dev(x, 1, C, side, side, w, C, 3, 3, b, 1, 1, o, side, side))
+
+
+def cfg2_flop():
+    return sum(f for _, f, _, _ in cfg2_ops({}, *(lambda *a: None,) * 4))
+
+
+def timed_steps_flushed(fn, steps, stream, pg, dev, flush):
+    """Sum over `steps` calls of the CUDA-event time of each, with `flush` (a write of a
+    buffer larger than L2) run untimed before every call; barrier + synchronize on both
+    sides, max over ranks."""
+    import torch
+
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    total = 0.0
+    evs = []
+    for _ in range(steps):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    total = sum(a.elapsed_time(b) for a, b in evs)
+    if pg:
+        pg.barrier()
+    t = torch.tensor([total], device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_unet(args, world, rank, local, pg, dev):
+    """BASELINE config 2 on this library through the C ABI (sdb200_gemm_nt_f32 on tf32
+    tensor cores, sdb200_attention, sdb200_geglu, sdb200_conv2d), L2 flushed before each
+    step. value = ms per pass over the config-2 ops; every rank runs its own replica."""
+    import torch
+
+    import sdb200
+    from sdb200 import backend as be
+
+    L = sdb200.lib()
+    t = cfg2_tensors(dev)
+    ops = cfg2_ops_sdb(t)
+    flop = sum(o[1] for o in ops)
+    flush_buf = torch.empty(64 << 20, device=dev)  # 256 MB > L2
+    flush = flush_buf.zero_
+    step = lambda: [o[3]() for o in ops]  # noqa: E731
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    n0 = L.sdb200_launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed_steps_flushed(step, args.steps, stream, pg, dev, flush)
+    launches = L.sdb200_launch_count() - n0
+    ms_step = ms / args.steps
+    # per-op CUDA-event times (one flushed pass per op)
+    per_op = {}
+    pk = peaks()
+    for name, f, nbytes, call in ops:
+        opms = timed_steps_flushed(call, 3, stream, None, dev, flush) / 3
+        per_op[name] = {"us": opms * 1e3, "tflops": f / (opms * 1e-3) / 1e12 if f else None,
+                        "gb_s_min_bytes": nbytes / (opms * 1e-3) / 1e9}
+    top = max(per_op, key=lambda n: per_op[n]["us"])
+    # end to end: the step's inputs (latent tokens, text states, conv input) from pinned
+    # host memory and its outputs (self, cross and FFN outputs, conv output) back
+    ins = [t[n] for n in ("x", "ctx", "img")]
+    outs = [t[n] for n in ("o1", "o2", "f2", "y")]
+    hin = [x.cpu().pin_memory() for x in ins]
+    hout = [torch.empty_like(x, device="cpu").pin_memory() for x in outs]
+
+    def e2e_step():
+        for h, d in zip(hin, ins):
+            sdb200.check(L.sdb200_upload(d.data_ptr(), h.data_ptr(), h.numel() * 4))
+        step()
+        for h, d in zip(hout, outs):
+            sdb200.check(L.sdb200_download(h.data_ptr(), d.data_ptr(), h.numel() * 4))
+
+    e2e_step()
+    e2e_ms = timed_steps_flushed(e2e_step, args.steps, stream, pg, dev, flush) / args.steps
+    if rank == 0:
+        top_f = next(o for o in ops if o[0] == top)
+        top_tf = per_op[top]["tflops"]
+        print(json.dumps({
+            "metric": "SD 1.5 UNet config-2 op set ms per pass (512^2: 4096 tokens x 320 ch)", "value": ms_step,
+            "unit": "ms/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32 weights/activations; tf32 tensor-core GEMM and conv operands, fp16 attention operands",
+            "data": "synthetic (N(0,0.02) fp32 weights, N(0,1) activations)",
+            "config": {"workload": "cfg2: SD 1.5 transformer block at 512^2 (self-attn q/k/v/out 4096x320x320, "
+                                   "8 heads of 40; cross-attn 77 tokens of 768; GEGLU FFN 320->2560->1280->320) "
+                                   "+ 3x3 conv 320->320 on 64x64",
+                       "parallelism": f"replicas x{world}", "l2": "256 MB buffer written before every step (untimed)",
+                       "gflop_per_step": flop / 1e9},
+            "step_tflops": flop / (ms_step * 1e-3) / 1e12, "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": f"{top} (the op with the largest time)",
+                         "achieved": top_tf, "peak": pk["burst"], "unit": "TFLOP/s",
+                         "frac": top_tf / pk["burst"] if top_tf else None,
+                         "peak_kind": f"{pk['kind']} bf16 burst (the tf32 rate is half of it)",
+                         "traffic": None, "ops": per_op, "top_op_flop": top_f[1]},
+            "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int(sum(h.numel() * 4 for h in hin)),
+                    "d2h_bytes_per_step": int(sum(h.numel() * 4 for h in hout))},
+            "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": be.device_error_word()}), flush=True)
+
+
+def ref_unet_ops_cpu():
+    """The config-2 op set on the reference's CPU path (oracle/_ref: gemm_nt, attention,
+    geglu, conv2d on host arrays): returns (call, FLOP, threads)."""
+    import numpy as np
+
+    from oracle import RefCPU
+
+    ref = RefCPU()
+    ref.set_num_threads(0)
+    c = CFG2
+    T, C, L, E, F, side, H = c["T"], c["C"], c["L"], c["E"], c["F"], c["side"], c["heads"]
+    rng = np.random.default_rng(55)
+    rn = lambda *shape, s=1.0: (s * rng.standard_normal(shape)).astype(np.float32)  # noqa: E731
+    x, ctx, img = rn(T, C), rn(L, E), rn(1, C, side, side)
+    W = {n: rn(C, C, s=0.02) for n in ("q1", "k1", "v1", "o1", "q2", "o2")}
+    Wk2, Wv2, Wf1, Wf2, Wc = rn(C, E, s=0.02), rn(C, E, s=0.02), rn(2 * F, C, s=0.02), rn(C, F, s=0.02), rn(
+        C, C, 3, 3, s=0.02)
+    b = rn(C, s=0.02)
+    bf1 = rn(2 * F, s=0.02)
+
+    def fn():
+        q1, k1, v1 = (ref.gemm_nt(x, W[n]) for n in ("q1", "k1", "v1"))
+        a1 = ref.attention(q1[None], k1[None], v1[None], H)[0]
+        ref.gemm_nt(a1, W["o1"], b)
+        q2 = ref.gemm_nt(x, W["q2"])
+        k2, v2 = ref.gemm_nt(ctx, Wk2), ref.gemm_nt(ctx, Wv2)
+        a2 = ref.attention(q2[None], k2[None], v2[None], H)[0]
+        ref.gemm_nt(a2, W["o2"], b)
+        g = ref.geglu(ref.gemm_nt(x, Wf1, bf1))
+        ref.gemm_nt(g, Wf2, b)
+        ref.conv2d(img, Wc, b, 1, 1)
+
+    return fn, cfg2_flop(), ref.num_threads()
+
+
+def dropin_line(args, world, local):
+    """The maintainer's link: the reference's own model code (zimage.cpp,
+    unet.cpp over tensor.cpp / modules.cpp) linked against libsdb200.so in place of its
+    backend (oracle/_ref/libsdref_b200.so), timed on this run's model workload beside the
+    same code on its own GPU backend. Returns the JSON object or a note."""
+    if args.no_ref_gpu:
+        return {"value": None, "unavailable": "--no-ref-gpu"}
+    try:
+        import torch
+
+        if world != 1 or local != 0:
+            return {"value": None, "unavailable": "single-GPU runs only"}
+        if not torch.cuda.is_available():
+            return {"value": None, "unavailable": "no CUDA device"}
+        from oracle import RefOnB200
+
+        if not RefOnB200.available():
+            return {"value": None, "unavailable": "oracle/_ref/libsdref_b200.so not built"}
+        r = RefOnB200()
+        dev = torch.device("cuda", 0)
+        kind = ("the reference's own model code (tensor.cpp, modules.cpp, zimage.cpp / unet.cpp) linked against "
+                "libsdb200.so in place of its backend: every sd::cuda call lands in this library")
+        if args.workload == "dit":
+            from sdb200.zimage import Z_IMAGE, random_weights_torch
+
+            wts = random_weights_torch(Z_IMAGE, 0, dev)
+            rm = r.zimage_cuda(wts, heads=Z_IMAGE.heads)
+            del wts
+            g = torch.Generator(device=dev)
+            g.manual_seed(1000)
+            x = torch.randn((1, Z_IMAGE.in_channels, LAT_H, LAT_W), generator=g, device=dev).cpu().numpy()
+            cap = torch.randn((1, TEXT_TOKENS, Z_IMAGE.cap_dim), generator=g, device=dev).cpu().numpy()
+            rm(x, 0.5, cap)
+            reps = 3
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                rm(x, 0.5, cap)
+            dt = (time.perf_counter() - t0) / reps
+            del rm
+            torch.cuda.empty_cache()
+            return {"value": dt * 1e3 * GLOBAL_BATCH, "unit": "ms/step", "kind": kind,
+                    "ms_per_image": dt * 1e3,
+                    "sample": f"batch-1 forwards of the full 30-layer model at 1024^2 (mean of {reps}, wall clock "
+                              f"with latent in and prediction out) x {GLOBAL_BATCH} images per step"}
+        if args.workload == "unet":
+            import numpy as np
+
+            from oracle import RefCUDA
+            from sdb200.unet import SD15, unet_weights
+
+            w = unet_weights(seed=3, device="cuda", **SD15)
+            rng = np.random.default_rng(4)
+            x = rng.standard_normal((2, 4, 64, 64)).astype(np.float32)
+            ctx = rng.standard_normal((2, 77, 768)).astype(np.float32)
+            times, outs = {}, {}
+            for name, lib in (("reference_backend", RefCUDA() if RefCUDA.available() else None), ("sdb200", r)):
+                if lib is None:
+                    continue
+                m = lib.unet(w, heads=8, on_device=True)
+                m(x, 500.0, ctx)
+                t0 = time.perf_counter()
+                for _ in range(3):
+                    outs[name] = m(x, 500.0, ctx)
+                times[name] = (time.perf_counter() - t0) / 3 * 1e3
+                del m
+            agree = None
+            if len(outs) == 2:
+                a, b2 = outs["sdb200"].astype(np.float64), outs["reference_backend"].astype(np.float64)
+                agree = float(np.linalg.norm(a - b2) / np.linalg.norm(b2))
+            return {"value": times["sdb200"], "unit": "ms/UNet step", "kind": kind,
+                    "reference_backend_ms": times.get("reference_backend"), "rel_diff_vs_reference_backend": agree,
+                    "sample": "the full SD 1.5 UNet (unet.cpp, 860 M fp32 parameters) at 512^2 with a CFG batch of 2, "
+                              "mean of 3 steps, wall clock with latent in and prediction out"}
         return {"value": None, "unavailable": f"not measured for workload {args.workload}"}
     except Exception as e:  # reported, never required
         return {"value": None, "unavailable": f"failed: {e}"}
@@ -421,6 +747,21 @@ def run_reference(args, world, rank, local=0):
                 "cpu_baseline": {"value": ms, "unit": "ms/decode", "cores": cores, "kind": "reference",
                                  "sample": f"VAEDecoder::decode of a 256^2 image per step ({dt:.2f} s), FLOP-scaled"},
                 "e2e": {"value": ms, "unit": "ms/decode", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    elif args.workload == "unet":
+        fn, flop, cores = ref_unet_ops_cpu()
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        ms = (time.perf_counter() - t0) / args.steps * 1e3
+        line = {"impl": "reference", "metric": "SD 1.5 UNet config-2 op set ms per pass (512^2: 4096 tokens x 320 ch)",
+                "value": ms, "unit": "ms/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 (CPU)", "data": "synthetic (N(0,0.02) fp32 weights, N(0,1) activations)",
+                "config": {"workload": "cfg2 op set (see --workload unet)", "parallelism": "reference CPU thread pool"},
+                "cpu_baseline": {"value": ms, "unit": "ms/step", "cores": cores, "kind": "reference",
+                                 "sample": f"the whole config-2 op set per step ({flop / 1e9:.1f} GFLOP)"},
+                "e2e": {"value": ms, "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     elif args.workload == "conv":
         fn, flop, cores = ref_conv_sample()
         for _ in range(min(args.warmup, 1)):
@@ -457,6 +798,8 @@ def run_reference(args, world, rank, local=0):
                                  "sample": "512 of 4096 rows per step"},
                 "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     line["reference_gpu"] = reference_gpu_line(args, world, local)
+    if args.workload in ("dit", "unet"):
+        line["reference_code_on_sdb200"] = dropin_line(args, world, local)
     print(json.dumps(line), flush=True)
 
 
@@ -483,6 +826,80 @@ def timed_loop(fn, steps, stream, pg, dev):
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     return float(t.item())
+
+
+# The skinny and epilogue-bound GEMM shapes of the DiT (HBM-bound: arithmetic intensity
+# below the bf16 ridge of about 250 FLOP/byte), called the way the reference calls them
+# (fp32 A, bf16 weights, fp32 out, bias): zimage.cpp:97-112 (adaLN), :171 (cap_embed),
+# :198 (context refiner at M = 128 text tokens).
+SKINNY_SHAPES = [
+    ("adaln_gemv", 1, 15360, 256),
+    ("cap_embed", 128, 3840, 2560),
+    ("context_refiner_qkv", 128, 11520, 3840),
+    ("context_refiner_w13", 128, 20480, 3840),
+    ("context_refiner_w2", 128, 3840, 10240),
+]
+
+
+def skinny_shapes(dev, stream, hbm_peak, launches=40):
+    """CUDA-event time per call of sdb200_gemm_nt_bf16 on each SKINNY_SHAPES entry. Each
+    shape cycles through enough distinct weight matrices to hold more than 2x the 126 MB
+    L2, so every call streams its weights from HBM. Algorithmic bytes per call: weights
+    2NK + A 4MK + C 4MN + bias 4N."""
+    import torch
+
+    import sdb200
+
+    L = sdb200.lib()
+    out = {}
+    for name, M, N, K in SKINNY_SHAPES:
+        wbytes = 2 * N * K
+        copies = max(2, -(-(256 << 20) // wbytes))
+        g = torch.Generator(device=dev)
+        g.manual_seed(N + K)
+        Ws = [(0.02 * torch.randn((N, K), generator=g, device=dev)).to(torch.bfloat16) for _ in range(copies)]
+        A = torch.randn((M, K), generator=g, device=dev)
+        bias = 0.01 * torch.randn((N,), generator=g, device=dev)
+        C = torch.empty((M, N), device=dev)
+
+        def call(i):
+            sdb200.check(L.sdb200_gemm_nt_bf16(M, N, K, A.data_ptr(), K, Ws[i % copies].data_ptr(), K, C.data_ptr(),
+                                               N, bias.data_ptr(), 0))
+
+        for i in range(copies):
+            call(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(launches):
+            call(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / launches
+        nbytes = wbytes + 4 * M * K + 4 * M * N + 4 * N
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"M": M, "N": N, "K": K, "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "gb_s": gbs,
+                     "frac_hbm": gbs / hbm_peak, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
+                     "path": "k_gemm_skinny (exact fp32 A)" if M <= 16 else "bf16 pack + k_gemm_tc",
+                     "weights_cycled": copies}
+        del Ws, A, bias, C
+    torch.cuda.empty_cache()
+    return out
+
+
+def hbm_in_step(prof, hbm_peak):
+    """GB/s of the memory-bound kernels timed live inside one profiled step (CUDA events
+    around every launch on the library's stream), against the measured copy bandwidth."""
+    out = {"peak_gb_s": hbm_peak, "peak_kind": "MEASURED_PEAKS.json hbm_gbs (copy)"}
+    for key, kern in (("post_norm", "k_post_norm_mod_bcast_v4 (post-norm + gated residual + next RMSNorm x mod)"),
+                      ("adaln", "k_gemm_skinny (adaLN GEMV, M = 1, N = 15360, K = 256)")):
+        ms, nbytes, n = prof.get(key + "_ms", 0.0), prof.get(key + "_bytes", 0.0), prof.get(key + "_launches", 0.0)
+        if not ms:
+            continue
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[key] = {"kernel": kern, "ms_per_step": ms, "launches_per_step": n, "bytes_per_launch": nbytes / n,
+                    "gb_s": gbs, "frac_hbm": gbs / hbm_peak}
+    return out
 
 
 def run_dit(args, world, rank, local, pg, dev):
@@ -525,6 +942,7 @@ def run_dit(args, world, rank, local, pg, dev):
     pk = peaks()
     gemm_tf = prof["gemm_flop"] / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] else None
     attn_tf = prof["attn_flop"] / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] else None
+    hbm = hbm_in_step(prof, pk["hbm"])
 
     # end to end through the C ABI: latents + text states in from pinned host memory,
     # prediction back out, every step
@@ -544,7 +962,17 @@ def run_dit(args, world, rank, local, pg, dev):
     # The whole sampler of BASELINE config 4 (8 flow-matching Euler steps, shift 3,
     # scheduler.cpp:117-135) on the device, once, after the per-step timing.
     sampler_ms = timed_loop(lambda: model.sample(x, cap, steps=8, shift=3.0), 1, stream, pg, dev)
+    if rank == 0:
+        hbm["skinny_shapes_standalone"] = skinny_shapes(dev, stream, pk["hbm"])
     err = be.device_error_word()
+    # At N > 1 the same run also times BASELINE config 5 (tensor parallelism over the N
+    # ranks), so a scaling run records both multi-GPU modes.
+    tp = None
+    if world > 1:
+        del model, wts
+        torch.cuda.empty_cache()
+        tp = measure_tp(args, world, rank, local, pg, dev, check_vs_single=True)
+        err |= be.device_error_word()
     cpu = cpu_baseline("dit") if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank == 0:
         line = {
@@ -573,19 +1001,23 @@ def run_dit(args, world, rank, local, pg, dev):
                     "d2h_bytes_per_step": int(outh.numel() * 4)},
             "sampler_8_steps": {"ms": sampler_ms, "ms_per_step": sampler_ms / 8,
                                 "note": "sdb200_zimage_sample: 8 flow-matching Euler steps, shift 3, on the device"},
+            "hbm_kernels": hbm,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "device_error_word": err,
         }
+        if tp is not None:
+            line["cfg5_tp"] = tp
         print(json.dumps(line), flush=True)
 
 
-def run_dit_tp(args, world, rank, local, pg, dev):
-    """the 30-layer DiT at batch 1, 2048x2048 (256x256 latent: 16384
-    image + 128 text tokens), Megatron tensor parallelism over the N ranks (column-parallel
-    QKV by heads and w1/w3, row-parallel to_out and w2, NCCL all-reduce after each
-    row-parallel projection, or with --tp-mode 1 the exchange fused into the kernels).
-    Total work fixed: "scaling": "strong"."""
+def measure_tp(args, world, rank, local, pg, dev, check_vs_single=False):
+    """BASELINE config 5 on the N ranks: the 30-layer DiT at batch 1, 2048x2048 (256x256
+    latent: 16384 image + 128 text tokens), Megatron tensor parallelism (column-parallel
+    QKV by heads and w1/w3, row-parallel to_out and w2; --tp-mode 1 combines the
+    row-parallel outputs inside the kernels over NVLink, 0 with an NCCL all-reduce).
+    Returns the measurements (every rank); with check_vs_single, rank 0 also runs the
+    unsharded model on its GPU and reports the relative error of the TP output."""
     import torch
 
     import sdb200
@@ -638,33 +1070,76 @@ def run_dit_tp(args, world, rank, local, pg, dev):
 
     e2e_step()
     e2e_ms = timed_loop(e2e_step, args.steps, stream, pg, dev) / args.steps
+    # every rank holds the whole output: the largest difference from rank 0's copy
+    y0 = out.clone()
+    if pg:
+        pg.broadcast(y0, src=0)
+    rank_diff = torch.tensor([float((out - y0).abs().max().item())], device=dev)
+    if pg:
+        pg.all_reduce(rank_diff, op=pg.ReduceOp.MAX)
+    hbm = hbm_in_step(prof, pk["hbm"])
+    model.set_tp(None)
+    comm.close()
+    del model, shards
+    torch.cuda.empty_cache()
+    rel = None
+    if check_vs_single and rank == 0:
+        single = ZImageB200(random_weights_torch(cfg, 0, dev), cfg)
+        ys = single.forward(x, 0.5, cap)
+        torch.cuda.synchronize()
+        rel = float((out.double() - ys.double()).norm() / ys.double().norm())
+        del single, ys
+        torch.cuda.empty_cache()
+    if pg:
+        pg.barrier()
+    comm_ms = prof["allreduce_ms"]
+    return {
+        "workload": "cfg5: 30-layer Z-Image DiT @2048^2 (16512 tokens), batch 1, one denoising step",
+        "ms_per_step": ms_step, "e2e_ms_per_step": e2e_ms, "tp_ranks": world, "steps": args.steps,
+        "parallelism": f"tensor-parallel x{world} (column QKV/w1/w3, row to_out/w2; " + (
+            "partial rows scattered to their owner rank from the GEMM epilogue over NVLink, "
+            "sequence-sharded post-norm broadcasting the next bf16 input)" if args.tp_mode == 1 else
+            "NCCL all-reduce fp32)"),
+        "tp_mode": args.tp_mode, "tp_barrier": args.tp_barrier if args.tp_mode == 1 else None,
+        "communicator_ranks": world, "step_tflops": fl["total"] / (ms_step * 1e-3) / 1e12,
+        "gemm_ms_per_step": prof["gemm_ms"], "gemm_tflops": gemm_tf, "attention_ms_per_step": prof["attn_ms"],
+        "attention_tflops": attn_tf, "comm_ms_per_step": comm_ms, "comm_calls_per_step": prof["allreduces"],
+        "comm_share": comm_ms / prof["forward_ms"] if prof["forward_ms"] else None,
+        "forward_ms_profiled": prof["forward_ms"], "hbm_kernels": hbm, "gpu_launches": int(launches),
+        "max_rank_diff": float(rank_diff.item()), "rel_err_vs_single_gpu": rel,
+        "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
+                "d2h_bytes_per_step": int(outh.numel() * 4)},
+        "gemm_peak": pk["sustained"], "clocks": clk.summary(),
+    }
+
+
+def run_dit_tp(args, world, rank, local, pg, dev):
+    """BASELINE config 5 as the line's own workload (see measure_tp). Total work fixed:
+    "scaling": "strong"."""
+    from sdb200 import backend as be
+
+    tp = measure_tp(args, world, rank, local, pg, dev)
     err = be.device_error_word()
     if rank == 0:
+        gemm_tf, peak = tp["gemm_tflops"], tp["gemm_peak"]
         print(json.dumps({
-            "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
+            "metric": METRIC, "value": tp["ms_per_step"], "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tp["ms_per_step"], "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 GEMM operands, fp16 attention operands, fp32 accumulate/activations",
             "data": "synthetic (random-init Z-Image-shaped weights, N(0,1) latent and text states)",
-            "config": {"workload": "cfg5: 30-layer Z-Image DiT @2048^2 (16512 tokens), batch 1, one denoising step",
-                       "global_batch": 1, "seq_len": 16512, "parallelism": f"tensor-parallel x{world} "
-                       "(column QKV/w1/w3, row to_out/w2; " + (
-                           "partial rows scattered to their owner rank from the GEMM epilogue over NVLink, "
-                           "sequence-sharded post-norm broadcasting the next bf16 input)" if args.tp_mode == 1 else
-                           "NCCL all-reduce fp32)"),
-                       "tp_barrier": args.tp_barrier if args.tp_mode == 1 else None},
-            "step_tflops": fl["total"] / (ms_step * 1e-3) / 1e12,
-            "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc_pair / k_gemm_tc (all GEMMs of one step, rank 0)", "achieved": gemm_tf,
-                         "peak": pk["sustained"], "unit": "TFLOP/s",
-                         "frac": (gemm_tf / pk["sustained"]) if gemm_tf else None,
-                         "peak_kind": f"{pk['kind']} bf16 sustained", "traffic": None,
-                         "gemm_ms_per_step": prof["gemm_ms"], "attention_tflops": attn_tf,
-                         "attention_ms_per_step": prof["attn_ms"], "comm_ms_per_step": prof["allreduce_ms"],
-                         "comm_calls_per_step": prof["allreduces"], "forward_ms_profiled": prof["forward_ms"]},
-            "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": int((xh.numel() + caph.numel()) * 4),
-                    "d2h_bytes_per_step": int(outh.numel() * 4)},
-            "cpu_baseline": None, "clocks": clk.summary(), "device_error_word": err}), flush=True)
-    comm.close()
+            "config": {"workload": tp["workload"], "global_batch": 1, "seq_len": 16512,
+                       "parallelism": tp["parallelism"], "tp_barrier": tp["tp_barrier"]},
+            "step_tflops": tp["step_tflops"], "gpu_launches": tp["gpu_launches"],
+            "roofline": {"bound": "tensor", "kernel": "k_gemm_tc_pair / k_gemm_tc (all GEMMs of one step, rank 0)",
+                         "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (gemm_tf / peak) if gemm_tf else None, "peak_kind": "bf16 sustained",
+                         "traffic": None, "gemm_ms_per_step": tp["gemm_ms_per_step"],
+                         "attention_tflops": tp["attention_tflops"],
+                         "attention_ms_per_step": tp["attention_ms_per_step"],
+                         "comm_ms_per_step": tp["comm_ms_per_step"], "comm_calls_per_step": tp["comm_calls_per_step"],
+                         "forward_ms_profiled": tp["forward_ms_profiled"]},
+            "hbm_kernels": tp["hbm_kernels"], "e2e": tp["e2e"], "max_rank_diff": tp["max_rank_diff"],
+            "cpu_baseline": None, "clocks": tp["clocks"], "device_error_word": err}), flush=True)
 
 
 def run_gemm(args, world, rank, local, pg, dev):
@@ -1060,7 +1535,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae"])
+    ap.add_argument("--workload", default="dit",
+                    choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae", "unet"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip the reference GPU backend comparison (oracle/_ref/libsdref_cuda.so)")
@@ -1104,6 +1580,8 @@ def main():
         run_conv(args, world, rank, local, pg, dev)
     elif args.workload == "vae":
         run_vae(args, world, rank, local, pg, dev)
+    elif args.workload == "unet":
+        run_unet(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:

@@ -102,16 +102,25 @@ int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
                          int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
 
-/* No counterpart in the reference. The gemm_nt_bf16 contraction above, same kernels and
- * results, for callers that cannot allocate device memory: code inside someone else's
- * CUDA-graph capture, hosts whose framework owns every device allocation, loops where
- * a synchronising cudaMalloc/cudaFree would stall. sdb200_gemm_nt_bf16 may grow a
- * workspace and create a device context (both cudaMalloc); this entry point calls no
- * allocator. A's bf16 copy goes to a fixed 32 MiB device array held by every GPU that
- * loads the library: M * round_up(K, 8) <= 16,777,216, and B must be 16-byte aligned
- * with ldb % 8 == 0, else SDB200_ERR_INVALID_ARG. The first call on a device resolves
- * the array's address (cudaGetSymbolAddress): make it before any stream capture. All
- * calls share the array; calls that overlap on the GPU race on it. */
+/* Extension: the activation rounding of gemm_nt_bf16 on its own (the pack kernel it runs
+ * before the tensor-core GEMM, backend_cuda.cu:183-188 / tensor.cpp:114-121: nearest
+ * even, inf and NaN truncated). src fp32 [rows, ld] -> dst bf16 bit patterns [rows, ldo],
+ * stream-ordered. Lets a caller round A once and reuse it through gemm_nt_bf16a. */
+int sdb200_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols);
+
+/* No counterpart in the reference. The gemm_nt_bf16 contraction above (same kernels,
+ * bit-identical results; M <= 16 takes the same exact fp32-A kernel) for callers that
+ * cannot allocate device memory: hosts whose framework owns every device allocation
+ * through its own pool, and loops that must never reach cudaMalloc/cudaFree (a cudaFree
+ * synchronises the device). sdb200_gemm_nt_bf16 may grow a workspace and create a
+ * device context (both cudaMalloc); this entry point calls no allocator. A's bf16 copy
+ * goes to a fixed 32 MiB device array held by every GPU that loads the library:
+ * M * round_up(K, 8) <= 16,777,216, and B must be 16-byte aligned with ldb % 8 == 0, else
+ * SDB200_ERR_INVALID_ARG. The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress); make it before any stream capture. It runs on the stream set by
+ * sdb200_set_stream when a context exists, else on the legacy default stream. All calls
+ * share the array; calls that overlap on the GPU race on it. A bounded-wait expiry is
+ * reported by sdb200_device_error_word / sdb200_synchronize. */
 int sdb200_gemm_nt_bf16_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
                                 int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
 
@@ -184,6 +193,11 @@ void sdb200_zimage_destroy(void* model);
  * last read, synchronising. */
 int sdb200_zimage_profile(void* model, int enable);
 int sdb200_zimage_profile_read(void* model, double* out10);
+/* The same record with the memory-bound kernels (n <= 16 values): out[0..10) as above,
+ * then post-norm ms, post-norm bytes, post-norm launches, adaLN GEMV ms, adaLN GEMV bytes,
+ * adaLN GEMV launches; bytes are the algorithmic minimum (inputs read once, outputs
+ * written once). */
+int sdb200_zimage_profile_read_ex(void* model, double* out, int n);
 /* Extension (the reference has no multi-GPU mode): Megatron-style tensor parallelism.
  * The caller registers this rank's shards (to_q/to_k/to_v rows and to_out columns of its
  * heads, w1/w3 rows and w2 columns of its FFN slice, row-parallel biases on rank 0 only)
@@ -223,6 +237,20 @@ int sdb200_zimage_load(void* model, const char* dir, const char* base, int rank,
  * dims). dst may be NULL to query the shape and dtype. */
 int sdb200_safetensors_read(const char* path, const char* name, int keep_bf16, int64_t bf16_min_numel, void* dst,
                             int64_t dst_bytes, int64_t* shape, int* ndim, int* is_bf16);
+/* Host only (extension of safetensors.cpp:80-194 / pipeline.cpp:113-115, which read the
+ * whole checkpoint on every process): the tensor `name` of the checkpoint <dir>/<base>
+ * exactly as sdb200_zimage_load uploads it for `rank` of `world` with `heads` attention
+ * heads - the same file lookup, dtype rule and Megatron cut. *ndim = -1 when this rank
+ * holds no part of it (a row-parallel bias on rank > 0) or its dtype is not read. dst may
+ * be NULL to query the shape and dtype. */
+int sdb200_checkpoint_read_shard(const char* dir, const char* base, const char* name, int rank, int world, int heads,
+                                 int64_t bf16_min_numel, void* dst, int64_t dst_bytes, int64_t* shape, int* ndim,
+                                 int* is_bf16);
+/* Extension: copies the weight `name` registered in the model (sdb200_zimage_set_weight
+ * or sdb200_zimage_load) to host memory dst (BF16 bit patterns when *is_bf16, else F32);
+ * synchronises. dst may be NULL to query the shape and dtype. */
+int sdb200_zimage_get_weight(void* model, const char* name, void* dst, int64_t dst_bytes, int64_t* shape, int* ndim,
+                             int* is_bf16);
 /* FlowMatchScheduler::set_timesteps (scheduler.cpp:117-127) on the host: sigmas[0..steps],
  * bit-identical to the reference's values. */
 int sdb200_flow_sigmas(int steps, float shift, float* sigmas);

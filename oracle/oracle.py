@@ -551,6 +551,9 @@ class RefCUDA(RefCPU):
                                    C.c_int)
         self._gemm_cuda = self.fn("cuda_gemm_nt_bf16", [_i64, _i64, _i64, v, _i64, v, _i64, v, _i64, v, C.c_int],
                                   C.c_int)
+        self._gemm32_cuda = self.fn("cuda_gemm_nt_f32", [_i64, _i64, _i64, v, _i64, v, _i64, v, _i64, v, C.c_int],
+                                    C.c_int)
+        self._geglu_cuda = self.fn("cuda_geglu", [v, v, _i64, _i64], C.c_int)
         self._attn_cuda = self.fn("cuda_attention", [v, v, v, v, _i64, _i64, _i64, C.c_int, C.c_int, _i64, C.c_int],
                                   C.c_int)
         self._conv_cuda = self.fn("cuda_conv2d", [v, _i64, _i64, _i64, _i64, v, _i64, _i64, _i64, v, C.c_int, C.c_int,
@@ -560,6 +563,12 @@ class RefCUDA(RefCPU):
 
     def gemm_nt_bf16_dev(self, M, N, K, A, lda, B, ldb, Cp, ldc, bias, acc=False):
         self._chk(self._gemm_cuda(M, N, K, A, lda, B, ldb, Cp, ldc, bias, int(acc)))
+
+    def gemm_nt_f32_dev(self, M, N, K, A, lda, B, ldb, Cp, ldc, bias, acc=False):
+        self._chk(self._gemm32_cuda(M, N, K, A, lda, B, ldb, Cp, ldc, bias, int(acc)))
+
+    def geglu_dev(self, x, y, rows, D):
+        self._chk(self._geglu_cuda(x, y, rows, D))
 
     def attention_dev(self, q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal=False):
         self._chk(self._attn_cuda(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, int(causal)))

@@ -233,6 +233,13 @@ int sdref_cuda_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int
                             int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
   return guard([&] { cuda::gemm_nt_bf16(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0); });
 }
+int sdref_cuda_gemm_nt_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                           float* C, int64_t ldc, const float* bias, int accumulate) {
+  return guard([&] { cuda::gemm_nt_f32(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0); });
+}
+int sdref_cuda_geglu(const float* x, float* y, int64_t rows, int64_t D) {
+  return guard([&] { cuda::geglu(x, y, rows, D); });
+}
 int sdref_cuda_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq,
                          int64_t Skv, int heads, int kv_heads, int64_t d, int causal) {
   return guard([&] { cuda::attention(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal != 0); });

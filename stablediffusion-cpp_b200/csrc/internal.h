@@ -8,6 +8,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 namespace sdb {
@@ -36,6 +37,9 @@ enum : int {
 };
 
 struct DeviceContext {
+  // Set (release) once every other field is filled; readers that skip the creation lock
+  // load it with acquire before touching the rest.
+  std::atomic<bool> ready{false};
   int device = -1;
   int num_sms = 0;
   int cc_major = 0, cc_minor = 0;
@@ -173,6 +177,15 @@ void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream
 // Small-M (M <= 16) GEMM through a memory-bound SIMT kernel (weights streamed once).
 void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
                         bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate);
+// The same kernel on an explicit SM count and stream (no device context needed).
+void launch_gemm_skinny_on(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
+                           bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate, int num_sms,
+                           cudaStream_t stream);
+// Whether (M, K) takes the skinny kernel in gemm_nt_bf16 / gemm_nt_f32.
+inline bool skinny_shape(int64_t M, int64_t K) { return M <= 16 && (size_t)(M * K) * 4 <= 160 * 1024; }
+// Bounded-wait status word of the no-allocation GEMM (noalloc.cu) on device `dev`: 0 when
+// that entry point never ran there; cleared after the read when `clear`.
+int noalloc_error_word(int dev, bool clear);
 
 // fp32 [rows, cols] (ld) -> bf16 [rows, cols] (ldo), RNE as the reference rounds.
 void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols);

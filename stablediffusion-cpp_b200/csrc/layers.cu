@@ -19,13 +19,13 @@ namespace {
 
 constexpr int kT = 256;
 
-unsigned grid_for(int64_t n, int per_thread = 1) {
+unsigned blocks_for(int64_t n, int per_thread = 1) {
   const int64_t blocks = (n / per_thread + kT - 1) / kT;
   const int64_t cap = (int64_t)std::max(1, ctx().num_sms) * 16;
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, cap));
 }
 
-#define GRID_STRIDE(i, n) \
+#define FOR_GRID_ITEMS(i, n) \
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (n); i += (int64_t)gridDim.x * blockDim.x)
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -66,7 +66,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // fp32 -> bf16 (reference rounding), 8 elements per thread when rows allow it.
 __global__ void k_pack_bf16_vec(const float* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
                                 int64_t rows, int64_t cols8) {
-  GRID_STRIDE(i, rows * cols8) {
+  FOR_GRID_ITEMS(i, rows * cols8) {
     const int64_t r = i / cols8, c = (i - r * cols8) * 8;
     const float4 a = *reinterpret_cast<const float4*>(src + r * ld + c);
     const float4 b = *reinterpret_cast<const float4*>(src + r * ld + c + 4);
@@ -80,7 +80,7 @@ __global__ void k_pack_bf16_vec(const float* __restrict__ src, int64_t ld, uint1
 }
 __global__ void k_pack_bf16(const float* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
                             int64_t rows, int64_t cols) {
-  GRID_STRIDE(i, rows * cols) {
+  FOR_GRID_ITEMS(i, rows * cols) {
     const int64_t r = i / cols, c = i - r * cols;
     dst[r * ldo + c] = f32_to_bf16_rne(src[r * ld + c]);
   }
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(256) k_pack_nhwc(const float* __restrict__ x, 
 }
 __global__ void k_conv_pack_w(const float* __restrict__ w, float* __restrict__ wp, int64_t Cin, int64_t taps,
                               int64_t cq, int64_t total) {
-  GRID_STRIDE(i, total) {
+  FOR_GRID_ITEMS(i, total) {
     const int64_t ci = i % cq, r = i / cq, t = r % taps, co = r / taps;
     wp[i] = ci < Cin ? round_tf32(__ldg(w + (co * Cin + ci) * taps + t)) : 0.0f;
   }
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(256) k_conv_direct_nhwc(
 // Split-K reduction (deterministic: the splits are summed in order).
 __global__ void k_split_reduce(const float* __restrict__ part, int splits, int64_t total, int64_t C, int64_t hw,
                                const float* __restrict__ bias, const float* res, float* out) {
-  GRID_STRIDE(i, total) {
+  FOR_GRID_ITEMS(i, total) {
     float s = part[i];
     for (int k = 1; k < splits; ++k) s += part[k * total + i];
     if (bias) s += __ldg(bias + (i / hw) % C);
@@ -376,27 +376,27 @@ __global__ void __launch_bounds__(256) k_pack_tf32_rows(const float* __restrict_
 }
 // In place (no restrict): x[r * ld + c] = tf32(x[r * ld + c]).
 __global__ void k_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
-  GRID_STRIDE(i, rows * cols) {
+  FOR_GRID_ITEMS(i, rows * cols) {
     const int64_t r = i / cols, c = i - r * cols;
     x[r * ld + c] = round_tf32(x[r * ld + c]);
   }
 }
 __global__ void k_copy2d_16(const uint16_t* __restrict__ src, int64_t ld, uint16_t* __restrict__ dst, int64_t ldo,
                             int64_t rows, int64_t cols) {
-  GRID_STRIDE(i, rows * cols) {
+  FOR_GRID_ITEMS(i, rows * cols) {
     const int64_t r = i / cols, c = i - r * cols;
     dst[r * ldo + c] = src[r * ld + c];
   }
 }
 __global__ void k_copy2d_32(const float* __restrict__ src, int64_t ld, float* __restrict__ dst, int64_t ldo,
                             int64_t rows, int64_t cols) {
-  GRID_STRIDE(i, rows * cols) {
+  FOR_GRID_ITEMS(i, rows * cols) {
     const int64_t r = i / cols, c = i - r * cols;
     dst[r * ldo + c] = src[r * ld + c];
   }
 }
 __global__ void k_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, int acc) {
-  GRID_STRIDE(i, M * N) {
+  FOR_GRID_ITEMS(i, M * N) {
     const int64_t r = i / N, c = i - r * N;
     const float b = bias ? bias[c] : 0.0f;
     float* p = C + r * ldc + c;
@@ -775,28 +775,6 @@ __global__ void k_rms_norm_heads(float* __restrict__ x, int64_t groups, int64_t 
   for (int64_t i = lane; i < dim; i += 32) p[i] = p[i] * rstd * (gamma ? gamma[i] : 1.0f);
 }
 
-// RoPE in place on x [N*S, inner], tables [S, dim] (tensor.cpp:701-730).
-__global__ void k_rope(float* __restrict__ x, int64_t NS, int64_t S, int64_t inner, int64_t dim,
-                       const float* __restrict__ cs, const float* __restrict__ sn, int interleaved) {
-  const int64_t half = dim / 2, heads = inner / dim;
-  GRID_STRIDE(i, NS * heads * half) {
-    const int64_t ns = i / (heads * half), rem = i - ns * heads * half, h = rem / half, j = rem - h * half;
-    const int64_t s = ns % S;
-    float* p = x + ns * inner + h * dim;
-    const float* c = cs + s * dim;
-    const float* sv = sn + s * dim;
-    if (interleaved) {
-      const int64_t a = 2 * j;
-      const float u = p[a], w = p[a + 1];
-      p[a] = u * c[a] - w * sv[a];
-      p[a + 1] = w * c[a] + u * sv[a];
-    } else {
-      const float u = p[j], w = p[j + half];
-      p[j] = u * c[j] - w * sv[j];
-      p[j + half] = w * c[j + half] + u * sv[j + half];
-    }
-  }
-}
 
 // Scaled, max-subtracted softmax per row; causal rows keep (row0 + r % rows_per_head) + 1
 // entries and zero the rest (tensor.cpp:752-769). Rows are ld apart; with round_out the
@@ -877,102 +855,11 @@ __global__ void k_transpose_tf32(const float* __restrict__ src, int64_t ld_src, 
   }
 }
 
-// ---------------------------------------------------------------------------------
-// Activations and elementwise (tensor.cpp:732-748, :813-935)
-// ---------------------------------------------------------------------------------
-__global__ void k_geglu(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t D) {
-  GRID_STRIDE(i, rows * D) {
-    const int64_t r = i / D, c = i - r * D;
-    const float a = x[r * 2 * D + c], g = x[r * 2 * D + D + c];
-    y[i] = a * 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-  }
-}
-__global__ void k_swiglu(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ y, int64_t n) {
-  GRID_STRIDE(i, n) y[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
-}
-__global__ void k_unary(float* __restrict__ x, int64_t n, int op) {
-  GRID_STRIDE(i, n) {
-    const float v = x[i];
-    float o;
-    switch (op) {
-      case 0: o = v / (1.0f + expf(-v)); break;                               // silu
-      case 1: o = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); break;  // gelu (erf)
-      case 2: o = v / (1.0f + expf(-1.702f * v)); break;                       // quick_gelu
-      default: o = tanhf(v); break;                                            // tanh
-    }
-    x[i] = o;
-  }
-}
-__global__ void k_add(float* __restrict__ a, const float* __restrict__ b, int64_t n) { GRID_STRIDE(i, n) a[i] += b[i]; }
-__global__ void k_affine(float* __restrict__ x, float a, float b, int64_t n) { GRID_STRIDE(i, n) x[i] = x[i] * a + b; }
-__global__ void k_mul_rows(float* __restrict__ x, const float* __restrict__ v, int64_t n, int64_t dim) {
-  GRID_STRIDE(i, n) x[i] *= v[i % dim];
-}
-__global__ void k_add_rows_scaled(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ g,
-                                  int64_t n, int64_t dim) {
-  GRID_STRIDE(i, n) x[i] += g[i % dim] * y[i];
-}
-__global__ void k_add_channel_bias(float* __restrict__ x, const float* __restrict__ b, int64_t n, int64_t HW) {
-  GRID_STRIDE(i, n) x[i] += b[i / HW];
-}
-__global__ void k_add_bias_rows(float* __restrict__ C, int64_t ldc, int64_t M, int64_t N, const float* __restrict__ b) {
-  GRID_STRIDE(i, M * N) {
-    const int64_t r = i / N, c = i - r * N;
-    C[r * ldc + c] += b[r];
-  }
-}
-
-// ---------------------------------------------------------------------------------
-// Layout ops (tensor.cpp:936-1090)
-// ---------------------------------------------------------------------------------
-__global__ void k_upsample2x(const float* __restrict__ x, float* __restrict__ y, int64_t NC, int64_t H, int64_t W) {
-  GRID_STRIDE(i, NC * 4 * H * W) {
-    const int64_t W2 = 2 * W, H2 = 2 * H;
-    const int64_t nc = i / (H2 * W2), rem = i - nc * H2 * W2, yy = rem / W2, xx = rem - yy * W2;
-    y[i] = x[(nc * H + yy / 2) * W + xx / 2];
-  }
-}
-__global__ void k_concat_channels(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
-                                  int64_t N, int64_t Ca, int64_t Cb, int64_t HW) {
-  GRID_STRIDE(i, N * (Ca + Cb) * HW) {
-    const int64_t C = Ca + Cb, n = i / (C * HW), rem = i - n * C * HW, c = rem / HW, s = rem - c * HW;
-    y[i] = c < Ca ? a[(n * Ca + c) * HW + s] : b[(n * Cb + (c - Ca)) * HW + s];
-  }
-}
-__global__ void k_nchw_to_nlc(const float* __restrict__ x, float* __restrict__ y, int64_t N, int64_t C, int64_t HW) {
-  GRID_STRIDE(i, N * C * HW) {  // i indexes y [N, HW, C]
-    const int64_t n = i / (HW * C), rem = i - n * HW * C, s = rem / C, c = rem - s * C;
-    y[i] = x[(n * C + c) * HW + s];
-  }
-}
-__global__ void k_nlc_to_nchw(const float* __restrict__ x, float* __restrict__ y, int64_t N, int64_t C, int64_t HW) {
-  GRID_STRIDE(i, N * C * HW) {  // i indexes y [N, C, HW]
-    const int64_t n = i / (C * HW), rem = i - n * C * HW, c = rem / HW, s = rem - c * HW;
-    y[i] = x[(n * HW + s) * C + c];
-  }
-}
-__global__ void k_patchify(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t H, int64_t W, int p) {
-  const int64_t Wt = W / p, F = (int64_t)p * p * C;
-  GRID_STRIDE(idx, C * H * W) {  // idx indexes the image [C, H, W]
-    const int64_t c = idx / (H * W), hh = (idx / W) % H, ww = idx % W;
-    const int64_t h = hh / p, ph = hh % p, w = ww / p, pw = ww % p;
-    y[(h * Wt + w) * F + (ph * p + pw) * C + c] = x[idx];
-  }
-}
-__global__ void k_unpatchify(const float* __restrict__ x, float* __restrict__ y, int64_t C, int64_t H, int64_t W,
-                             int p) {
-  const int64_t Wt = W / p, F = (int64_t)p * p * C;
-  GRID_STRIDE(idx, C * H * W) {
-    const int64_t c = idx / (H * W), hh = (idx / W) % H, ww = idx % W;
-    const int64_t h = hh / p, ph = hh % p, w = ww / p, pw = ww % p;
-    y[idx] = x[(h * Wt + w) * F + (ph * p + pw) * C + c];
-  }
-}
 // im2col rows for pixels p0..p0+P-1: cols[p, (ci, ky, kx)] (tensor.cpp:551-575).
 __global__ void k_im2col(const float* __restrict__ x, float* __restrict__ cols, int64_t Cin, int64_t H, int64_t W,
                          int64_t kh, int64_t kw, int64_t Wo, int stride, int pad, int64_t p0, int64_t P, int64_t K,
                          int64_t ldk) {
-  GRID_STRIDE(i, P * K) {
+  FOR_GRID_ITEMS(i, P * K) {
     const int64_t p = i / K, k = i - p * K;
     const int64_t ci = k / (kh * kw), r = k - ci * kh * kw, ky = r / kw, kx = r - ky * kw;
     const int64_t oy = (p0 + p) / Wo, ox = (p0 + p) % Wo;
@@ -991,9 +878,9 @@ void launch_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, 
   const bool vec = (cols % 8 == 0) && (ld % 4 == 0) && (ldo % 8 == 0) && ((uintptr_t)src % 16 == 0) &&
                    ((uintptr_t)dst % 16 == 0);
   if (vec)
-    k_pack_bf16_vec<<<grid_for(rows * cols, 8), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols / 8);
+    k_pack_bf16_vec<<<blocks_for(rows * cols, 8), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols / 8);
   else
-    k_pack_bf16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
+    k_pack_bf16<<<blocks_for(rows * cols), kT, 0, ctx().stream>>>(src, ld, dst, ldo, rows, cols);
   check_launch("pack_bf16");
 }
 void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int64_t H, int64_t W, const float* wp,
@@ -1021,7 +908,7 @@ void launch_conv_direct(const float* xh, int64_t N, int64_t Cin, int64_t cp, int
 void launch_split_reduce(const float* part, int splits, int64_t total, int64_t C, int64_t hw, const float* bias,
                          const float* res, float* out) {
   if (total <= 0) return;
-  k_split_reduce<<<grid_for(total), kT, 0, ctx().stream>>>(part, splits, total, C, hw, bias, res, out);
+  k_split_reduce<<<blocks_for(total), kT, 0, ctx().stream>>>(part, splits, total, C, hw, bias, res, out);
   check_launch("split_reduce");
 }
 void launch_conv_pack_x(const float* x, float* xh, int64_t N, int64_t C, int64_t HW, int64_t cp) {
@@ -1057,7 +944,7 @@ void launch_conv_pack_w(const float* w, float* wp, int64_t Cout, int64_t Cin, in
     else
       go(k_conv_pack_w_slab<false>);
   } else {
-    k_conv_pack_w<<<grid_for(total), kT, 0, ctx().stream>>>(w, wp, Cin, taps, cq, total);
+    k_conv_pack_w<<<blocks_for(total), kT, 0, ctx().stream>>>(w, wp, Cin, taps, cq, total);
   }
   check_launch("conv_pack_w");
 }
@@ -1082,42 +969,48 @@ void launch_pack_tf32_pair(const float* s0, int64_t ld0, float* d0, int64_t ldo0
 }
 void launch_round_tf32_inplace(float* x, int64_t ld, int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return;
-  k_round_tf32_inplace<<<grid_for(rows * cols), kT, 0, ctx().stream>>>(x, ld, rows, cols);
+  k_round_tf32_inplace<<<blocks_for(rows * cols), kT, 0, ctx().stream>>>(x, ld, rows, cols);
   check_launch("round_tf32");
 }
 void launch_copy2d(const void* src, int64_t ld, void* dst, int64_t ldo, int64_t rows, int64_t cols, int esize) {
   if (rows <= 0 || cols <= 0) return;
   if (esize == 2)
-    k_copy2d_16<<<grid_for(rows * cols), kT, 0, ctx().stream>>>((const uint16_t*)src, ld, (uint16_t*)dst, ldo, rows,
+    k_copy2d_16<<<blocks_for(rows * cols), kT, 0, ctx().stream>>>((const uint16_t*)src, ld, (uint16_t*)dst, ldo, rows,
                                                                  cols);
   else
-    k_copy2d_32<<<grid_for(rows * cols), kT, 0, ctx().stream>>>((const float*)src, ld, (float*)dst, ldo, rows, cols);
+    k_copy2d_32<<<blocks_for(rows * cols), kT, 0, ctx().stream>>>((const float*)src, ld, (float*)dst, ldo, rows, cols);
   check_launch("copy2d");
 }
 void launch_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const float* bias, bool accumulate) {
   if (M <= 0 || N <= 0) return;
-  k_bias_fill<<<grid_for(M * N), kT, 0, ctx().stream>>>(C, ldc, M, N, bias, accumulate ? 1 : 0);
+  k_bias_fill<<<blocks_for(M * N), kT, 0, ctx().stream>>>(C, ldc, M, N, bias, accumulate ? 1 : 0);
   check_launch("bias_fill");
 }
 void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
                         bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate) {
+  DeviceContext& c = ctx();
+  launch_gemm_skinny_on(M, N, K, A, lda, B, ldb, b_bf16, C, ldc, bias, accumulate, c.num_sms, c.stream);
+}
+void launch_gemm_skinny_on(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
+                           bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate, int num_sms,
+                           cudaStream_t stream) {
   const size_t smem = (size_t)(M * K) * sizeof(float);
   const int wpb = 8;
-  const int64_t blocks = std::min<int64_t>((N + wpb - 1) / wpb, (int64_t)ctx().num_sms * 8);
+  const int64_t blocks = std::min<int64_t>((N + wpb - 1) / wpb, (int64_t)num_sms * 8);
   if (b_bf16) {
     const bool vec = (ldb % 8 == 0) && ((uintptr_t)B % 16 == 0);
     if (smem > 48 * 1024)
       check_cuda(cudaFuncSetAttribute(k_gemm_skinny<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                  "skinny attr");
-    k_gemm_skinny<true><<<(unsigned)blocks, wpb * 32, smem, ctx().stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C,
-                                                                            ldc, bias, accumulate, vec);
+    k_gemm_skinny<true><<<(unsigned)blocks, wpb * 32, smem, stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C, ldc,
+                                                                      bias, accumulate, vec);
   } else {
     const bool vec = (ldb % 4 == 0) && ((uintptr_t)B % 16 == 0);
     if (smem > 48 * 1024)
       check_cuda(cudaFuncSetAttribute(k_gemm_skinny<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                  "skinny attr");
-    k_gemm_skinny<false><<<(unsigned)blocks, wpb * 32, smem, ctx().stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C,
-                                                                             ldc, bias, accumulate, vec);
+    k_gemm_skinny<false><<<(unsigned)blocks, wpb * 32, smem, stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C, ldc,
+                                                                       bias, accumulate, vec);
   }
   check_launch("gemm_skinny");
 }
@@ -1206,13 +1099,6 @@ void op_rms_norm_heads(float* x, int64_t groups, int64_t dim, const float* gamma
   k_rms_norm_heads<<<(unsigned)blocks, kT, 0, ctx().stream>>>(x, groups, dim, gamma, eps);
   check_launch("rms_norm_heads");
 }
-void op_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const float* cs, const float* sn,
-             bool interleaved) {
-  const int64_t total = N * S * (inner / dim) * (dim / 2);
-  if (total <= 0) return;
-  k_rope<<<grid_for(total), kT, 0, ctx().stream>>>(x, N * S, S, inner, dim, cs, sn, interleaved ? 1 : 0);
-  check_launch("rope");
-}
 void op_softmax_rows(float* x, int64_t rows, int64_t cols, float scale, bool causal, int64_t rows_per_head) {
   op_softmax_rows_ex(x, rows, cols, cols, scale, causal, rows_per_head, 0, false);
 }
@@ -1233,85 +1119,10 @@ void launch_transpose_tf32(const float* src, int64_t ld_src, float* dst, int64_t
   k_transpose_tf32<<<grid, dim3(32, 8), 0, ctx().stream>>>(src, ld_src, dst, ld_dst, rows, cols);
   check_launch("transpose_tf32");
 }
-void op_geglu(const float* x, float* y, int64_t rows, int64_t D) {
-  if (rows * D <= 0) return;
-  k_geglu<<<grid_for(rows * D), kT, 0, ctx().stream>>>(x, y, rows, D);
-  check_launch("geglu");
-}
-void op_swiglu(const float* g, const float* u, float* y, int64_t n) {
-  if (n <= 0) return;
-  k_swiglu<<<grid_for(n), kT, 0, ctx().stream>>>(g, u, y, n);
-  check_launch("swiglu");
-}
-void op_unary(float* x, int64_t n, int op) {
-  if (n <= 0) return;
-  k_unary<<<grid_for(n), kT, 0, ctx().stream>>>(x, n, op);
-  check_launch("unary");
-}
-void op_add(float* a, const float* b, int64_t n) {
-  if (n <= 0) return;
-  k_add<<<grid_for(n), kT, 0, ctx().stream>>>(a, b, n);
-  check_launch("add");
-}
-void op_affine(float* x, float a, float b, int64_t n) {
-  if (n <= 0) return;
-  k_affine<<<grid_for(n), kT, 0, ctx().stream>>>(x, a, b, n);
-  check_launch("affine");
-}
-void op_mul_rows(float* x, const float* v, int64_t rows, int64_t dim) {
-  if (rows * dim <= 0) return;
-  k_mul_rows<<<grid_for(rows * dim), kT, 0, ctx().stream>>>(x, v, rows * dim, dim);
-  check_launch("mul_rows");
-}
-void op_add_rows_scaled(float* x, const float* y, const float* g, int64_t rows, int64_t dim) {
-  if (rows * dim <= 0) return;
-  k_add_rows_scaled<<<grid_for(rows * dim), kT, 0, ctx().stream>>>(x, y, g, rows * dim, dim);
-  check_launch("add_rows_scaled");
-}
-void op_add_channel_bias(float* x, const float* b, int64_t N, int64_t C, int64_t HW) {
-  if (N * C * HW <= 0) return;
-  k_add_channel_bias<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, b, N * C * HW, HW);
-  check_launch("add_channel_bias");
-}
-void op_add_bias_rows(float* C, int64_t ldc, int64_t M, int64_t N, const float* b) {
-  if (M * N <= 0) return;
-  k_add_bias_rows<<<grid_for(M * N), kT, 0, ctx().stream>>>(C, ldc, M, N, b);
-  check_launch("add_bias_rows");
-}
-void op_upsample2x(const float* x, float* y, int64_t NC, int64_t H, int64_t W) {
-  if (NC * H * W <= 0) return;
-  k_upsample2x<<<grid_for(NC * 4 * H * W), kT, 0, ctx().stream>>>(x, y, NC, H, W);
-  check_launch("upsample_nearest2x");
-}
-void op_concat_channels(const float* a, const float* b, float* y, int64_t N, int64_t Ca, int64_t Cb, int64_t HW) {
-  if (N * (Ca + Cb) * HW <= 0) return;
-  k_concat_channels<<<grid_for(N * (Ca + Cb) * HW), kT, 0, ctx().stream>>>(a, b, y, N, Ca, Cb, HW);
-  check_launch("concat_channels");
-}
-void op_nchw_to_nlc(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
-  if (N * C * HW <= 0) return;
-  k_nchw_to_nlc<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, y, N, C, HW);
-  check_launch("nchw_to_nlc");
-}
-void op_nlc_to_nchw(const float* x, float* y, int64_t N, int64_t C, int64_t HW) {
-  if (N * C * HW <= 0) return;
-  k_nlc_to_nchw<<<grid_for(N * C * HW), kT, 0, ctx().stream>>>(x, y, N, C, HW);
-  check_launch("nlc_to_nchw");
-}
-void op_patchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
-  if (C * H * W <= 0) return;
-  k_patchify<<<grid_for(C * H * W), kT, 0, ctx().stream>>>(x, y, C, H, W, p);
-  check_launch("patchify");
-}
-void op_unpatchify(const float* x, float* y, int64_t C, int64_t H, int64_t W, int p) {
-  if (C * H * W <= 0) return;
-  k_unpatchify<<<grid_for(C * H * W), kT, 0, ctx().stream>>>(x, y, C, H, W, p);
-  check_launch("unpatchify");
-}
 void op_im2col(const float* x, float* cols, int64_t Cin, int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t Wo,
                int stride, int pad, int64_t p0, int64_t P, int64_t K, int64_t ldk) {
   if (P * K <= 0) return;
-  k_im2col<<<grid_for(P * K), kT, 0, ctx().stream>>>(x, cols, Cin, H, W, kh, kw, Wo, stride, pad, p0, P, K, ldk);
+  k_im2col<<<blocks_for(P * K), kT, 0, ctx().stream>>>(x, cols, Cin, H, W, kh, kw, Wo, stride, pad, p0, P, K, ldk);
   check_launch("im2col");
 }
 

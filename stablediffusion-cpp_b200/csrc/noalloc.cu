@@ -1,37 +1,42 @@
-// noalloc.cu - sdb200_gemm_nt_bf16_noalloc: the bf16-weight GEMM (same kernels and
-// results as sdb200_gemm_nt_bf16) for callers that cannot allocate device memory.
+// noalloc.cu - sdb200_gemm_nt_bf16_noalloc: the bf16-weight GEMM of sdb200_gemm_nt_bf16
+// (same kernels, bit-identical results) for callers that cannot allocate device memory.
 //
-// Who needs it: code that runs where cudaMalloc / cudaFree are unavailable or
-// forbidden - inside a region being captured into a CUDA graph by someone else,
-// under a host framework that owns every device allocation through its own pool
-// and rejects outside allocations, in a real-time loop where a synchronising
-// cudaMalloc (or freeing a grown workspace, which synchronises the device) would
-// stall the stream. sdb200_gemm_nt_bf16 may allocate: it grows a per-device
-// workspace for the bf16 copy of A on demand and creates a device context whose
-// error word is cudaMalloc'ed. This entry point does neither.
+// Who needs it: a host framework that owns every device allocation through its own pool
+// and rejects allocations made behind its back, and loops that must never reach a
+// cudaMalloc or cudaFree (cudaFree synchronises the whole device, so freeing a grown
+// workspace stalls every stream). sdb200_gemm_nt_bf16 may allocate on any call: it grows
+// a per-device workspace for the bf16 copy of A on demand, and its first call on a device
+// creates a device context whose error word is cudaMalloc'ed. This entry point does
+// neither.
 //
-// How: the bf16 copy of A lives in a file-scope device array of fixed size,
-// g_noalloc_a (16 Mi bf16 elements = 32 MiB). Every GPU that loads this library's
-// module holds that array until the process exits. Its device address is obtained
-// once per device with cudaGetSymbolAddress, with that device current, on the first
-// call made on the device; make that first call before any stream capture. Host code
-// must never pass the array's name itself to a kernel: on the host it is only a
-// stand-in symbol, not a device address.
+// How: the bf16 copy of A lives in a file-scope device array of fixed size, g_noalloc_a
+// (16 Mi bf16 elements = 32 MiB). Every GPU that loads this library's module holds that
+// array until the process exits. Its device address is obtained once per device with
+// cudaGetSymbolAddress, with that device current, during the first call made on the
+// device; that first call should come before any stream capture. Host code never passes
+// the array's name itself to a kernel: on the host it is only a stand-in symbol, not a
+// device address.
+//
+// Stream: the call is issued on the stream given to sdb200_set_stream for this device
+// when a library context exists, otherwise on the legacy default stream.
 //
 // Limits and sharing:
-//   * M * round_up(K, 8) must not exceed 16,777,216 (e.g. 4096 x 3840); larger
-//     problems are rejected with SDB200_ERR_INVALID_ARG before any GPU work.
-//   * B (the bf16 weights) is read in place by TMA, so it must be 16-byte aligned with
-//     ldb a multiple of 8 (there is no scratch to repack it); otherwise rejected.
+//   * M * round_up(K, 8) must not exceed 16,777,216 (e.g. 4096 x 3840); larger problems
+//     are rejected with SDB200_ERR_INVALID_ARG before any GPU work.
+//   * B (the bf16 weights) is read in place by TMA, so it must be 16-byte aligned with ldb
+//     a multiple of 8 (there is no scratch to repack it); otherwise rejected.
+//   * M <= 16 runs the exact fp32-A kernel of sdb200_gemm_nt_bf16 (A read in place, no
+//     scratch used), as that entry point does.
 //   * Every call on a device shares the one array and leaves its contents behind.
 //     Nothing in it has to start at zero: each call overwrites the rows and columns it
-//     reads (the kernel never reads past column K). Calls that may overlap on the GPU
+//     reads (the kernel's tensor map ends at column K). Calls that may overlap on the GPU
 //     (different streams, or different host threads on one device) race on the array;
 //     issue them on one stream or serialise them.
-//   * A bounded-wait expiry inside the kernel is recorded in the device error word of
-//     the library's context for this device when one exists (sdb200_synchronize reports
-//     it), otherwise in a word of this file's own; the kernel returns either way.
+//   * A bounded-wait expiry inside the kernel is recorded in a status word of this file,
+//     g_noalloc_err; sdb200_device_error_word reads it and sdb200_synchronize reports and
+//     clears it, together with the library context's own word.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -43,25 +48,26 @@ namespace sdb {
 namespace {
 
 constexpr size_t kNoAllocScratchElems = (size_t)16 << 20;  // bf16 elements (32 MiB)
+constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) uint16_t g_noalloc_a[kNoAllocScratchElems];
 static __device__ int g_noalloc_err;
 
 struct NoAllocDevice {
-  bool ready = false;
-  uint16_t* scratch = nullptr;  // device address of g_noalloc_a on this device
-  int* err = nullptr;           // device address of g_noalloc_err on this device
+  std::atomic<bool> ready{false};  // release-stored after the fields below are filled
+  uint16_t* scratch = nullptr;     // device address of g_noalloc_a on this device
+  int* err = nullptr;              // device address of g_noalloc_err on this device
   int num_sms = 0;
 };
-NoAllocDevice g_noalloc_dev[64];
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
 std::mutex g_noalloc_mutex;
 
 // Once per device, with that device current: resolve the arrays' device addresses.
 NoAllocDevice& noalloc_setup(int dev) {
   NoAllocDevice& d = g_noalloc_dev[dev];
-  if (d.ready) return d;
+  if (d.ready.load(std::memory_order_acquire)) return d;
   std::lock_guard<std::mutex> lk(g_noalloc_mutex);
-  if (d.ready) return d;
+  if (d.ready.load(std::memory_order_relaxed)) return d;
   int major = 0;
   check_cuda(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "cudaDeviceGetAttribute");
   if (major != 10) fail(kErrUnsupported, "gemm_nt_bf16_noalloc: device is not sm_100");
@@ -72,7 +78,7 @@ NoAllocDevice& noalloc_setup(int dev) {
   p = nullptr;
   check_cuda(cudaGetSymbolAddress(&p, g_noalloc_err), "cudaGetSymbolAddress(g_noalloc_err)");
   d.err = static_cast<int*>(p);
-  d.ready = true;
+  d.ready.store(true, std::memory_order_release);
   return d;
 }
 
@@ -109,22 +115,24 @@ void gemm_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, 
   require(ldc >= N, "ldc < N");
   require((reinterpret_cast<uintptr_t>(C) & 3) == 0, "C not 4-byte aligned");
   const int64_t Kp = (K + 7) / 8 * 8;
+  const bool skinny = K > 0 && skinny_shape(M, K);
   if (K > 0) {
     require(A != nullptr && B != nullptr, "null pointer A or B");
     require(lda >= K && ldb >= K, "lda or ldb < K");
-    require((reinterpret_cast<uintptr_t>(B) & 15) == 0 && ldb % 8 == 0,
-            "B must be 16-byte aligned with ldb a multiple of 8 (read in place; no scratch to repack it)");
-    require((size_t)M * (size_t)Kp <= kNoAllocScratchElems,
-            "M * round_up(K, 8) = " + std::to_string(M * Kp) + " exceeds the fixed scratch of " +
-                std::to_string(kNoAllocScratchElems) + " bf16 elements");
+    if (!skinny) {
+      require((reinterpret_cast<uintptr_t>(B) & 15) == 0 && ldb % 8 == 0,
+              "B must be 16-byte aligned with ldb a multiple of 8 (read in place; no scratch to repack it)");
+      require((size_t)M * (size_t)Kp <= kNoAllocScratchElems,
+              "M * round_up(K, 8) = " + std::to_string(M * Kp) + " exceeds the fixed scratch of " +
+                  std::to_string(kNoAllocScratchElems) + " bf16 elements");
+    }
   }
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-  require(dev >= 0 && dev < 64, "device ordinal out of range");
+  require(dev >= 0 && dev < kNoAllocMaxDevices, "device ordinal out of range");
   NoAllocDevice& d = noalloc_setup(dev);
   DeviceContext* c = ctx_if_created(dev);  // never creates one (that would allocate)
   cudaStream_t stream = c ? c->stream : nullptr;
-  int* err = c ? c->err_word : d.err;
   const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((M * std::max<int64_t>(K, N) + 255) / 256,
                                                                             (int64_t)d.num_sms * 16));
   if (K == 0) {
@@ -132,6 +140,7 @@ void gemm_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, 
     check_launch("gemm_nt_bf16_noalloc bias");
     return;
   }
+  if (skinny) return launch_gemm_skinny_on(M, N, K, A, lda, B, ldb, true, C, ldc, bias, acc, d.num_sms, stream);
   k_noalloc_pack<<<blocks, 256, 0, stream>>>(A, lda, d.scratch, Kp, M, K);
   check_launch("gemm_nt_bf16_noalloc pack");
   GemmCall g{};
@@ -150,10 +159,21 @@ void gemm_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, 
   g.epi = Epi::kStore;
   g.out_bf16 = false;
   g.bn = 0;
-  launch_gemm_tc_explicit(g, d.num_sms, stream, err, dev);
+  launch_gemm_tc_explicit(g, d.num_sms, stream, d.err, dev);
 }
 
 }  // namespace
+
+int noalloc_error_word(int dev, bool clear) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return 0;
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready.load(std::memory_order_acquire)) return 0;  // the entry point never ran on dev
+  int w = 0;
+  check_cuda(cudaMemcpy(&w, d.err, sizeof(int), cudaMemcpyDeviceToHost), "read no-alloc error word");
+  if (w && clear) check_cuda(cudaMemset(d.err, 0, sizeof(int)), "clear no-alloc error word");
+  return w;
+}
+
 }  // namespace sdb
 
 extern "C" int sdb200_gemm_nt_bf16_noalloc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,

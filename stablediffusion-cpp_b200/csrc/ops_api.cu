@@ -124,7 +124,7 @@ void gemm_f32_core(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
   launch_gemm_tc(g);
 }
 
-bool skinny_ok(int64_t M, int64_t K) { return M <= 16 && (size_t)(M * K) * 4 <= 160 * 1024; }
+bool skinny_ok(int64_t M, int64_t K) { return skinny_shape(M, K); }
 
 }  // namespace
 
@@ -338,6 +338,18 @@ int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
                          int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
   SDB_GUARD(gemm_nt_bf16a_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
+}
+int sdb200_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols) {
+  SDB_GUARD({
+    require(rows >= 0 && cols >= 0, "pack_bf16", "rows and cols must be >= 0");
+    if (rows == 0 || cols == 0) return kOk;
+    require(ld >= cols && ldo >= cols, "pack_bf16", "ld or ldo < cols");
+    require_ptr(src, "pack_bf16", "src");
+    require_ptr(dst, "pack_bf16", "dst");
+    require((reinterpret_cast<uintptr_t>(src) & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 1) == 0, "pack_bf16",
+            "misaligned src or dst");
+    launch_pack_bf16(src, ld, dst, ldo, rows, cols);
+  })
 }
 int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, int a_bf16,
                               const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, int y_bf16, const float* bias,

@@ -71,16 +71,19 @@ DeviceContext& ctx() {
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) fail(kErrUnsupported, "device ordinal out of range");
   DeviceContext& c = g_ctx[dev];
-  if (c.device < 0) {
+  if (!c.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lk(g_ctx_mutex);
-    if (c.device < 0) init_context(c, dev);
+    if (!c.ready.load(std::memory_order_relaxed)) {
+      init_context(c, dev);
+      c.ready.store(true, std::memory_order_release);
+    }
   }
   return c;
 }
 
 DeviceContext* ctx_if_created(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return nullptr;
-  return g_ctx[dev].device >= 0 ? &g_ctx[dev] : nullptr;
+  return g_ctx[dev].ready.load(std::memory_order_acquire) ? &g_ctx[dev] : nullptr;
 }
 
 void* workspace(size_t bytes) {
@@ -331,8 +334,9 @@ int sdb200_synchronize(void) {
     check_cuda(cudaStreamSynchronize(c.stream), "synchronize");
     int w = 0;
     check_cuda(cudaMemcpy(&w, c.err_word, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    if (w) check_cuda(cudaMemset(c.err_word, 0, sizeof(int)), "clear error word");
+    w |= noalloc_error_word(c.device, true);
     if (w) {
-      check_cuda(cudaMemset(c.err_word, 0, sizeof(int)), "clear error word");
       char buf[128];
       std::snprintf(buf, sizeof buf, "a kernel's bounded wait expired (device error word 0x%x)", w);
       fail(kErrDeviceWait, buf);
@@ -346,6 +350,7 @@ int sdb200_device_error_word(int* out) {
     DeviceContext& c = ctx();
     check_cuda(cudaStreamSynchronize(c.stream), "synchronize");
     check_cuda(cudaMemcpy(out, c.err_word, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    *out |= noalloc_error_word(c.device, false);
   })
 }
 

@@ -464,7 +464,7 @@ std::vector<std::string> checkpoint_files(const std::string& dir, const std::str
 }
 
 void read_checkpoint(const std::vector<std::string>& files, bool keep_bf16, int64_t min_numel, const TpShard* tp,
-                     const std::function<void(HostTensor&&)>& sink) {
+                     const std::function<void(HostTensor&&)>& sink, const std::string* only) {
   std::vector<File> fs;
   std::map<std::string, int64_t> rows;  // first dimension of every tensor (sharding needs D and F)
   for (const auto& path : files) {
@@ -478,6 +478,7 @@ void read_checkpoint(const std::vector<std::string>& files, bool keep_bf16, int6
   };
   for (const File& f : fs)
     for (const Entry& e : f.entries) {
+      if (only && e.name != *only) continue;
       const Plan plan = plan_shard(e.name, e.shape, tp, rows_of);
       if (plan.cut == Cut::Drop) continue;
       HostTensor t;

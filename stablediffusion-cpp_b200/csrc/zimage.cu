@@ -182,29 +182,39 @@ class ZImage {
     }
     marks.clear();
   }
-  // out[0..10]: gemm ms, gemm flop, gemm launches, attention ms, attention flop,
-  // attention launches, forward ms, forwards, all-reduce ms, all-reduces.
+  // out[0..n): gemm ms, gemm flop, gemm launches, attention ms, attention flop,
+  // attention launches, forward ms, forwards, all-reduce ms, all-reduces, then (n = 16)
+  // post-norm ms, post-norm bytes, post-norm launches, adaLN GEMV ms, adaLN bytes, adaLN
+  // launches. Bytes are the algorithmic minimum (inputs read once, outputs written once).
   // Synchronises; resets the record.
-  void prof_read(double* out) {
-    for (int i = 0; i < 10; ++i) out[i] = 0.0;
+  static constexpr int kProfValues = 16;
+  void prof_read(double* out, int n) {
+    double v[kProfValues] = {};
     check_cuda(cudaStreamSynchronize(ctx().stream), "profile sync");
     for (Mark& m : marks) {
       float ms = 0.0f;
       check_cuda(cudaEventElapsedTime(&ms, m.a, m.b), "cudaEventElapsedTime");
-      if (m.cat == 3) {
-        out[8] += ms;
-        out[9] += 1.0;
-        continue;
-      }
-      const int base = m.cat == 0 ? 0 : m.cat == 1 ? 3 : 6;
-      out[base] += ms;
-      if (m.cat < 2) {
-        out[base + 1] += m.flop;
-        out[base + 2] += 1.0;
-      } else {
-        out[7] += 1.0;
+      switch (m.cat) {
+        case 0: case 1: {  // GEMM, attention: ms, FLOP, launches
+          const int base = m.cat == 0 ? 0 : 3;
+          v[base] += ms;
+          v[base + 1] += m.flop;
+          v[base + 2] += 1.0;
+          break;
+        }
+        case 2: v[6] += ms; v[7] += 1.0; break;          // whole forward
+        case 3: v[8] += ms; v[9] += 1.0; break;          // collectives and barriers
+        case 4: case 5: {  // post-norm, adaLN GEMV: ms, bytes, launches
+          const int base = m.cat == 4 ? 10 : 13;
+          v[base] += ms;
+          v[base + 1] += m.flop;
+          v[base + 2] += 1.0;
+          break;
+        }
+        default: break;
       }
     }
+    for (int i = 0; i < n && i < kProfValues; ++i) out[i] = v[i];
     prof_clear();
   }
 
@@ -386,6 +396,15 @@ class ZImage {
     return (R + w - 1) / w * w;
   }
 
+  // Algorithmic bytes of one post-norm launch over `own` rows: the world partial rows and
+  // x read, x written, the next GEMM's bf16 row stored into nh buffers.
+  double post_norm_bytes(int64_t own, int world, int nh) const {
+    return (double)own * (double)D * (4.0 * world + 8.0 + 2.0 * nh);
+  }
+  // Algorithmic bytes of one adaLN GEMV: the bf16 weights [4D, tdim], the fp32 input,
+  // bias and output.
+  double adaln_bytes() const { return 2.0 * 4 * D * tdim + 4.0 * tdim + 8.0 * 4 * D; }
+
   void run_stage(const std::vector<Block>& blocks, float* x, int64_t B, int64_t S, const float* cs, const float* sn,
                  bool modulated) {
     if (blocks.empty()) return;
@@ -419,8 +438,10 @@ class ZImage {
     if (modulated)
       for (int64_t i = 0; i < nb; ++i) {
         float* mi = mods.as<float>() + i * 4 * D;
-        gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, blocks[i].adaln, tdim, mi, 4 * D, blocks[i].adaln_b,
-                          false);
+        timed(5, adaln_bytes(), [&] {
+          gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, blocks[i].adaln, tdim, mi, 4 * D,
+                            blocks[i].adaln_b, false);
+        });
         dit_adaln_split(mi, (int)D);
       }
     auto part = [&](int64_t i, int k) -> const float* {  // 0 scale_msa, 1 gate_msa, 2 scale_mlp, 3 gate_mlp
@@ -464,8 +485,10 @@ class ZImage {
       });
       timed(0, gf * D * Dq, [&] { gemm_bf16_scatter_impl(R, D, Dq, ao.p, Dq, true, b.wout, Dq, b.bout, so); });
       timed(3, 0.0, [&] { comm_barrier(comm); });
-      dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.attn_norm2, part(i, 1), b.ffn_norm1, part(i, 2),
-                              hall, w, norm_eps);
+      timed(4, post_norm_bytes(own, w, w), [&] {
+        dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.attn_norm2, part(i, 1), b.ffn_norm1, part(i, 2),
+                                hall, w, norm_eps);
+      });
       timed(3, 0.0, [&] { comm_barrier(comm); });
       timed(0, gf * 2 * b.F * D, [&] {
         gemm_bf16_epilogue_impl(R, 2 * b.F, D, hloc, D, true, b.w13.as<uint16_t>(), D, g.p, b.F, true,
@@ -474,12 +497,16 @@ class ZImage {
       timed(0, gf * b.F * D, [&] { gemm_bf16_scatter_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, b.b2, so); });
       timed(3, 0.0, [&] { comm_barrier(comm); });
       if (i + 1 < nb) {
-        dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), blocks[i + 1].attn_norm1,
-                                part(i + 1, 0), hall, w, norm_eps);
+        timed(4, post_norm_bytes(own, w, w), [&] {
+          dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), blocks[i + 1].attn_norm1,
+                                  part(i + 1, 0), hall, w, norm_eps);
+        });
         timed(3, 0.0, [&] { comm_barrier(comm); });
       } else {
-        dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), nullptr, nullptr, hall, 0,
-                                norm_eps);
+        timed(4, post_norm_bytes(own, w, 0), [&] {
+          dit_post_norm_mod_bcast(slots, Rs, w, row0, own, x, (int)D, b.ffn_norm2, part(i, 3), nullptr, nullptr, hall,
+                                  0, norm_eps);
+        });
       }
     }
     // Every rank gets every row of x (the buffer holds w * Rs rows).
@@ -493,8 +520,10 @@ class ZImage {
     const int64_t R = B * S;
     const float *scale_msa = nullptr, *gate_msa = nullptr, *scale_mlp = nullptr, *gate_mlp = nullptr;
     if (modulated) {
-      gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, b.adaln, tdim, mod.as<float>(), 4 * D, b.adaln_b,
-                        false);
+      timed(5, adaln_bytes(), [&] {
+        gemm_nt_bf16_impl(1, 4 * D, tdim, adaln.as<float>(), tdim, b.adaln, tdim, mod.as<float>(), 4 * D, b.adaln_b,
+                          false);
+      });
       dit_adaln_split(mod.as<float>(), (int)D);
       scale_msa = mod.as<float>();
       gate_msa = scale_msa + D;
@@ -528,7 +557,7 @@ class ZImage {
     });
     timed(0, gf * D * Dq, [&] { gemm_bf16_epilogue_impl(R, D, Dq, ao.p, Dq, true, b.wout, Dq, a.p, D, false, b.bout, 0); });
     if (comm_world(comm) > 1) timed(3, 0.0, [&] { comm_allreduce_sum(comm, a.as<float>(), (size_t)(R * D)); });
-    dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.attn_norm2, gate_msa, norm_eps);
+    timed(4, 12.0 * (double)(R * D), [&] { dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.attn_norm2, gate_msa, norm_eps); });
     // feed-forward
     dit_rms_mod_bf16(x, h.as<uint16_t>(), R, (int)D, b.ffn_norm1, scale_mlp, norm_eps);
     timed(0, gf * 2 * b.F * D, [&] {
@@ -537,7 +566,7 @@ class ZImage {
     });
     timed(0, gf * b.F * D, [&] { gemm_bf16_epilogue_impl(R, D, b.F, g.p, b.F, true, b.w2, b.F, a.p, D, false, b.b2, 0); });
     if (comm_world(comm) > 1) timed(3, 0.0, [&] { comm_allreduce_sum(comm, a.as<float>(), (size_t)(R * D)); });
-    dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.ffn_norm2, gate_mlp, norm_eps);
+    timed(4, 12.0 * (double)(R * D), [&] { dit_post_norm_residual(x, a.as<float>(), R, (int)D, b.ffn_norm2, gate_mlp, norm_eps); });
   }
 
   static int64_t pad_to(int64_t n) { return (n + 31) / 32 * 32; }
@@ -743,7 +772,14 @@ int sdb200_zimage_profile(void* m, int enable) {
 int sdb200_zimage_profile_read(void* m, double* out10) {
   SDB_GUARD({
     if (!m || !out10) sdb::fail(sdb::kErrInvalidArg, "zimage_profile_read: null pointer");
-    static_cast<ZImage*>(m)->prof_read(out10);
+    static_cast<ZImage*>(m)->prof_read(out10, 10);
+  })
+}
+
+int sdb200_zimage_profile_read_ex(void* m, double* out, int n) {
+  SDB_GUARD({
+    if (!m || !out || n < 0) sdb::fail(sdb::kErrInvalidArg, "zimage_profile_read_ex: null pointer or n < 0");
+    static_cast<ZImage*>(m)->prof_read(out, n);
   })
 }
 
@@ -791,6 +827,66 @@ int sdb200_zimage_load(void* m, const char* dir, const char* base, int rank, int
                            });
     } catch (const std::runtime_error& e) {
       sdb::fail(sdb::kErrInvalidArg, std::string("zimage_load: ") + e.what());
+    }
+  })
+}
+
+int sdb200_checkpoint_read_shard(const char* dir, const char* base, const char* name, int rank, int world, int heads,
+                                 int64_t bf16_min_numel, void* dst, int64_t dst_bytes, int64_t* shape, int* ndim,
+                                 int* is_bf16) {
+  SDB_GUARD({
+    if (!dir || !base || !name || !shape || !ndim || !is_bf16)
+      sdb::fail(sdb::kErrInvalidArg, "checkpoint_read_shard: null argument");
+    if (world < 1 || world > sdb::kMaxTpRanks || rank < 0 || rank >= world || heads < 1)
+      sdb::fail(sdb::kErrInvalidArg, "checkpoint_read_shard: bad rank / world / heads");
+    sdb::TpShard tp;
+    tp.rank = rank;
+    tp.world = world;
+    tp.heads = heads;
+    const std::string want(name);
+    *ndim = -1;  // no part of the tensor on this rank (or not read)
+    try {
+      const std::vector<std::string> files = sdb::checkpoint_files(dir, base);
+      sdb::read_checkpoint(
+          files, true, bf16_min_numel > 0 ? bf16_min_numel : ((int64_t)1 << 20), world > 1 ? &tp : nullptr,
+          [&](sdb::HostTensor&& t) {
+            if (t.shape.size() > 8) throw std::runtime_error("more than 8 dimensions");
+            *ndim = (int)t.shape.size();
+            for (size_t i = 0; i < t.shape.size(); ++i) shape[i] = t.shape[i];
+            *is_bf16 = t.bf16 ? 1 : 0;
+            if (dst) {
+              if ((int64_t)t.data.size() > dst_bytes) throw std::runtime_error("dst too small");
+              std::memcpy(dst, t.data.data(), t.data.size());
+            }
+          },
+          &want);
+    } catch (const std::runtime_error& e) {
+      sdb::fail(sdb::kErrInvalidArg, std::string("checkpoint_read_shard: ") + e.what());
+    }
+  })
+}
+
+int sdb200_zimage_get_weight(void* m, const char* name, void* dst, int64_t dst_bytes, int64_t* shape, int* ndim,
+                             int* is_bf16) {
+  SDB_GUARD({
+    if (!m || !name || !shape || !ndim || !is_bf16) sdb::fail(sdb::kErrInvalidArg, "zimage_get_weight: null argument");
+    ZImage* z = static_cast<ZImage*>(m);
+    const auto it = z->w.find(name);
+    if (it == z->w.end()) sdb::fail(sdb::kErrInvalidArg, std::string("zimage_get_weight: no weight ") + name);
+    const sdb::WRef& r = it->second;
+    if (r.shape.size() > 8) sdb::fail(sdb::kErrUnsupported, "zimage_get_weight: more than 8 dimensions");
+    int64_t n = 1;
+    for (size_t i = 0; i < r.shape.size(); ++i) {
+      shape[i] = r.shape[i];
+      n *= r.shape[i];
+    }
+    *ndim = (int)r.shape.size();
+    *is_bf16 = r.bf16 ? 1 : 0;
+    if (dst) {
+      const int64_t bytes = n * (r.bf16 ? 2 : 4);
+      if (bytes > dst_bytes) sdb::fail(sdb::kErrInvalidArg, "zimage_get_weight: dst too small");
+      sdb::check_cuda(cudaStreamSynchronize(sdb::ctx().stream), "zimage_get_weight: sync");
+      sdb::check_cuda(cudaMemcpy(dst, r.p, (size_t)bytes, cudaMemcpyDeviceToHost), "zimage_get_weight: copy");
     }
   })
 }

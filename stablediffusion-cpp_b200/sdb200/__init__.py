@@ -69,6 +69,7 @@ _SIGS = {
     "sdb200_gemm_nt_bf16": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16_noalloc": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16a": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
+    "sdb200_pack_bf16": ([_v, _i64, _v, _i64, _i64, _i64], _i),
     "sdb200_gemm_bf16_epilogue": ([_i64, _i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i, _v, _i], _i),
     "sdb200_set_attention_path": ([_i], _i),
     "sdb200_attention_f16": ([_v, _v, _v, _v, _i, _i64, _i64, _i64, _i, _i, _i64, _i64, _i], _i),
@@ -81,6 +82,7 @@ _SIGS = {
     "sdb200_zimage_destroy": ([_v], None),
     "sdb200_zimage_profile": ([_v, _i], _i),
     "sdb200_zimage_profile_read": ([_v, C.POINTER(C.c_double)], _i),
+    "sdb200_zimage_profile_read_ex": ([_v, C.POINTER(C.c_double), _i], _i),
     "sdb200_zimage_set_tp": ([_v, _v], _i),
     "sdb200_zimage_set_tp_mode": ([_v, _i], _i),
     "sdb200_zimage_sample": ([_v, _v, _i64, _i64, _i64, _i64, _v, _v, _i64, _i64, _f, _i, _f], _i),
@@ -96,6 +98,9 @@ _SIGS = {
     "sdb200_vae_profile": ([_v, _i], _i),
     "sdb200_vae_profile_read": ([_v, C.POINTER(C.c_double)], _i),
     "sdb200_safetensors_read": ([C.c_char_p, C.c_char_p, _i, _i64, _v, _i64, _v, _v, _v], _i),
+    "sdb200_checkpoint_read_shard": ([C.c_char_p, C.c_char_p, C.c_char_p, _i, _i, _i, _i64, _v, _i64, _v, _v, _v],
+                                     _i),
+    "sdb200_zimage_get_weight": ([_v, C.c_char_p, _v, _i64, _v, _v, _v], _i),
     "sdb200_comm_unique_id": ([_v], _i),
     "sdb200_comm_create": ([_v, _i, _i], _v),
     "sdb200_comm_allreduce_sum_f32": ([_v, _v, C.c_size_t], _i),
@@ -185,3 +190,27 @@ def safetensors_read(path: str, name: str, keep_bf16: bool = True, bf16_min_nume
                                         out.ctypes.data_as(C.c_void_p), out.nbytes, shape, C.byref(ndim),
                                         C.byref(isb)))
     return out
+
+
+def _read_tensor(call):
+    """Runs a (dst, dst_bytes, shape, ndim, is_bf16) reader twice: shape query, then data.
+    Returns a numpy uint16 (BF16 bits) or float32 array, or None when ndim < 0."""
+    import numpy as np
+
+    shape = (C.c_int64 * 8)()
+    ndim, isb = C.c_int(0), C.c_int(0)
+    check(call(None, 0, shape, C.byref(ndim), C.byref(isb)))
+    if ndim.value < 0:
+        return None
+    out = np.empty([shape[i] for i in range(ndim.value)], dtype=np.uint16 if isb.value else np.float32)
+    check(call(out.ctypes.data_as(C.c_void_p), out.nbytes, shape, C.byref(ndim), C.byref(isb)))
+    return out
+
+
+def checkpoint_read_shard(dir_: str, base: str, name: str, rank: int, world: int, heads: int,
+                          bf16_min_numel: int = 1 << 20):
+    """One tensor of a checkpoint as sdb200_zimage_load uploads it for rank of world
+    (host only); None when this rank holds no part of it."""
+    return _read_tensor(lambda d, nb, s, n, b: lib().sdb200_checkpoint_read_shard(
+        dir_.encode(), base.encode(), name.encode(), int(rank), int(world), int(heads), int(bf16_min_numel), d, nb,
+        s, n, b))

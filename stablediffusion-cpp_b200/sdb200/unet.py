@@ -1,12 +1,17 @@
-"""Random-init weights for a miniature SD 1.x UNet under the diffusers UNet2DConditionModel
-names that the reference binds (src/unet.cpp:18-56, src/modules.cpp:11-31, :86-131):
-conv_in, a time MLP, down blocks of (resnet [+ transformer]) with downsamplers, a mid block,
-up blocks of (layers + 1) resnets over concatenated skips with upsamplers, conv_out.
+"""Random-init weights for an SD 1.x UNet under the diffusers UNet2DConditionModel names
+that the reference binds (src/unet.cpp:18-56, src/modules.cpp:11-31, :86-131): conv_in, a
+time MLP, down blocks of (resnet [+ transformer]) with downsamplers, a mid block, up
+blocks of (layers + 1) resnets over concatenated skips with upsamplers, conv_out. No
+checkpoint exists here, so the UNet tests and benchmarks run on these.
 
 Convolution and linear weights ~N(0, 1/fan_in) so activations keep their scale, biases
-~N(0, 0.02), norm gammas ~N(1, 0.1) and betas ~N(0, 0.1). Test infrastructure only.
+~N(0, 0.02), norm gammas ~N(1, 0.1) and betas ~N(0, 0.1). `SD15` holds the SD 1.5 layout
+(channels 320 / 640 / 1280 / 1280, 2 layers per block, attention in the first three
+stages, text width 768).
 """
 import numpy as np
+
+SD15 = dict(channels=(320, 640, 1280, 1280), layers=2, in_ch=4, ctx_dim=768, attn=(True, True, True, False))
 
 
 def unet_specs(channels=(64, 128), layers=1, in_ch=4, ctx_dim=96, attn=(True, False)):

@@ -164,6 +164,14 @@ class ZImageB200:
         check(L.sdb200_zimage_finalize(self._m))
         return self
 
+    def get_weight(self, name: str):
+        """The registered weight `name` copied back to the host: numpy uint16 (BF16 bits)
+        or float32 (sdb200_zimage_get_weight)."""
+        from . import _read_tensor
+
+        return _read_tensor(lambda d, nb, s, n, b: lib().sdb200_zimage_get_weight(self._m, name.encode(), d, nb, s,
+                                                                                   n, b))
+
     def forward(self, x, t: float, cap, out=None):
         """x [B, C, H, W], cap [B, L, cap_dim] (CUDA fp32) -> [B, C, H, W]."""
         import torch
@@ -190,10 +198,12 @@ class ZImageB200:
         check(lib().sdb200_zimage_profile(self._m, int(enable)))
 
     def profile_read(self) -> dict:
-        out = (C.c_double * 10)()
-        check(lib().sdb200_zimage_profile_read(self._m, out))
+        """Kernel times since the last read (ms), algorithmic FLOP or bytes, launches."""
+        out = (C.c_double * 16)()
+        check(lib().sdb200_zimage_profile_read_ex(self._m, out, 16))
         keys = ("gemm_ms", "gemm_flop", "gemm_launches", "attn_ms", "attn_flop", "attn_launches", "forward_ms",
-                "forwards", "allreduce_ms", "allreduces")
+                "forwards", "allreduce_ms", "allreduces", "post_norm_ms", "post_norm_bytes", "post_norm_launches",
+                "adaln_ms", "adaln_bytes", "adaln_launches")
         return dict(zip(keys, list(out)))
 
     def set_tp(self, comm, mode: int = 1):

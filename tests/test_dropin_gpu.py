@@ -33,7 +33,7 @@ def dropin():
     (dict(channels=(320, 640), layers=1, in_ch=4, ctx_dim=768, attn=(True, True)), 8, 2, 16, 77),
 ])
 def test_unet_on_this_library(sdb, ref, dropin, cfg, heads, N, HW, L):
-    from unet_weights import unet_weights
+    from sdb200.unet import unet_weights
 
     w = unet_weights(seed=1, **cfg)
     rng = np.random.default_rng(2)
@@ -84,7 +84,7 @@ def test_sd15_unet_step_through_both_backends(sdb, dropin, capsys):
     import time
 
     from oracle import RefCUDA
-    from unet_weights import unet_weights
+    from sdb200.unet import unet_weights
 
     if not RefCUDA.available():
         pytest.skip("oracle/_ref/libsdref_cuda.so not built here")

@@ -108,8 +108,8 @@ def test_dit_forward_vs_reference_gpu(sdb, rgpu):
 
 def test_dit_full_model_vs_reference_gpu(sdb, rgpu):
     """BASELINE config 4's model at full size (30 layers + 2 + 2 refiners, 6.15 B parameters)
-    at 1024^2 for one image, against the reference's GPU forward over the same weights: the
-    full-depth parity check the CPU reference is too slow for."""
+    at 1024^2 for one image, against the reference's GPU forward over the same weights
+    (the CPU forward is the other full-depth check, tests/test_zimage_gpu.py)."""
     import torch
 
     from sdb200.zimage import Z_IMAGE, ZImageB200, random_weights_torch

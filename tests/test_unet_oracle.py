@@ -4,7 +4,7 @@ resnet with a skip of the right width, and predicts a latent of the input's shap
 import numpy as np
 import pytest
 
-from unet_weights import unet_specs, unet_weights
+from sdb200.unet import unet_specs, unet_weights
 
 
 @pytest.mark.parametrize("cfg,heads", [

@@ -100,6 +100,61 @@ def test_zimage_cfg3_block_1024(sdb, ref):
     assert rel_fro(got, want) <= TOL_LATENT
 
 
+def test_zimage_cfg5_block_2048(sdb, ref):
+    """BASELINE config 5's sequence on one GPU: one full-width single-stream block at 2048^2
+    (16384 image + 128 text tokens = 16512), random-init bf16 weights, against the
+    reference CPU forward compiled from its sources (zimage.cpp:90-136 at S = 16512)."""
+    from sdb200.zimage import ZConfig
+
+    cfg = ZConfig(layers=1, noise_refiners=0, context_refiners=0)
+    w, bf, m = _model(cfg, 21)
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((1, 16, 256, 256)).astype(np.float32)
+    cap = rng.standard_normal((1, 128, 2560)).astype(np.float32)
+    got = _np(m.forward(_t(x), 0.35, _t(cap)))
+    want = ref.zimage(w, bf, heads=30)(x, 0.35, cap)
+    assert np.isfinite(got).all()
+    assert rel_fro(got, want) <= TOL_LATENT
+
+
+class _HostFloat32(dict):
+    """name -> torch CUDA tensor, handed out one tensor at a time as a float32 numpy array
+    (the reference model keeps its own bf16 copy; 6 B parameters never sit in fp32 on the
+    host at once)."""
+
+    def items(self):
+        for n, t in super().items():
+            yield n, t.float().cpu().numpy()
+
+
+def test_dit_full_model_vs_reference_cpu(sdb, ref):
+    """BASELINE config 4's model at full size (30 layers + 2 + 2 refiners, 6.15 B
+    parameters) for one image at 1024^2 (4224 tokens), against the reference's CPU
+    ZImageTransformer::forward (zimage.cpp:138-228) over the same weights: the full-depth
+    check against the CPU path, whose activations stay fp32 (the device rounds every GEMM
+    operand to bf16 and runs attention on fp16)."""
+    import torch
+
+    from sdb200.zimage import Z_IMAGE, ZImageB200, random_weights_torch
+
+    wts = random_weights_torch(Z_IMAGE, 5, "cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2025)
+    x = torch.randn((1, 16, 128, 128), generator=g, device="cuda")
+    cap = torch.randn((1, 128, Z_IMAGE.cap_dim), generator=g, device="cuda")
+    model = ZImageB200(wts, Z_IMAGE)
+    got = _np(model.forward(x, 0.6, cap))
+    del model
+    bf = {n for n, t in wts.items() if t.dtype == torch.bfloat16}
+    rm = ref.zimage(_HostFloat32(wts), bf, heads=Z_IMAGE.heads)
+    del wts
+    torch.cuda.empty_cache()
+    want = rm(x.cpu().numpy(), 0.6, cap.cpu().numpy())
+    del rm
+    assert np.isfinite(got).all()
+    assert rel_fro(got, want) <= TOL_LATENT
+
+
 @pytest.mark.parametrize("cfg_scale", [0.0, 2.0])
 def test_zimage_sampler_on_device(sdb, orc, ref, cfg_scale):
     """sdb200_zimage_sample (the pipeline's flow-matching Euler loop run on the device)

@@ -1,11 +1,14 @@
 """GPU: sdb200_gemm_nt_bf16_noalloc, the GEMM entry point for callers that cannot
-allocate device memory (inside another party's graph capture, under a framework that
-owns all device allocations, in loops that must not hit a synchronising cudaMalloc).
+allocate device memory (a host framework that owns every device allocation through its
+own pool, or a loop that must never reach a device-synchronising cudaMalloc / cudaFree).
 
-It must give the results of sdb200_gemm_nt_bf16 (same kernels) on consecutive calls
-that share its fixed scratch array, leave device free memory unchanged, and reject
-problems larger than the scratch. No sdb200 call precedes the first no-alloc call here,
-so in a fresh process it also runs without a library device context.
+It must give exactly the results of sdb200_gemm_nt_bf16 (the same kernels and the same
+bf16 rounding of A) on consecutive calls that share its fixed scratch array, stay within
+the bf16-weight GEMM gate of the CPU oracle, leave device free memory unchanged, report a
+clean status word, and reject problems larger than the scratch. No sdb200 call precedes
+the first no-alloc call here, so in a fresh process the first two calls also run without
+a library device context. This file is collected last so that a failure here comes after
+every other test has run.
 """
 import ctypes
 
@@ -16,7 +19,7 @@ from conftest import rel_fro
 
 pytestmark = pytest.mark.gpu
 
-TOL_BF16 = 2e-3  # the bf16-weight GEMM tolerance of tests/test_gemm_gpu.py
+TOL_BF16 = 2e-3  # the bf16-weight GEMM gate of tests/test_gemm_gpu.py
 
 
 def _inputs(rng, M, N, K):
@@ -24,14 +27,25 @@ def _inputs(rng, M, N, K):
 
     from sdb200.workloads import f32_to_bf16_bits
 
-    A = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    A = rng.standard_normal((M, K)).astype(np.float32)
     Wb = f32_to_bf16_bits((0.02 * rng.standard_normal((N, K))).astype(np.float32))
-    B = torch.from_numpy(Wb.view(np.int16)).cuda().view(torch.bfloat16)
-    bias = torch.from_numpy((0.01 * rng.standard_normal(N)).astype(np.float32)).cuda()
-    return A, B, bias
+    bias = (0.01 * rng.standard_normal(N)).astype(np.float32)
+    dev = (torch.from_numpy(A).cuda(), torch.from_numpy(Wb.view(np.int16)).cuda(), torch.from_numpy(bias).cuda())
+    return (A, Wb, bias), dev
 
 
-def test_noalloc_matches_gemm_nt_bf16_on_consecutive_calls():
+def _noalloc(L, sdb200, M, N, K, A, B, bias, Y):
+    sdb200.check(L.sdb200_gemm_nt_bf16_noalloc(M, N, K, A.data_ptr(), K, B.data_ptr(), K, Y.data_ptr(), N,
+                                               bias.data_ptr(), 0))
+
+
+def _error_word(L, sdb200):
+    w = ctypes.c_int(-1)
+    sdb200.check(L.sdb200_device_error_word(ctypes.byref(w)))
+    return w.value
+
+
+def test_noalloc_matches_gemm_nt_bf16_on_consecutive_calls(orc):
     import torch
 
     import sdb200
@@ -40,48 +54,55 @@ def test_noalloc_matches_gemm_nt_bf16_on_consecutive_calls():
         pytest.fail("GPU test selected but torch sees no CUDA device")
     L = sdb200.lib()
     rng = np.random.default_rng(2024)
-    shapes = [(1000, 1536, 640), (4096, 2304, 3840)]  # second: M * K = 15.7 Mi, near the 16 Mi limit
+    # (1000, 1536, 640): ragged M; (4096, 2304, 3840): M * K = 15.7 Mi, near the 16 Mi
+    # limit; (8, 3840, 256): M <= 16, the exact fp32-A kernel, no scratch used.
+    shapes = [(1000, 1536, 640), (4096, 2304, 3840), (8, 3840, 256)]
     cases = []
     for M, N, K in shapes:
-        A, B, bias = _inputs(rng, M, N, K)
-        cases.append((M, N, K, A, B, bias, torch.empty((M, N), device="cuda"), torch.empty((M, N), device="cuda")))
+        host, (A, B, bias) = _inputs(rng, M, N, K)
+        cases.append((M, N, K, host, A, B, bias, torch.empty((M, N), device="cuda"),
+                      torch.empty((M, N), device="cuda")))
     torch.cuda.synchronize()
 
     # first call on this device: resolves the scratch address (set-up), then runs
-    M, N, K, A, B, bias, Y, _ = cases[0]
-    sdb200.check(L.sdb200_gemm_nt_bf16_noalloc(M, N, K, A.data_ptr(), K, B.data_ptr(), K, Y.data_ptr(), N,
-                                               bias.data_ptr(), 0))
+    M, N, K, _, A, B, bias, Y, _ = cases[0]
+    _noalloc(L, sdb200, M, N, K, A, B, bias, Y)
     torch.cuda.synchronize()
 
     # second call, larger shape, measured: device free memory must not move
-    M2, N2, K2, A2, B2, bias2, Y2, _ = cases[1]
+    M, N, K, _, A, B, bias, Y, _ = cases[1]
     free_before, _ = torch.cuda.mem_get_info()
-    sdb200.check(L.sdb200_gemm_nt_bf16_noalloc(M2, N2, K2, A2.data_ptr(), K2, B2.data_ptr(), K2, Y2.data_ptr(), N2,
-                                               bias2.data_ptr(), 0))
+    _noalloc(L, sdb200, M, N, K, A, B, bias, Y)
     torch.cuda.synchronize()
     free_after, _ = torch.cuda.mem_get_info()
     assert free_after == free_before, "the no-alloc entry point changed device free memory"
+    # the status of those two calls (no library context existed while they ran)
+    assert _error_word(L, sdb200) == 0
 
-    # the existing entry point on the same inputs
-    for M, N, K, A, B, bias, Y, Yref in cases:
+    # third call: the small-M path
+    M, N, K, _, A, B, bias, Y, _ = cases[2]
+    _noalloc(L, sdb200, M, N, K, A, B, bias, Y)
+
+    # the existing entry point on the same inputs: bit-identical outputs
+    for M, N, K, _, A, B, bias, _, Yref in cases:
         sdb200.check(L.sdb200_gemm_nt_bf16(M, N, K, A.data_ptr(), K, B.data_ptr(), K, Yref.data_ptr(), N,
                                            bias.data_ptr(), 0))
     torch.cuda.synchronize()
-    for M, N, K, A, B, bias, Y, Yref in cases:
+    for M, N, K, (Ah, Wh, bh), _, _, _, Y, Yref in cases:
         got, want = Y.cpu().numpy(), Yref.cpu().numpy()
         assert np.isfinite(got).all()
-        assert rel_fro(got, want) <= TOL_BF16, (M, N, K)
+        assert np.array_equal(got, want), (M, N, K, float(np.abs(got - want).max()))
+        rows = np.arange(M) if M <= 1024 else np.random.default_rng(M).choice(M, 256, replace=False)
+        assert rel_fro(got[rows], orc.gemm_nt_bf16(np.ascontiguousarray(Ah[rows]), Wh, bh)) <= TOL_BF16, (M, N, K)
 
     # repeat the first shape after the larger one: stale scratch contents do not leak in
-    M, N, K, A, B, bias, Y, Yref = cases[0]
+    M, N, K, _, A, B, bias, Y, Yref = cases[0]
     Y.zero_()
-    sdb200.check(L.sdb200_gemm_nt_bf16_noalloc(M, N, K, A.data_ptr(), K, B.data_ptr(), K, Y.data_ptr(), N,
-                                               bias.data_ptr(), 0))
+    _noalloc(L, sdb200, M, N, K, A, B, bias, Y)
     torch.cuda.synchronize()
-    assert rel_fro(Y.cpu().numpy(), Yref.cpu().numpy()) <= TOL_BF16
-    w = ctypes.c_int(0)
-    sdb200.check(L.sdb200_device_error_word(ctypes.byref(w)))
-    assert w.value == 0
+    assert torch.equal(Y, Yref)
+    assert _error_word(L, sdb200) == 0
+    sdb200.check(L.sdb200_synchronize())
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
