@@ -122,7 +122,8 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g));
 __device__ __forceinline__ float gelu_erf_f(float g) { return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f)); }
 
 // Stores 32 consecutive fp32 results of one row (columns col0..col0+31).
-__device__ __forceinline__ void store_row32(const GemmParams& p, int row, int col0, float (&v)[32]) {
+__device__ __forceinline__ void store_row32(const GemmParams& p, int row, int col0, float (&v)[32],
+                                            long long off = 0) {
   if (p.out_bf16) {
     uint16_t* c = reinterpret_cast<uint16_t*>(p.C) + (long long)row * p.ldc + col0;
     if (p.vec_ok && col0 + 32 <= p.N) {
@@ -143,7 +144,7 @@ __device__ __forceinline__ void store_row32(const GemmParams& p, int row, int co
     }
     return;
   }
-  float* c = reinterpret_cast<float*>(p.C) + (long long)row * p.ldc + col0;
+  float* c = reinterpret_cast<float*>(p.C) + off + (long long)row * p.ldc + col0;
   if (p.vec_ok && col0 + 32 <= p.N) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -314,9 +315,11 @@ __device__ __forceinline__ void store_row16(const GemmParams& p, int row, int oc
 // The epilogue of one accumulator tile for one warp: TMEM lanes of rows
 // row_base..row_base+31 (this thread: row_base + lane) at TMEM address tbase, tile column
 // block nb. stg is this warp's 32 x kStgPitch staging block (Epi::kScatter).
+// With split-K (p.splits > 1, Epi::kStore only) the raw partial tile of K split `split`
+// goes to C + split * split_stride; bias and accumulate are applied by the reduction.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, uint32_t tbase, int row_base, int nb,
-                                              int lane) {
+                                              int lane, int split = 0) {
   const int row = row_base + lane;
   const bool row_ok = row < p.M;
   if constexpr (BN % 128 == 0) {
@@ -358,7 +361,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, u
       }
     }
     if (p.epi == (int)Epi::kStore) {
-      store_row32(p, row, col0, v);
+      store_row32(p, row, col0, v, (long long)split * p.split_stride);
     } else {
       // Interleaved pairs: columns [16j, 16j+16) are gates (SwiGLU) / values
       // (GEGLU) and [16j+16, 16j+32) the matching up / gate columns.
@@ -700,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (CONV)
         epilogue_conv<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane, split);
       else
-        epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane);
+        epilogue_tile<BN>(p, stg + q * (32 * kStgPitch), tbase, mb * kBM + q * 32, nb, lane, split);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -1052,6 +1055,46 @@ void launch_bn_explicit(const GemmCall& g, const GemmParams& p, int num_sms, cud
   check_launch("gemm_tc");
 }
 
+// C[m, n] = sum over s < S of part[s][m][n] (+ bias[n]) (+ C[m, n] when acc): the
+// reduction of a split-K GEMM, partial tiles dense [S][M][N]; the sum runs in split order,
+// so results are deterministic. Four columns per thread when N, ldc and C allow it.
+__global__ void __launch_bounds__(256) k_split_k_sum(const float* __restrict__ part, int S, int64_t M, int64_t N,
+                                                     float* __restrict__ C, int64_t ldc, const float* __restrict__ bias,
+                                                     int acc, int vec) {
+  const int64_t stride = M * N;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const int64_t n4 = N / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * n4; i += step) {
+      const int64_t m = i / n4, c = (i - m * n4) * 4;
+      float4 t = *reinterpret_cast<const float4*>(part + m * N + c);
+      for (int s = 1; s < S; ++s) {
+        const float4 u = *reinterpret_cast<const float4*>(part + s * stride + m * N + c);
+        t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+      }
+      if (bias) {
+        const float4 b = *reinterpret_cast<const float4*>(bias + c);
+        t.x += b.x; t.y += b.y; t.z += b.z; t.w += b.w;
+      }
+      float4* d = reinterpret_cast<float4*>(C + m * ldc + c);
+      if (acc) {
+        const float4 o = *d;
+        t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
+      }
+      *d = t;
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * N; i += step) {
+    const int64_t m = i / N, c = i - m * N;
+    float t = part[i];
+    for (int s = 1; s < S; ++s) t += part[s * stride + i];
+    if (bias) t += bias[c];
+    float* d = C + m * ldc + c;
+    *d = acc ? *d + t : t;
+  }
+}
+
 int choose_bn(int64_t M, int64_t N, int num_sms, Epi epi) {
   // Every candidate BN is a multiple of the 32-column gated chunk; the QKV epilogue
   // needs whole 128-column heads per tile.
@@ -1134,6 +1177,53 @@ void launch_gemm_tc(const GemmCall& g) {
     const double pair_cost = (double)((pair_tiles + clusters - 1) / clusters) * (256 + 48) * 0.92;
     if (pair_cost <= single_cost || g_gemm_pair == 2) {
       launch_pair(g, p, c.device, c.stream);
+      return;
+    }
+  }
+  // Split-K for few-tile, long-K plain GEMMs (M of a few hundred rows against large
+  // weights: the context refiner and caption embedder at one image, the reference's
+  // linear() on short sequences). A single pass would leave most SMs idle while the rest
+  // stream the weights; instead each K split of each 128 x 256 tile runs on its own SM and
+  // a reduction kernel adds the partial tiles in split order with the bias.
+  // Taken when the 128 x 256 tiles fill at most half of the SMs and K has at least 16
+  // blocks; every split keeps at least 4 K blocks.
+  const int sbn = 256;
+  const int64_t tiles256 = (int64_t)p.m_tiles * ((g.N + sbn - 1) / sbn);
+  if (g.epi == Epi::kStore && !g.out_bf16 && !g.bn && !g_forced_bn && p.k_blocks >= 16 && tiles256 * 2 <= c.num_sms) {
+    const int64_t want = std::min<int64_t>(c.num_sms / tiles256, p.k_blocks / 4);
+    if (want >= 2) {
+      const int kb_split = (int)((p.k_blocks + want - 1) / want);
+      const int splits = (p.k_blocks + kb_split - 1) / kb_split;
+      const size_t part_bytes = (size_t)splits * (size_t)(g.M * g.N) * 4;
+      float* part = static_cast<float*>(split_workspace(part_bytes));
+      GemmCall gs = g;
+      gs.C = part;
+      gs.ldc = g.N;
+      gs.bias = nullptr;
+      gs.accumulate = false;
+      GemmParams ps = p;
+      ps.n_tiles = (int)((g.N + sbn - 1) / sbn);
+      ps.base_tiles = ps.m_tiles * ps.n_tiles;
+      ps.splits = splits;
+      ps.kb_split = kb_split;
+      ps.num_tiles = ps.base_tiles * splits;
+      ps.split_stride = (long long)(g.M * g.N);
+      ps.C = part;
+      ps.ldc = g.N;
+      ps.bias = nullptr;
+      ps.accumulate = 0;
+      ps.vec_ok = (g.N % 4) == 0;
+      if (g.tf32)
+        launch_bn<256, true>(gs, ps, c.num_sms);
+      else
+        launch_bn<256, false>(gs, ps, c.num_sms);
+      const bool vec = (g.N % 4 == 0) && (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) &&
+                       (!g.bias || (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0);
+      const int64_t work = vec ? g.M * (g.N / 4) : g.M * g.N;
+      const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)c.num_sms * 8));
+      k_split_k_sum<<<(unsigned)blocks, 256, 0, c.stream>>>(part, splits, g.M, g.N, static_cast<float*>(g.C), g.ldc,
+                                                            g.bias, g.accumulate ? 1 : 0, vec ? 1 : 0);
+      check_launch("gemm split-K reduction");
       return;
     }
   }

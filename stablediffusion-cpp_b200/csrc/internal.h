@@ -51,6 +51,10 @@ struct DeviceContext {
   // run in order, so one workspace per context is safe.
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // Split-K partial tiles of the GEMM (a second workspace: the first may hold the packed
+  // operands of the same call).
+  void* ws_split = nullptr;
+  size_t ws_split_bytes = 0;
 };
 
 // Context of the calling thread's current device (created on first use).
@@ -59,6 +63,8 @@ DeviceContext& ctx();
 DeviceContext* ctx_if_created(int dev);
 // Returns a workspace pointer of at least `bytes` bytes (256-byte aligned).
 void* workspace(size_t bytes);
+// The split-K partial-tile workspace (independent of workspace()).
+void* split_workspace(size_t bytes);
 // Encodes a 2-D/3-D tiled tensor map through the driver entry point.
 void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);

@@ -405,85 +405,99 @@ __global__ void k_bias_fill(float* C, int64_t ldc, int64_t M, int64_t N, const f
 }
 
 // ---------------------------------------------------------------------------------
-// Small-M GEMM: C[M,N] = A[M,K] B[N,K]^T (+bias) (+C), M <= 16, A staged in shared
-// memory, each warp streams whole rows of B (the weights) once. HBM-bound on B.
+// Small-M GEMM: C[M,N] = A[M,K] B[N,K]^T (+bias) (+C), M <= 16. HBM-bound on the
+// weights B, which are read once. A (fp32) is staged in shared memory once per CTA; each
+// warp then owns groups of kGemvRows consecutive rows of B and, per K chunk, issues the
+// 16-byte loads of all of them before any arithmetic, so that every warp keeps
+// kGemvRows x 512 bytes in flight. The 32 lane partial sums of each (row of B, row of A)
+// are combined by one shuffle tree at the end. MMAX (1, 4 or 16) bounds M at compile
+// time, so the M = 1 GEMV of the adaLN modulation carries no unused accumulators.
 // ---------------------------------------------------------------------------------
-template <bool BF16>
-__global__ void __launch_bounds__(256) k_gemm_skinny(int M, int N, int K, const float* __restrict__ A, int64_t lda,
-                                                     const void* __restrict__ Bv, int64_t ldb, float* __restrict__ C,
-                                                     int64_t ldc, const float* __restrict__ bias, int acc, int vec) {
-  extern __shared__ float sa[];  // [M][K]
-  for (int i = threadIdx.x; i < M * K; i += blockDim.x) sa[i] = A[(int64_t)(i / K) * lda + (i % K)];
+constexpr int kGemvRows = 4;
+constexpr int kGemvWarps = 8;
+
+__device__ __forceinline__ void widen_bf16x8(const uint4 w, float (&b)[8]) {
+  b[0] = __uint_as_float(w.x << 16); b[1] = __uint_as_float(w.x & 0xFFFF0000u);
+  b[2] = __uint_as_float(w.y << 16); b[3] = __uint_as_float(w.y & 0xFFFF0000u);
+  b[4] = __uint_as_float(w.z << 16); b[5] = __uint_as_float(w.z & 0xFFFF0000u);
+  b[6] = __uint_as_float(w.w << 16); b[7] = __uint_as_float(w.w & 0xFFFF0000u);
+}
+
+template <bool BF16, int MMAX>
+__global__ void __launch_bounds__(256) k_gemv_rows(int M, int N, int K, const float* __restrict__ A, int64_t lda,
+                                                   const void* __restrict__ Bv, int64_t ldb, float* __restrict__ C,
+                                                   int64_t ldc, const float* __restrict__ bias, int acc, int vec) {
+  constexpr int R = kGemvRows;
+  constexpr int E = BF16 ? 8 : 4;  // elements of B per 16-byte load
+  extern __shared__ float sa[];    // A as [M][K]
+  for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
+    const int m = i / K;
+    sa[i] = A[(int64_t)m * lda + (i - m * K)];
+  }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int wpb = blockDim.x >> 5;
-  const int64_t w0 = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5);
-  const int64_t wstep = (int64_t)gridDim.x * wpb;
-  for (int64_t n = w0; n < N; n += wstep) {
-    float s[16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int groups = (N + R - 1) / R;
+  for (int grp = blockIdx.x * kGemvWarps + warp; grp < groups; grp += gridDim.x * kGemvWarps) {
+    const int n0 = grp * R;
+    float s[R][MMAX];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) s[m] = 0.0f;
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int m = 0; m < MMAX; ++m) s[r][m] = 0.0f;
     int k0 = 0;
-    if (BF16) {
-      const uint16_t* b = reinterpret_cast<const uint16_t*>(Bv) + n * ldb;
-      if (vec) {
-        const int kv = K & ~255;
-        for (int k = lane * 8; k < kv; k += 256) {
-          const uint4 w = __ldg(reinterpret_cast<const uint4*>(b + k));
-          float bf[8];
-          bf[0] = __uint_as_float(w.x << 16); bf[1] = __uint_as_float(w.x & 0xFFFF0000u);
-          bf[2] = __uint_as_float(w.y << 16); bf[3] = __uint_as_float(w.y & 0xFFFF0000u);
-          bf[4] = __uint_as_float(w.z << 16); bf[5] = __uint_as_float(w.z & 0xFFFF0000u);
-          bf[6] = __uint_as_float(w.w << 16); bf[7] = __uint_as_float(w.w & 0xFFFF0000u);
+    if (vec) {
+      const int kv = K / (32 * E) * (32 * E);
+      for (int k = lane * E; k < kv; k += 32 * E) {
+        uint4 w[R];
 #pragma unroll
-          for (int m = 0; m < 16; ++m)
+        for (int r = 0; r < R; ++r) {
+          const int n = min(n0 + r, N - 1);  // rows past N repeat the last row; never stored
+          const char* row = reinterpret_cast<const char*>(Bv) + (int64_t)n * ldb * (BF16 ? 2 : 4);
+          w[r] = __ldg(reinterpret_cast<const uint4*>(row) + k / E);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float b[8];
+          if (BF16) {
+            widen_bf16x8(w[r], b);
+          } else {
+            b[0] = __uint_as_float(w[r].x); b[1] = __uint_as_float(w[r].y);
+            b[2] = __uint_as_float(w[r].z); b[3] = __uint_as_float(w[r].w);
+          }
+#pragma unroll
+          for (int m = 0; m < MMAX; ++m)
             if (m < M) {
               const float* a = sa + m * K + k;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) s[m] = fmaf(a[j], bf[j], s[m]);
+              for (int e = 0; e < E; ++e) s[r][m] = fmaf(a[e], b[e], s[r][m]);
             }
         }
-        k0 = kv;
       }
-      for (int k = k0 + lane; k < K; k += 32) {
-        const float bf = bf16_to_f32(b[k]);
+      k0 = kv;
+    }
+    for (int k = k0 + lane; k < K; k += 32) {
 #pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < M) s[m] = fmaf(sa[m * K + k], bf, s[m]);
-      }
-    } else {
-      const float* b = reinterpret_cast<const float*>(Bv) + n * ldb;
-      if (vec) {
-        const int kv = K & ~127;
-        for (int k = lane * 4; k < kv; k += 128) {
-          const float4 w = __ldg(reinterpret_cast<const float4*>(b + k));
+      for (int r = 0; r < R; ++r) {
+        const int n = min(n0 + r, N - 1);
+        const float b = BF16 ? bf16_to_f32(reinterpret_cast<const uint16_t*>(Bv)[(int64_t)n * ldb + k])
+                             : reinterpret_cast<const float*>(Bv)[(int64_t)n * ldb + k];
 #pragma unroll
-          for (int m = 0; m < 16; ++m)
-            if (m < M) {
-              const float* a = sa + m * K + k;
-              s[m] = fmaf(a[0], w.x, s[m]);
-              s[m] = fmaf(a[1], w.y, s[m]);
-              s[m] = fmaf(a[2], w.z, s[m]);
-              s[m] = fmaf(a[3], w.w, s[m]);
-            }
-        }
-        k0 = kv;
-      }
-      for (int k = k0 + lane; k < K; k += 32) {
-        const float bf = b[k];
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < M) s[m] = fmaf(sa[m * K + k], bf, s[m]);
+        for (int m = 0; m < MMAX; ++m)
+          if (m < M) s[r][m] = fmaf(sa[m * K + k], b, s[r][m]);
       }
     }
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      if (m < M) {
-        const float t = warp_sum(s[m]);
-        if (lane == 0) {
-          float* c = C + (int64_t)m * ldc + n;
-          const float v = t + (bias ? bias[n] : 0.0f);
-          *c = acc ? *c + v : v;
+    for (int r = 0; r < R; ++r) {
+      const int n = n0 + r;
+#pragma unroll
+      for (int m = 0; m < MMAX; ++m) {
+        if (m < M) {
+          const float t = warp_sum(s[r][m]);
+          if (lane == 0 && n < N) {
+            float* c = C + (int64_t)m * ldc + n;
+            const float v = t + (bias ? bias[n] : 0.0f);
+            *c = acc ? *c + v : v;
+          }
         }
       }
     }
@@ -995,22 +1009,26 @@ void launch_gemm_skinny_on(int64_t M, int64_t N, int64_t K, const float* A, int6
                            bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate, int num_sms,
                            cudaStream_t stream) {
   const size_t smem = (size_t)(M * K) * sizeof(float);
-  const int wpb = 8;
-  const int64_t blocks = std::min<int64_t>((N + wpb - 1) / wpb, (int64_t)num_sms * 8);
+  const int64_t groups = (N + kGemvRows - 1) / kGemvRows;
+  const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(8, (int64_t)(200 * 1024) / (int64_t)std::max<size_t>(smem, 1)));
+  const int64_t blocks = std::max<int64_t>(
+      1, std::min<int64_t>((groups + kGemvWarps - 1) / kGemvWarps, (int64_t)num_sms * per_sm));
+  const int esz = b_bf16 ? 2 : 4;
+  const bool vec = ((ldb * esz) % 16 == 0) && ((uintptr_t)B % 16 == 0);
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024)
+      check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gemv attr");
+    kern<<<(unsigned)blocks, kGemvWarps * 32, smem, stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C, ldc, bias,
+                                                              accumulate ? 1 : 0, vec ? 1 : 0);
+  };
   if (b_bf16) {
-    const bool vec = (ldb % 8 == 0) && ((uintptr_t)B % 16 == 0);
-    if (smem > 48 * 1024)
-      check_cuda(cudaFuncSetAttribute(k_gemm_skinny<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                 "skinny attr");
-    k_gemm_skinny<true><<<(unsigned)blocks, wpb * 32, smem, stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C, ldc,
-                                                                      bias, accumulate, vec);
+    if (M == 1) go(k_gemv_rows<true, 1>);
+    else if (M <= 4) go(k_gemv_rows<true, 4>);
+    else go(k_gemv_rows<true, 16>);
   } else {
-    const bool vec = (ldb % 4 == 0) && ((uintptr_t)B % 16 == 0);
-    if (smem > 48 * 1024)
-      check_cuda(cudaFuncSetAttribute(k_gemm_skinny<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                 "skinny attr");
-    k_gemm_skinny<false><<<(unsigned)blocks, wpb * 32, smem, stream>>>((int)M, (int)N, (int)K, A, lda, B, ldb, C, ldc,
-                                                                       bias, accumulate, vec);
+    if (M == 1) go(k_gemv_rows<false, 1>);
+    else if (M <= 4) go(k_gemv_rows<false, 4>);
+    else go(k_gemv_rows<false, 16>);
   }
   check_launch("gemm_skinny");
 }

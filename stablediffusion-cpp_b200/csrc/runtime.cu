@@ -98,6 +98,18 @@ void* workspace(size_t bytes) {
   return c.ws;
 }
 
+void* split_workspace(size_t bytes) {
+  DeviceContext& c = ctx();
+  if (bytes <= c.ws_split_bytes) return c.ws_split;
+  if (c.ws_split) check_cuda(cudaFree(c.ws_split), "cudaFree(split workspace)");
+  c.ws_split = nullptr;
+  c.ws_split_bytes = 0;
+  const size_t want = std::max(bytes, (size_t)16 << 20);
+  check_cuda(cudaMalloc(&c.ws_split, want), "cudaMalloc(split workspace)");
+  c.ws_split_bytes = want;
+  return c.ws_split;
+}
+
 void encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   if (!g_encode) {

@@ -230,3 +230,71 @@ def test_fused_gated_epilogue(sdb, orc, epi, y_bf16):
 def test_no_device_wait_expired(sdb):
     assert sdb.backend.device_error_word() == 0
     sdb.backend.synchronize()
+
+
+@pytest.mark.parametrize("M,N,K,f32", [(128, 3840, 10240, False), (128, 3840, 2560, False), (77, 1000, 3000, False),
+                                       (200, 1000, 4096, True)])
+def test_gemm_split_k(sdb, orc, M, N, K, f32):
+    """Few-tile, long-K GEMMs (the context refiner and caption embedder at one image: M =
+    128 text tokens against 3840 x 10240 / 3840 x 2560 weights) run as split-K: each K
+    split of each tile on its own SM, partial tiles added in split order with the bias by a
+    reduction kernel. Checked against the oracle (bias, accumulate, padded ldc), for
+    determinism, and against the unsplit kernel (forced tile width; same operands, only the
+    fp32 summation order differs)."""
+    import torch
+
+    rng = np.random.default_rng(M + N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    bias = (0.01 * rng.standard_normal(N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N + 4)).astype(np.float32)
+    rows = np.sort(np.random.default_rng(K).choice(M, 24, replace=False))
+    be = sdb.backend
+    if f32:
+        Wd = _t(W)
+        run = lambda C, acc, b: be.gemm_nt_f32(_t(A), Wd, b, C, acc, M=M, N=N, K=K, ldc=N + 4)  # noqa: E731
+        want = orc.gemm_nt(np.ascontiguousarray(A[rows]), W, bias, C0[rows], len(rows), N, K)
+        tol = TOL_TF32
+    else:
+        Wh = orc.to_bf16(W)
+        Wd = _bf16_t(Wh)
+        run = lambda C, acc, b: be.gemm_nt_bf16(_t(A), Wd, b, C, acc, M=M, N=N, K=K, ldc=N + 4)  # noqa: E731
+        want = orc.gemm_nt_bf16(np.ascontiguousarray(A[rows]), Wh, bias, C0[rows], len(rows), N, K)
+        tol = TOL_BF16
+    C = _t(C0)
+    run(C, True, _t(bias))
+    got = _np(C)
+    assert rel_fro(got[rows, :N], want[:, :N]) <= tol
+    assert np.array_equal(got[:, N:], C0[:, N:])  # padding columns untouched
+    C2 = _t(C0)
+    run(C2, True, _t(bias))
+    assert torch.equal(C, C2)  # deterministic
+    sdb.check(sdb.lib().sdb200_set_gemm_tile(256))
+    C3 = _t(C0)
+    run(C3, True, _t(bias))
+    sdb.check(sdb.lib().sdb200_set_gemm_tile(0))
+    assert rel_fro(got[:, :N], _np(C3)[:, :N]) <= TOL_EXACT
+
+
+@pytest.mark.parametrize("M", [1, 3, 16])
+@pytest.mark.parametrize("N,K,pad,f32", [(15360, 256, 0, False), (3841, 1000, 0, False), (1001, 2560, 3, False),
+                                         (777, 320, 0, True), (500, 700, 1, True)])
+def test_gemv_small_m(sdb, orc, M, N, K, pad, f32):
+    """M <= 16: the memory-bound GEMV (exact fp32 A, weights read once; the adaLN
+    modulation is M = 1, N = 15360, K = 256). Ragged N, a K tail outside the 16-byte body,
+    and a weight pitch that rules the vector loads out; bias and accumulate."""
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (0.02 * rng.standard_normal((N, K + pad))).astype(np.float32)
+    bias = (0.01 * rng.standard_normal(N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    be = sdb.backend
+    C = _t(C0)
+    if f32:
+        want = orc.gemm_nt(A, W, bias, C0, M, N, K, ldb=K + pad)
+        be.gemm_nt_f32(_t(A), _t(W), _t(bias), C, True, M=M, N=N, K=K, ldb=K + pad)
+    else:
+        Wh = orc.to_bf16(W)
+        want = orc.gemm_nt_bf16(A, Wh, bias, C0, M, N, K, ldb=K + pad)
+        be.gemm_nt_bf16(_t(A), _bf16_t(Wh), _t(bias), C, True, M=M, N=N, K=K, ldb=K + pad)
+    assert rel_fro(_np(C), want) <= TOL_EXACT
