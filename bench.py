@@ -842,13 +842,16 @@ SKINNY_SHAPES = [
 
 
 def skinny_shapes(dev, stream, hbm_peak, launches=40):
-    """CUDA-event time per call of sdb200_gemm_nt_bf16 on each SKINNY_SHAPES entry. Each
-    shape cycles through enough distinct weight matrices to hold more than 2x the 126 MB
-    L2, so every call streams its weights from HBM. Algorithmic bytes per call: weights
-    2NK + A 4MK + C 4MN + bias 4N."""
+    """Device time per call of sdb200_gemm_nt_bf16 on each SKINNY_SHAPES entry. Each shape
+    cycles through enough distinct weight matrices to hold more than 2x the 126 MB L2, so
+    every call streams its weights from HBM. The calls are recorded once into a CUDA graph
+    and replayed, so that the CUDA-event time is the kernels' (back to back on the device)
+    and not the host's per-call launch cost; `host_us_per_call` is the same loop launched
+    directly. Algorithmic bytes per call: weights 2NK + A 4MK + C 4MN + bias 4N."""
     import torch
 
     import sdb200
+    from sdb200 import backend as be
 
     L = sdb200.lib()
     out = {}
@@ -875,16 +878,63 @@ def skinny_shapes(dev, stream, hbm_peak, launches=40):
             call(i)
         b.record(stream)
         torch.cuda.synchronize()
+        host_ms = a.elapsed_time(b) / launches
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(stream)
+        with torch.cuda.graph(graph, stream=side):
+            be.bind_stream()  # the library issues on the capturing stream
+            for i in range(launches):
+                call(i)
+        be.bind_stream()
+        graph.replay()
+        torch.cuda.synchronize()
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
         ms = a.elapsed_time(b) / launches
+        del graph
         nbytes = wbytes + 4 * M * K + 4 * M * N + 4 * N
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out[name] = {"M": M, "N": N, "K": K, "us_per_call": ms * 1e3, "bytes_per_call": nbytes, "gb_s": gbs,
-                     "frac_hbm": gbs / hbm_peak, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
-                     "path": "k_gemm_skinny (exact fp32 A)" if M <= 16 else "bf16 pack + k_gemm_tc",
+        out[name] = {"M": M, "N": N, "K": K, "us_per_call": ms * 1e3, "host_us_per_call": host_ms * 1e3,
+                     "bytes_per_call": nbytes, "gb_s": gbs, "frac_hbm": gbs / hbm_peak,
+                     "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12,
+                     "path": "k_gemv_rows (exact fp32 A)" if M <= 16 else "bf16 pack + k_gemm_tc (split-K)",
                      "weights_cycled": copies}
         del Ws, A, bias, C
     torch.cuda.empty_cache()
     return out
+
+
+def run_skinny(args, world, rank, local, pg, dev):
+    """The skinny and epilogue-bound DiT GEMM shapes alone (SKINNY_SHAPES), through
+    sdb200_gemm_nt_bf16 with fp32 A, each cycling through more than 2x L2 of weights.
+    value = achieved HBM GB/s of the adaLN GEMV (M = 1, the first shape); the line lists
+    every shape."""
+    import torch
+
+    from sdb200 import backend as be
+
+    pk = peaks()
+    stream = torch.cuda.current_stream()
+    with ClockSampler(local) as clk:
+        shapes = skinny_shapes(dev, stream, pk["hbm"], launches=max(args.steps, 8))
+    first = shapes[SKINNY_SHAPES[0][0]]
+    if rank == 0:
+        print(json.dumps({
+            "metric": "HBM GB/s of the DiT's skinny GEMMs (adaLN GEMV M=1 x 15360 x 256)", "value": first["gb_s"],
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": first["us_per_call"] * 1e-3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32 A, bf16 weights, fp32 accumulate",
+            "data": "synthetic N(0,1) activations, N(0,0.02) weights",
+            "config": {"workload": "skinny DiT GEMM shapes through gemm_nt_bf16", "parallelism": f"replicas x{world}",
+                       "l2": "each shape cycles through > 256 MB of distinct weights"},
+            "roofline": {"bound": "hbm", "kernel": "k_gemv_rows (adaLN GEMV)", "achieved": first["gb_s"],
+                         "peak": pk["hbm"], "unit": "GB/s", "frac": first["gb_s"] / pk["hbm"],
+                         "traffic": profile_value("skinny_gemm_shapes.md", "traffic_bytes_per_launch")},
+            "shapes": shapes, "cpu_baseline": None, "clocks": clk.summary(),
+            "device_error_word": be.device_error_word()}), flush=True)
 
 
 def hbm_in_step(prof, hbm_peak):
@@ -892,13 +942,17 @@ def hbm_in_step(prof, hbm_peak):
     around every launch on the library's stream), against the measured copy bandwidth."""
     out = {"peak_gb_s": hbm_peak, "peak_kind": "MEASURED_PEAKS.json hbm_gbs (copy)"}
     for key, kern in (("post_norm", "k_post_norm_mod_bcast_v4 (post-norm + gated residual + next RMSNorm x mod)"),
-                      ("adaln", "k_gemm_skinny (adaLN GEMV, M = 1, N = 15360, K = 256)")):
+                      ("adaln", "k_gemv_rows (adaLN GEMV, M = 1, N = 15360, K = 256)")):
         ms, nbytes, n = prof.get(key + "_ms", 0.0), prof.get(key + "_bytes", 0.0), prof.get(key + "_launches", 0.0)
         if not ms:
             continue
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[key] = {"kernel": kern, "ms_per_step": ms, "launches_per_step": n, "bytes_per_launch": nbytes / n,
                     "gb_s": gbs, "frac_hbm": gbs / hbm_peak}
+    if "post_norm" in out:
+        out["post_norm"]["traffic_ncu_4096_rows"] = profile_value("post_norm_dit.md", "traffic_bytes_per_launch")
+        out["post_norm"]["traffic_note"] = ("ncu DRAM read + write of one 4096-row launch "
+                                            "(profiles/post_norm_dit.md; algorithmic 220 MB)")
     return out
 
 
@@ -913,8 +967,13 @@ def run_dit(args, world, rank, local, pg, dev):
     L = sdb200.lib()
     if GLOBAL_BATCH % world:
         raise SystemExit(f"global batch {GLOBAL_BATCH} does not split over {world} GPUs")
-    B = GLOBAL_BATCH // world
+    B = args.dit_batch or GLOBAL_BATCH // world
     cfg = Z_IMAGE
+    if args.dit_layers:
+        import dataclasses
+
+        cfg = dataclasses.replace(Z_IMAGE, layers=args.dit_layers)
+    profiling_size = bool(args.dit_layers or args.dit_batch)
     wts = random_weights_torch(cfg, 0, dev)
     model = ZImageB200(wts, cfg)
     g = torch.Generator(device=dev)
@@ -932,7 +991,7 @@ def run_dit(args, world, rank, local, pg, dev):
     launches = L.sdb200_launch_count() - n0
     ms_step = ms / args.steps
     fl = dit_forward_flops(cfg)
-    step_flop = GLOBAL_BATCH * fl["total"]
+    step_flop = B * world * fl["total"]
 
     # one profiled step: GEMM and attention kernels timed live with CUDA events
     model.profile(True)
@@ -962,7 +1021,7 @@ def run_dit(args, world, rank, local, pg, dev):
     # The whole sampler of BASELINE config 4 (8 flow-matching Euler steps, shift 3,
     # scheduler.cpp:117-135) on the device, once, after the per-step timing.
     sampler_ms = timed_loop(lambda: model.sample(x, cap, steps=8, shift=3.0), 1, stream, pg, dev)
-    if rank == 0:
+    if rank == 0 and not profiling_size:
         hbm["skinny_shapes_standalone"] = skinny_shapes(dev, stream, pk["hbm"])
     err = be.device_error_word()
     # At N > 1 the same run also times BASELINE config 5 (tensor parallelism over the N
@@ -985,7 +1044,7 @@ def run_dit(args, world, rank, local, pg, dev):
                        "global_batch": GLOBAL_BATCH, "images_per_gpu": B, "seq_len": 4224,
                        "parallelism": f"image-parallel x{world} (no collective)",
                        "l2": "weights 12.3 GB + activations > 126 MB L2 per step, no flush needed"},
-            "images_per_s": GLOBAL_BATCH / (ms_step * 1e-3),
+            "images_per_s": B * world / (ms_step * 1e-3),
             "step_tflops": step_flop / (ms_step * 1e-3) / 1e12,
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc_pair / k_gemm_tc (all GEMMs of one step, rank 0)",
@@ -1008,6 +1067,10 @@ def run_dit(args, world, rank, local, pg, dev):
         }
         if tp is not None:
             line["cfg5_tp"] = tp
+        if profiling_size:
+            line["config"]["workload"] = (f"PROFILING SIZE, not config 4: {cfg.layers}-layer Z-Image DiT @1024^2, "
+                                          f"{B} image(s) per GPU")
+            line["config"]["global_batch"] = B * world
         print(json.dumps(line), flush=True)
 
 
@@ -1536,7 +1599,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="dit",
-                    choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae", "unet"])
+                    choices=["dit", "dit_tp", "gemm", "attention", "conv", "vae", "unet", "skinny"])
+    ap.add_argument("--dit-layers", type=int, default=0,
+                    help="dit: profiling size - this many main layers instead of 30 (the line then says so)")
+    ap.add_argument("--dit-batch", type=int, default=0,
+                    help="dit: profiling size - this many images per GPU instead of 8 / N")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip the reference GPU backend comparison (oracle/_ref/libsdref_cuda.so)")
@@ -1582,6 +1649,8 @@ def main():
         run_vae(args, world, rank, local, pg, dev)
     elif args.workload == "unet":
         run_unet(args, world, rank, local, pg, dev)
+    elif args.workload == "skinny":
+        run_skinny(args, world, rank, local, pg, dev)
     else:
         run_gemm(args, world, rank, local, pg, dev)
     if pg:

@@ -423,18 +423,25 @@ __device__ __forceinline__ void widen_bf16x8(const uint4 w, float (&b)[8]) {
   b[6] = __uint_as_float(w.w << 16); b[7] = __uint_as_float(w.w & 0xFFFF0000u);
 }
 
-template <bool BF16, int MMAX>
+// ASMEM: A staged in shared memory (M up to 16 rows); otherwise each lane reads its A
+// values straight from global memory (small M x K, cached in L1 / L2 after the first warp),
+// so that the weight loads are issued at once instead of after an A staging round trip.
+template <bool BF16, int MMAX, bool ASMEM>
 __global__ void __launch_bounds__(256) k_gemv_rows(int M, int N, int K, const float* __restrict__ A, int64_t lda,
                                                    const void* __restrict__ Bv, int64_t ldb, float* __restrict__ C,
                                                    int64_t ldc, const float* __restrict__ bias, int acc, int vec) {
   constexpr int R = kGemvRows;
   constexpr int E = BF16 ? 8 : 4;  // elements of B per 16-byte load
-  extern __shared__ float sa[];    // A as [M][K]
-  for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
-    const int m = i / K;
-    sa[i] = A[(int64_t)m * lda + (i - m * K)];
+  extern __shared__ float sa[];    // A as [M][K] (ASMEM)
+  if (ASMEM) {
+    for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
+      const int m = i / K;
+      sa[i] = A[(int64_t)m * lda + (i - m * K)];
+    }
+    __syncthreads();
   }
-  __syncthreads();
+  const float* Ab = ASMEM ? sa : A;
+  const int64_t ald = ASMEM ? K : lda;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int groups = (N + R - 1) / R;
   for (int grp = blockIdx.x * kGemvWarps + warp; grp < groups; grp += gridDim.x * kGemvWarps) {
@@ -455,6 +462,23 @@ __global__ void __launch_bounds__(256) k_gemv_rows(int M, int N, int K, const fl
           const char* row = reinterpret_cast<const char*>(Bv) + (int64_t)n * ldb * (BF16 ? 2 : 4);
           w[r] = __ldg(reinterpret_cast<const uint4*>(row) + k / E);
         }
+        // Direct A: this lane's A values of the chunk, loaded alongside the weights.
+        float a[ASMEM ? 1 : MMAX][E];
+        if constexpr (!ASMEM) {
+#pragma unroll
+          for (int m = 0; m < MMAX; ++m)
+            if (m < M) {
+              const float4* ap = reinterpret_cast<const float4*>(A + m * lda + k);
+#pragma unroll
+              for (int e = 0; e < E; e += 4) {
+                const float4 v = __ldg(ap + e / 4);
+                a[m][e] = v.x;
+                a[m][e + 1] = v.y;
+                a[m][e + 2] = v.z;
+                a[m][e + 3] = v.w;
+              }
+            }
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           float b[8];
@@ -467,9 +491,8 @@ __global__ void __launch_bounds__(256) k_gemv_rows(int M, int N, int K, const fl
 #pragma unroll
           for (int m = 0; m < MMAX; ++m)
             if (m < M) {
-              const float* a = sa + m * K + k;
 #pragma unroll
-              for (int e = 0; e < E; ++e) s[r][m] = fmaf(a[e], b[e], s[r][m]);
+              for (int e = 0; e < E; ++e) s[r][m] = fmaf(ASMEM ? sa[m * K + k + e] : a[ASMEM ? 0 : m][e], b[e], s[r][m]);
             }
         }
       }
@@ -483,7 +506,7 @@ __global__ void __launch_bounds__(256) k_gemv_rows(int M, int N, int K, const fl
                              : reinterpret_cast<const float*>(Bv)[(int64_t)n * ldb + k];
 #pragma unroll
         for (int m = 0; m < MMAX; ++m)
-          if (m < M) s[r][m] = fmaf(sa[m * K + k], b, s[r][m]);
+          if (m < M) s[r][m] = fmaf(Ab[m * ald + k], b, s[r][m]);
       }
     }
 #pragma unroll
@@ -1008,13 +1031,16 @@ void launch_gemm_skinny(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 void launch_gemm_skinny_on(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const void* B, int64_t ldb,
                            bool b_bf16, float* C, int64_t ldc, const float* bias, bool accumulate, int num_sms,
                            cudaStream_t stream) {
-  const size_t smem = (size_t)(M * K) * sizeof(float);
-  const int64_t groups = (N + kGemvRows - 1) / kGemvRows;
-  const int64_t per_sm = std::max<int64_t>(1, std::min<int64_t>(8, (int64_t)(200 * 1024) / (int64_t)std::max<size_t>(smem, 1)));
-  const int64_t blocks = std::max<int64_t>(
-      1, std::min<int64_t>((groups + kGemvWarps - 1) / kGemvWarps, (int64_t)num_sms * per_sm));
   const int esz = b_bf16 ? 2 : 4;
   const bool vec = ((ldb * esz) % 16 == 0) && ((uintptr_t)B % 16 == 0);
+  // A read in place when it is 16-byte aligned row by row and M <= 4; otherwise staged.
+  const bool a_direct = M <= 4 && (lda % 4 == 0) && ((uintptr_t)A % 16 == 0);
+  const size_t smem = a_direct ? 0 : (size_t)(M * K) * sizeof(float);
+  const int64_t groups = (N + kGemvRows - 1) / kGemvRows;
+  const int64_t per_sm =
+      std::max<int64_t>(1, std::min<int64_t>(8, (int64_t)(200 * 1024) / (int64_t)std::max<size_t>(smem, 1)));
+  const int64_t blocks = std::max<int64_t>(
+      1, std::min<int64_t>((groups + kGemvWarps - 1) / kGemvWarps, (int64_t)num_sms * per_sm));
   auto go = [&](auto kern) {
     if (smem > 48 * 1024)
       check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gemv attr");
@@ -1022,13 +1048,23 @@ void launch_gemm_skinny_on(int64_t M, int64_t N, int64_t K, const float* A, int6
                                                               accumulate ? 1 : 0, vec ? 1 : 0);
   };
   if (b_bf16) {
-    if (M == 1) go(k_gemv_rows<true, 1>);
-    else if (M <= 4) go(k_gemv_rows<true, 4>);
-    else go(k_gemv_rows<true, 16>);
+    if (a_direct) {
+      if (M == 1) go(k_gemv_rows<true, 1, false>);
+      else go(k_gemv_rows<true, 4, false>);
+    } else if (M <= 4) {
+      go(k_gemv_rows<true, 4, true>);
+    } else {
+      go(k_gemv_rows<true, 16, true>);
+    }
   } else {
-    if (M == 1) go(k_gemv_rows<false, 1>);
-    else if (M <= 4) go(k_gemv_rows<false, 4>);
-    else go(k_gemv_rows<false, 16>);
+    if (a_direct) {
+      if (M == 1) go(k_gemv_rows<false, 1, false>);
+      else go(k_gemv_rows<false, 4, false>);
+    } else if (M <= 4) {
+      go(k_gemv_rows<false, 4, true>);
+    } else {
+      go(k_gemv_rows<false, 16, true>);
+    }
   }
   check_launch("gemm_skinny");
 }
