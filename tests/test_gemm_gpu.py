@@ -198,6 +198,24 @@ def test_dit_shapes_sampled(sdb, orc, M, N, K):
     assert rel_fro(got[rows], want) <= TOL_BF16
 
 
+@pytest.mark.parametrize("N,K", [(11520, 3840), (20480, 3840), (3840, 10240)])
+def test_dit_shapes_full_output_vs_reference(sdb, ref, N, K):
+    """Every output element of the Z-Image block GEMMs of one 1024^2 image (M = 4224 rows:
+    the fused q/k/v projection, the w1/w3 pair, w2) against the reference's own CPU
+    gemm_nt_bf16 (tensor.cpp:412-474, compiled from its sources, all host cores): the
+    per-GEMM gate on whole outputs, not on sampled rows."""
+    M = 4224
+    ref.set_num_threads(0)
+    rng = np.random.default_rng(N + 3 * K)
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    Wh = ref.to_bf16((0.02 * rng.standard_normal((N, K), dtype=np.float32)).astype(np.float32))
+    bias = (0.01 * rng.standard_normal(N)).astype(np.float32)
+    got = _np(sdb.backend.gemm_nt_bf16(_t(X), _bf16_t(Wh), _t(bias)))
+    want = ref.gemm_nt_bf16(X, Wh, bias)
+    assert np.isfinite(got).all()
+    assert rel_fro(got, want) <= TOL_BF16
+
+
 @pytest.mark.parametrize("epi", [1, 2])
 @pytest.mark.parametrize("y_bf16", [False, True])
 def test_fused_gated_epilogue(sdb, orc, epi, y_bf16):

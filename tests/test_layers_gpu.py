@@ -114,9 +114,10 @@ def test_attention_wide_heads_vs_oracle(sdb, orc, N, Sq, Skv, H, KVH, d, causal)
     assert rel_fro(got, want) <= 2e-3
 
 
-def test_attention_gemm_path_row_chunks(sdb, attention_path):
+def test_attention_gemm_path_row_chunks(sdb, ref, attention_path):
     """Skv large enough that the 256 MB score block holds fewer rows than Sq: several
-    query-row chunks, with the causal mask offset per chunk; against the exact kernel."""
+    query-row chunks, with the causal mask offset per chunk; against the reference's own
+    CPU attention (tensor.cpp:771-810, compiled from its sources) and the exact kernel."""
     import torch
 
     g = torch.Generator(device="cuda")
@@ -125,9 +126,12 @@ def test_attention_gemm_path_row_chunks(sdb, attention_path):
     q = torch.randn((1, Sq, d), generator=g, device="cuda")
     k = torch.randn((1, Skv, d), generator=g, device="cuda")
     v = torch.randn((1, Skv, d), generator=g, device="cuda")
+    ref.set_num_threads(0)
+    qh, kh, vh = _np(q), _np(k), _np(v)
     for causal in (False, True):
         attention_path(0)
         got = _np(sdb.backend.attention(q, k, v, 1, causal=causal))
+        assert rel_fro(got, ref.attention(qh, kh, vh, 1, 1, causal)) <= 2e-3, causal
         attention_path(1)
         want = _np(sdb.backend.attention(q, k, v, 1, causal=causal))
         assert rel_fro(got, want) <= 2e-3, causal
