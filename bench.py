@@ -561,6 +561,11 @@ def run_unet(args, world, rank, local, pg, dev):
 
     e2e_step()
     e2e_ms = timed_steps_flushed(e2e_step, args.steps, stream, pg, dev, flush) / args.steps
+    # The same op set with the opt-in packed-operand cache (constant weights packed once).
+    sdb200.check(L.sdb200_set_operand_cache(1))
+    step()
+    cached_ms = timed_steps_flushed(step, args.steps, stream, pg, dev, flush) / args.steps
+    sdb200.check(L.sdb200_set_operand_cache(0))
     if rank == 0:
         top_f = next(o for o in ops if o[0] == top)
         top_tf = per_op[top]["tflops"]
@@ -576,6 +581,7 @@ def run_unet(args, world, rank, local, pg, dev):
                        "parallelism": f"replicas x{world}", "l2": "256 MB buffer written before every step (untimed)",
                        "gflop_per_step": flop / 1e9},
             "step_tflops": flop / (ms_step * 1e-3) / 1e12, "gpu_launches": int(launches),
+            "ms_per_step_operand_cache": cached_ms,
             "roofline": {"bound": "tensor", "kernel": f"{top} (the op with the largest time)",
                          "achieved": top_tf, "peak": pk["burst"], "unit": "TFLOP/s",
                          "frac": top_tf / pk["burst"] if top_tf else None,
@@ -675,10 +681,15 @@ def dropin_line(args, world, local):
             rng = np.random.default_rng(4)
             x = rng.standard_normal((2, 4, 64, 64)).astype(np.float32)
             ctx = rng.standard_normal((2, 77, 768)).astype(np.float32)
+            import sdb200
+
             times, outs = {}, {}
-            for name, lib in (("reference_backend", RefCUDA() if RefCUDA.available() else None), ("sdb200", r)):
+            for name, lib in (("reference_backend", RefCUDA() if RefCUDA.available() else None), ("sdb200", r),
+                              ("sdb200_operand_cache", r)):
                 if lib is None:
                     continue
+                if name == "sdb200_operand_cache":
+                    sdb200.check(sdb200.lib().sdb200_set_operand_cache(1))
                 m = lib.unet(w, heads=8, on_device=True)
                 m(x, 500.0, ctx)
                 t0 = time.perf_counter()
@@ -686,11 +697,18 @@ def dropin_line(args, world, local):
                     outs[name] = m(x, 500.0, ctx)
                 times[name] = (time.perf_counter() - t0) / 3 * 1e3
                 del m
+                sdb200.check(sdb200.lib().sdb200_set_operand_cache(0))
             agree = None
-            if len(outs) == 2:
+            if "sdb200" in outs and "reference_backend" in outs:
                 a, b2 = outs["sdb200"].astype(np.float64), outs["reference_backend"].astype(np.float64)
                 agree = float(np.linalg.norm(a - b2) / np.linalg.norm(b2))
+            cache_agree = None
+            if "sdb200_operand_cache" in outs:
+                a, b2 = outs["sdb200_operand_cache"].astype(np.float64), outs["sdb200"].astype(np.float64)
+                cache_agree = float(np.linalg.norm(a - b2) / np.linalg.norm(b2))
             return {"value": times["sdb200"], "unit": "ms/UNet step", "kind": kind,
+                    "with_operand_cache_ms": times.get("sdb200_operand_cache"),
+                    "operand_cache_rel_diff": cache_agree,
                     "reference_backend_ms": times.get("reference_backend"), "rel_diff_vs_reference_backend": agree,
                     "sample": "the full SD 1.5 UNet (unet.cpp, 860 M fp32 parameters) at 512^2 with a CFG batch of 2, "
                               "mean of 3 steps, wall clock with latent in and prediction out"}

@@ -102,6 +102,20 @@ int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t
 int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, const uint16_t* B,
                          int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate);
 
+/* Extension (opt-in; the reference repacks nothing, its cuBLAS calls read fp32 weights
+ * directly): keep the packed form of constant operands across calls - the tf32-rounded B of
+ * gemm_nt_f32 and the [Cout, tap, Cin] slab of conv2d's stride-1 weights - instead of
+ * repacking them on every call. While it is on, such an operand must not change while it
+ * stays allocated, except through sdb200_upload / sdb200_copy / sdb200_zero, which drop the
+ * entries they overwrite; sdb200_free drops the entries of the freed buffer. Buffers from
+ * another allocator are not tracked: turn the cache off (which clears it) before freeing or
+ * rewriting them. Only the C-ABI gemm_nt_f32 / conv2d calls use it. Default: off, or on when
+ * the environment variable SDB200_OPERAND_CACHE=1 is set (so an unmodified caller of the
+ * sd::cuda symbols can use it). Turning it off frees every entry. */
+int sdb200_set_operand_cache(int enable);
+/* Number of packed operands currently kept (tests). */
+int64_t sdb200_operand_cache_entries(void);
+
 /* Extension: the activation rounding of gemm_nt_bf16 on its own (the pack kernel it runs
  * before the tensor-core GEMM, backend_cuda.cu:183-188 / tensor.cpp:114-121: nearest
  * even, inf and NaN truncated). src fp32 [rows, ld] -> dst bf16 bit patterns [rows, ldo],

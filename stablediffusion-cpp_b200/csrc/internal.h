@@ -273,11 +273,25 @@ void comm_sym_free(Comm* c, SymBuf& b);
 void* pool_malloc(size_t bytes);
 void pool_free(void* p);
 
+// Packed-operand cache (operand_cache.cu, opt-in): tf32-rounded GEMM weights and conv
+// weight slabs kept across calls, dropped when their source is freed or overwritten through
+// this library.
+bool operand_cache_on();
+void operand_cache_enable(bool on);
+int64_t operand_cache_entries();
+void operand_cache_invalidate(const void* p, size_t bytes);
+// B [rows, cols] (ld) rounded to tf32 with row pitch ldo; packed on the first call.
+const float* cached_tf32_rows(const float* B, int64_t rows, int64_t cols, int64_t ld, int64_t ldo);
+// Conv weights [Cout, Cin, taps] as [Cout, taps, cq] tf32; packed on the first call.
+const float* cached_conv_weight(const float* w, int64_t Cout, int64_t Cin, int64_t taps, int64_t cq);
+
 // GEMM front-ends with argument checks (ops_api.cu).
 void gemm_nt_bf16_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B, int64_t ldb,
                        float* C, int64_t ldc, const float* bias, bool acc);
+// b_constant: B is a caller's weight buffer that the opt-in operand cache may keep packed
+// (the C-ABI entry only; internal callers pass activations or scratch as B).
 void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
-                      float* C, int64_t ldc, const float* bias, bool acc);
+                      float* C, int64_t ldc, const float* bias, bool acc, bool b_constant = false);
 void gemm_bf16_scatter_impl(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,
                             int64_t ldb, const float* bias, const ScatterOut& so);
 void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, bool a_bf16, const uint16_t* B,

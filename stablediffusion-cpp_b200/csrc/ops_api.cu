@@ -96,15 +96,25 @@ void gemm_bf16_core(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
   launch_gemm_tc(g);
 }
 
+// b_constant: B is a caller's weight buffer (the C-ABI entry), eligible for the opt-in
+// packed-operand cache; internal callers pass activations or scratch as B.
 void gemm_f32_core(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
-                   int64_t ldc, const float* bias, bool acc) {
+                   int64_t ldc, const float* bias, bool acc, bool b_constant) {
   const int64_t Kp = round_up(K, 4);  // 16-byte rows of fp32
+  const bool cache_b = b_constant && operand_cache_on();
   const size_t a_bytes = align256((size_t)(M * Kp) * 4);
-  const size_t b_bytes = align256((size_t)(N * Kp) * 4);
+  const size_t b_bytes = cache_b ? 0 : align256((size_t)(N * Kp) * 4);
   uint8_t* ws = static_cast<uint8_t*>(workspace(a_bytes + b_bytes));
   float* pa = reinterpret_cast<float*>(ws);
-  float* pb = reinterpret_cast<float*>(ws + a_bytes);
-  launch_pack_tf32_pair(A, lda, pa, Kp, M, B, ldb, pb, Kp, N, K);
+  const float* pb;
+  if (cache_b) {
+    pb = cached_tf32_rows(B, N, K, ldb, Kp);  // the weights, packed once
+    launch_pack_tf32(A, lda, pa, Kp, M, K);
+  } else {
+    float* pbw = reinterpret_cast<float*>(ws + a_bytes);
+    launch_pack_tf32_pair(A, lda, pa, Kp, M, B, ldb, pbw, Kp, N, K);
+    pb = pbw;
+  }
   GemmCall g{};
   g.M = M;
   g.N = N;
@@ -145,12 +155,12 @@ void gemm_nt_bf16a_impl(int64_t M, int64_t N, int64_t K, const uint16_t* A, int6
   gemm_bf16_core(M, N, K, A, lda, true, B, ldb, C, ldc, false, bias, acc, Epi::kStore);
 }
 void gemm_nt_f32_impl(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
-                      float* C, int64_t ldc, const float* bias, bool acc) {
+                      float* C, int64_t ldc, const float* bias, bool acc, bool b_constant) {
   if (M <= 0 || N <= 0) return;  // no-op before any check, as backend_cuda.cu:455/:464
   check_gemm_args("gemm_nt_f32", M, N, K, A, lda, B, ldb, C, ldc);
   if (K == 0) return launch_bias_fill(C, ldc, M, N, bias, acc);
   if (skinny_ok(M, K)) return launch_gemm_skinny(M, N, K, A, lda, B, ldb, false, C, ldc, bias, acc);
-  gemm_f32_core(M, N, K, A, lda, B, ldb, C, ldc, bias, acc);
+  gemm_f32_core(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, b_constant);
 }
 void gemm_tf32_direct(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                       float* C, int64_t ldc, const float* bias, bool acc) {
@@ -247,13 +257,20 @@ void conv2d_impl(const float* x, int64_t N, int64_t Cin, int64_t H, int64_t W, c
   if (stride == 1 && g_conv_implicit) {
     // Implicit GEMM: the input repacked once to NHWC, no im2col matrix.
     const int64_t cp = round_up(Cin, 4), cq = round_up(Cin, 32), taps = kh * kw;
+    const bool cache_w = operand_cache_on();  // conv2d_impl serves only the C-ABI conv2d: w is the caller's
     const size_t xb = align256((size_t)(N * H * W * cp) * 4);
-    const size_t wb = align256((size_t)(Cout * taps * cq) * 4);
+    const size_t wb = cache_w ? 0 : align256((size_t)(Cout * taps * cq) * 4);
     uint8_t* ws = static_cast<uint8_t*>(workspace(xb + wb));
     float* xh = reinterpret_cast<float*>(ws);
-    float* wp = reinterpret_cast<float*>(ws + xb);
+    const float* wp;
+    if (cache_w) {
+      wp = cached_conv_weight(w, Cout, Cin, taps, cq);  // the weights, packed once
+    } else {
+      float* wpw = reinterpret_cast<float*>(ws + xb);
+      launch_conv_pack_w(w, wpw, Cout, Cin, taps, cq);
+      wp = wpw;
+    }
     launch_conv_pack_x(x, xh, N, Cin, H * W, cp);
-    launch_conv_pack_w(w, wp, Cout, Cin, taps, cq);
     launch_conv_tc(xh, N, Cin, cp, H, W, wp, cq, Cout, (int)kh, (int)kw, pad, bias, nullptr, out, Ho, Wo);
     return;
   }
@@ -329,7 +346,7 @@ int sdb200_set_attention_path(int path) {
 
 int sdb200_gemm_nt_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                        float* C, int64_t ldc, const float* bias, int accumulate) {
-  SDB_GUARD(gemm_nt_f32_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
+  SDB_GUARD(gemm_nt_f32_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0, /*b_constant=*/true))
 }
 int sdb200_gemm_nt_bf16(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const uint16_t* B,
                         int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
@@ -339,6 +356,16 @@ int sdb200_gemm_nt_bf16a(int64_t M, int64_t N, int64_t K, const uint16_t* A, int
                          int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate) {
   SDB_GUARD(gemm_nt_bf16a_impl(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate != 0))
 }
+int sdb200_set_operand_cache(int enable) { SDB_GUARD(operand_cache_enable(enable != 0)) }
+
+int64_t sdb200_operand_cache_entries(void) {
+  try {
+    return operand_cache_entries();
+  } catch (...) {
+    return -1;
+  }
+}
+
 int sdb200_pack_bf16(const float* src, int64_t ld, uint16_t* dst, int64_t ldo, int64_t rows, int64_t cols) {
   SDB_GUARD({
     require(rows >= 0 && cols >= 0, "pack_bf16", "rows and cols must be >= 0");

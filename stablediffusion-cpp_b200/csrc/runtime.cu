@@ -262,17 +262,19 @@ void pool_free(void* p) {
   if (!p) return;
   const int dev = ctx().device;
   Pool& pl = g_pool[dev];
-  std::lock_guard<std::mutex> lk(pl.m);
+  std::unique_lock<std::mutex> lk(pl.m);
   auto it = pl.live.find(p);
   if (it == pl.live.end()) fail(kErrInvalidArg, "free: pointer not allocated by this library on the current device");
   const size_t cls = it->second;
   pl.live.erase(it);
   if (pl.idle_bytes + cls > kMaxIdle) {
     check_cuda(cudaFree(p), "cudaFree");
-    return;
+  } else {
+    pl.idle[cls].push_back(p);
+    pl.idle_bytes += cls;
   }
-  pl.idle[cls].push_back(p);
-  pl.idle_bytes += cls;
+  lk.unlock();
+  operand_cache_invalidate(p, cls);  // packed copies of this buffer's contents are stale now
 }
 
 }  // namespace sdb
@@ -372,6 +374,7 @@ int sdb200_upload(void* dst, const void* src, size_t bytes) {
   SDB_GUARD({
     if (bytes == 0) return kOk;
     if (!dst || !src) fail(kErrInvalidArg, "upload: null pointer");
+    operand_cache_invalidate(dst, bytes);
     check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx().stream), "upload");
   })
 }
@@ -389,6 +392,7 @@ int sdb200_copy(void* dst, const void* src, size_t bytes) {
   SDB_GUARD({
     if (bytes == 0) return kOk;
     if (!dst || !src) fail(kErrInvalidArg, "copy: null pointer");
+    operand_cache_invalidate(dst, bytes);
     check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx().stream), "copy");
   })
 }
@@ -397,6 +401,7 @@ int sdb200_zero(void* dst, size_t bytes) {
   SDB_GUARD({
     if (bytes == 0) return kOk;
     if (!dst) fail(kErrInvalidArg, "zero: null pointer");
+    operand_cache_invalidate(dst, bytes);
     check_cuda(cudaMemsetAsync(dst, 0, bytes, ctx().stream), "zero");
   })
 }

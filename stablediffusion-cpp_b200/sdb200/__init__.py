@@ -70,6 +70,8 @@ _SIGS = {
     "sdb200_gemm_nt_bf16_noalloc": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16a": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_pack_bf16": ([_v, _i64, _v, _i64, _i64, _i64], _i),
+    "sdb200_set_operand_cache": ([_i], _i),
+    "sdb200_operand_cache_entries": ([], _i64),
     "sdb200_gemm_bf16_epilogue": ([_i64, _i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i, _v, _i], _i),
     "sdb200_set_attention_path": ([_i], _i),
     "sdb200_attention_f16": ([_v, _v, _v, _v, _i, _i64, _i64, _i64, _i, _i, _i64, _i64, _i], _i),
