@@ -76,6 +76,7 @@ struct GemmParams {
   // C + s * split_stride (no bias or residual; a reduction kernel adds them).
   int splits, base_tiles, kb_split;
   long long split_stride;
+  int bias_vec;   // bias is 16-byte aligned: float4 loads in the epilogue
 };
 
 // Work item t -> tile index and K-block range.
@@ -118,18 +119,24 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   nb = r / gs;
 }
 
-// silu(g) = g * 1 / (1 + 2^(-g log2 e)) on the MUFU pipe: ex2.approx and rcp.approx, each
-// within 2 ulp of the exact fp32 value (PTX ISA), so the SwiGLU product differs from the
-// reference's g / (1 + expf(-g)) (tensor.cpp:732-748) by a few fp32 ulp, below the bf16
-// rounding of the output. g -> -inf gives 2^+inf = inf, rcp(inf) = 0 and a (-)0 result,
-// as the exact form does. Against the IEEE division and full expf this takes about 3%
-// off the w1/w3 GEMM of the DiT block at the power cap (the epilogue's instructions
-// share the SM's power budget with the tensor core).
-__device__ __forceinline__ float silu_f(float g) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
-  return g * r;
+// silu(g) = g * 1 / (1 + 2^(-g log2 e)) for a pair, on the MUFU pipe (ex2.approx and
+// rcp.approx, each within 2 ulp of the exact fp32 value per the PTX ISA) with packed fp32
+// multiplies and adds around them. The SwiGLU product differs from the reference's
+// g / (1 + expf(-g)) (tensor.cpp:732-748) by a few fp32 ulp, below the bf16 rounding of
+// the output. g -> -inf gives 2^+inf = inf, rcp(inf) = 0 and a (-)0 result, as the exact
+// form does. The epilogue shares the SM sub-partitions with the MMA issuer and the power
+// budget with the tensor core, so its instruction count shows in the GEMM's time: packed,
+// the w1/w3 GEMM launches of the DiT step run about 1% faster than with the same math
+// unpacked.
+__device__ __forceinline__ float2 silu2(float2 g) {
+  const float2 a = fmul2(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  float e0, e1, r0, r1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a.y));
+  const float2 d = fadd2(make_float2(e0, e1), make_float2(1.0f, 1.0f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d.y));
+  return fmul2(g, make_float2(r0, r1));
 }
 __device__ __forceinline__ float gelu_erf_f(float g) { return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f)); }
 
@@ -175,11 +182,39 @@ __device__ __forceinline__ void store_row32(const GemmParams& p, int row, int co
   }
 }
 
+// Adds bias[col0 .. col0 + 31] to v. With p.bias_vec (16-byte aligned bias) by float4
+// loads and packed adds; otherwise per element, masked at N. The sums are the same.
+__device__ __forceinline__ void add_bias32(const GemmParams& p, int col0, float (&v)[32]) {
+  if (!p.bias) return;
+  if (p.bias_vec && col0 + 32 <= p.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+      const float2 x0 = fadd2(make_float2(v[j], v[j + 1]), make_float2(b.x, b.y));
+      const float2 x1 = fadd2(make_float2(v[j + 2], v[j + 3]), make_float2(b.z, b.w));
+      v[j] = x0.x;
+      v[j + 1] = x0.y;
+      v[j + 2] = x1.x;
+      v[j + 3] = x1.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+  }
+}
+
 // Epi::kQkvRope for one row and one 128-column head of the accumulator at TMEM address
 // `hcol` (lane of this thread), head columns [col0, col0 + 128) of the GEMM output.
 // q and k: two passes over TMEM (sum of squares, then normalise, gamma, rotate, store);
-// v: one pass. The rotary pair (2i, 2i+1) maps to (x0 c - x1 s, x1 c + x0 s) with the
-// angle's cos c / sin s stored at both 2i and 2i + 1 of the table row.
+// v: one pass. The rotary pair (x0, x1) = columns (2i, 2i+1) maps to
+// (x0 c - x1 s, x1 c + x0 s). The tables hold cos at both 2i and 2i + 1 (cs) and
+// (-sin, +sin) at (2i, 2i + 1) (sn), so a pair is x * (c, c) + (x1, x0) * (-s, s): one
+// packed multiply and one packed FMA. The normalisation scale rstd * gamma is applied to
+// x first, so the pair costs four packed instructions in all. This epilogue runs beside
+// the MMA issuer on the same SM sub-partitions; against scalar math with per-element
+// gamma loads the packed form takes 2-4% off the fused-QKV GEMM launches of the DiT step
+// (ncu launch times at 32768 and 33792 rows).
 __device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol, int row, bool row_ok, int col0) {
   const QkvRope& q = p.rope;
   const int which = col0 / q.Dq;  // 0 q, 1 k, 2 v
@@ -193,10 +228,7 @@ __device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol
     tmem_wait_ld();
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (p.bias) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + cc * 32 + j);
-    }
+    add_bias32(p, col0 + cc * 32, v);
   };
   auto store32 = [&](int cc, const float (&o)[32]) {
     if (!row_ok) return;
@@ -222,15 +254,19 @@ __device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol
     }
     return;
   }
-  float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float2 ssa = make_float2(0.0f, 0.0f), ssb = make_float2(0.0f, 0.0f);
 #pragma unroll 1
   for (int cc = 0; cc < 4; ++cc) {
     float v[32];
     load(cc, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) ss[j & 3] = fmaf(v[j], v[j], ss[j & 3]);
+    for (int j = 0; j < 32; j += 4) {
+      ssa = ffma2(make_float2(v[j], v[j + 1]), make_float2(v[j], v[j + 1]), ssa);
+      ssb = ffma2(make_float2(v[j + 2], v[j + 3]), make_float2(v[j + 2], v[j + 3]), ssb);
+    }
   }
-  const float rstd = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / 128.0f + q.eps);
+  const float rstd = rsqrtf(((ssa.x + ssa.y) + (ssb.x + ssb.y)) / 128.0f + q.eps);
+  const float2 r2 = make_float2(rstd, rstd);
   const float* gam = which == 0 ? q.gq : q.gk;
   const int s = row_ok ? row % q.S : 0;
   const float* cr = q.cs + (long long)s * 128;
@@ -240,15 +276,28 @@ __device__ __forceinline__ void qkv_rope_head(const GemmParams& p, uint32_t hcol
     float v[32], o[32];
     load(cc, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gam ? v[j] * rstd * __ldg(gam + cc * 32 + j) : v[j] * rstd;
-#pragma unroll
     for (int j = 0; j < 32; j += 4) {
+      float4 g4 = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      if (gam) {
+        if (q.gamma_vec) {
+          g4 = __ldg(reinterpret_cast<const float4*>(gam + cc * 32 + j));
+        } else {
+          g4.x = __ldg(gam + cc * 32 + j);
+          g4.y = __ldg(gam + cc * 32 + j + 1);
+          g4.z = __ldg(gam + cc * 32 + j + 2);
+          g4.w = __ldg(gam + cc * 32 + j + 3);
+        }
+      }
       const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr + cc * 32 + j));
       const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr + cc * 32 + j));
-      o[j] = v[j] * c4.x - v[j + 1] * s4.x;
-      o[j + 1] = v[j + 1] * c4.x + v[j] * s4.x;
-      o[j + 2] = v[j + 2] * c4.z - v[j + 3] * s4.z;
-      o[j + 3] = v[j + 3] * c4.z + v[j + 2] * s4.z;
+      const float2 xa = fmul2(make_float2(v[j], v[j + 1]), fmul2(make_float2(g4.x, g4.y), r2));
+      const float2 xb = fmul2(make_float2(v[j + 2], v[j + 3]), fmul2(make_float2(g4.z, g4.w), r2));
+      const float2 oa = ffma2(make_float2(xa.y, xa.x), make_float2(s4.x, s4.y), fmul2(xa, make_float2(c4.x, c4.y)));
+      const float2 ob = ffma2(make_float2(xb.y, xb.x), make_float2(s4.z, s4.w), fmul2(xb, make_float2(c4.z, c4.w)));
+      o[j] = oa.x;
+      o[j + 1] = oa.y;
+      o[j + 2] = ob.x;
+      o[j + 3] = ob.y;
     }
     store32(cc, o);
   }
@@ -362,16 +411,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, u
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (p.bias) {
-      if (col0 + 32 <= p.N) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + col0 + j);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
-      }
-    }
+    add_bias32(p, col0, v);
     if (p.epi == (int)Epi::kStore) {
       store_row32(p, row, col0, v, (long long)split * p.split_stride);
     } else {
@@ -380,7 +420,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, float* stg, u
       float y[16];
       if (p.epi == (int)Epi::kSwiglu) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) y[j] = silu_f(v[j]) * v[16 + j];
+        for (int j = 0; j < 16; j += 2) {
+          const float2 y2 = fmul2(silu2(make_float2(v[j], v[j + 1])), make_float2(v[16 + j], v[17 + j]));
+          y[j] = y2.x;
+          y[j + 1] = y2.y;
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = v[j] * gelu_erf_f(v[16 + j]);
@@ -1170,6 +1214,7 @@ void launch_gemm_tc(const GemmCall& g) {
   p.C = g.C;
   p.ldc = g.ldc;
   p.bias = g.bias;
+  p.bias_vec = g.bias && (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0;
   p.accumulate = g.accumulate ? 1 : 0;
   p.epi = (int)g.epi;
   p.out_bf16 = g.out_bf16 ? 1 : 0;
@@ -1499,6 +1544,7 @@ void launch_gemm_tc_explicit(const GemmCall& g, int num_sms, cudaStream_t stream
   p.C = g.C;
   p.ldc = g.ldc;
   p.bias = g.bias;
+  p.bias_vec = g.bias && (reinterpret_cast<uintptr_t>(g.bias) & 15) == 0;
   p.accumulate = g.accumulate ? 1 : 0;
   p.epi = (int)g.epi;
   p.out_bf16 = g.out_bf16 ? 1 : 0;

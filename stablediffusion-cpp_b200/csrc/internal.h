@@ -103,12 +103,13 @@ struct QkvRope {
   int Dq;
   const float* gq;  // [128] or null (1)
   const float* gk;  // [128] or null (1)
-  const float* cs;  // [S, 128], each angle at 2i and 2i + 1
-  const float* sn;  // [S, 128]
+  const float* cs;  // [S, 128]: cos of angle i at 2i and 2i + 1
+  const float* sn;  // [S, 128]: -sin of angle i at 2i, +sin at 2i + 1
   float eps;
   void* q16;
   void* k16;
   void* v16;
+  int gamma_vec;    // gq and gk 16-byte aligned (set by gemm_bf16_qkv_rope_impl)
 };
 struct GemmCall {
   int64_t M, N, K;

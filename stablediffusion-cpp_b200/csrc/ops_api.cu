@@ -220,7 +220,9 @@ void gemm_bf16_qkv_rope_impl(int64_t M, int64_t K, const void* A, int64_t lda, b
   require_ptr(A, op, "A");
   require_ptr(B, op, "B");
   require(lda >= K && ldb >= K, op, "leading dimension < K");
-  gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kQkvRope, &r);
+  QkvRope rv = r;
+  rv.gamma_vec = ((reinterpret_cast<uintptr_t>(r.gq) | reinterpret_cast<uintptr_t>(r.gk)) & 15) == 0;
+  gemm_bf16_core(M, N, K, A, lda, a_bf16, B, ldb, nullptr, N, false, bias, false, Epi::kQkvRope, &rv);
 }
 
 // Row-parallel projection of tensor parallelism: X[M, K] times W[N, K]^T (+bias), every

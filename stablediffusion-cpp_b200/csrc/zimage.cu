@@ -330,6 +330,8 @@ class ZImage {
 
   // Rotary tables for (axis0, h, w) positions, interleaved layout (zimage.cpp:71-88):
   // freq = theta^(-2k/d_a) in double, angle = (float)(pos * freq), cos/sin in float.
+  // cs holds cos at both columns of a rotary pair, sn holds (-sin, +sin), the operand
+  // layout of the QKV epilogue's packed rotation (Epi::kQkvRope).
   void rope_tables(const std::vector<std::array<int, 3>>& pos, std::vector<float>& cs, std::vector<float>& sn) const {
     const int64_t S = (int64_t)pos.size(), d = head_dim;
     cs.assign((size_t)(S * d), 0.0f);
@@ -343,7 +345,8 @@ class ZImage {
           const float ang = (float)((double)pos[s][a] * freq);
           const float c = std::cos(ang), si = std::sin(ang);
           cs[s * d + off + 2 * k] = cs[s * d + off + 2 * k + 1] = c;
-          sn[s * d + off + 2 * k] = sn[s * d + off + 2 * k + 1] = si;
+          sn[s * d + off + 2 * k] = -si;
+          sn[s * d + off + 2 * k + 1] = si;
         }
         off += da;
       }
