@@ -151,6 +151,19 @@ int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, in
                               const uint16_t* B, int64_t ldb, void* Y, int64_t ldy, int y_bf16, const float* bias,
                               int epi);
 
+/* Fused-QKV projection (extension; the reference runs these as separate calls for each of
+ * q, k, v: linear, rms_norm_heads, rope, zimage.cpp:113-120): Y = X Wqkv^T (+ bias) with
+ * Wqkv [3 Dq, K] bf16, rows q | k | v, Dq = heads * 128. Then, per 128-wide head of q and
+ * of k, the RMS norm with eps times gamma (gq / gk, [128] each, or null for 1) and the
+ * interleaved rotary embedding of rope(): pair (2i, 2i+1) of row m rotated by
+ * cos[m % S][2i] / sin[m % S][2i] (cos, sin [S, 128]). q, k and v are stored as fp16
+ * [M, Dq] (q16, k16, v16, 16-byte aligned), the attention operand layout of
+ * sdb200_attention_f16 with dp = 128. X is bf16 when x_bf16 != 0, else fp32 (rounded to
+ * bf16 as gemm_nt_bf16 does). */
+int sdb200_gemm_bf16_qkv_rope(int64_t M, int64_t K, const void* X, int64_t ldx, int x_bf16, const uint16_t* Wqkv,
+                              int64_t ldw, const float* bias, int64_t Dq, int64_t S, const float* cos, const float* sin,
+                              const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16);
+
 /* Tuning extension (no reference counterpart): forces the GEMM tile width N (64, 128,
  * 192 or 256) for later calls of this process; 0 restores the automatic choice. */
 int sdb200_set_gemm_tile(int bn);

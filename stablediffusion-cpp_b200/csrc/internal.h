@@ -214,6 +214,8 @@ void op_group_norm(const float*, float*, int64_t, int64_t, int64_t, int, const f
 void op_row_norm(const float*, float*, int64_t, int64_t, const float*, const float*, float, bool);
 void op_rms_norm_heads(float*, int64_t, int64_t, const float*, float);
 void op_rope(float*, int64_t, int64_t, int64_t, int64_t, const float*, const float*, bool);
+// rope() tables (cos / sin [S, 128], interleaved) -> the Epi::kQkvRope layout (QkvRope::cs / sn).
+void op_rope_pair_tables(const float* cos, const float* sin, float* cs, float* sn, int64_t S);
 void op_softmax_rows(float*, int64_t, int64_t, float, bool, int64_t);
 // Softmax rows ld elements apart; causal row index = row0 + r % rows_per_head; with
 // round_out the probabilities are stored rounded to tf32.

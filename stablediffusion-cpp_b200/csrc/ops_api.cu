@@ -386,6 +386,43 @@ int sdb200_gemm_bf16_epilogue(int64_t M, int64_t N, int64_t K, const void* A, in
   SDB_GUARD(gemm_bf16_epilogue_impl(M, N, K, A, lda, a_bf16 != 0, B, ldb, Y, ldy, y_bf16 != 0, bias, epi))
 }
 
+int sdb200_gemm_bf16_qkv_rope(int64_t M, int64_t K, const void* X, int64_t ldx, int x_bf16, const uint16_t* Wqkv,
+                              int64_t ldw, const float* bias, int64_t Dq, int64_t S, const float* cos, const float* sin,
+                              const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16) {
+  SDB_GUARD({
+    const char* op = "gemm_bf16_qkv_rope";
+    require(M >= 0 && K > 0 && Dq > 0 && S > 0, op, "bad shape");
+    require(Dq % 128 == 0 && Dq <= ((int64_t)1 << 30), op, "Dq must be a multiple of 128 (heads of 128)");
+    require(S <= ((int64_t)1 << 30), op, "S too large");
+    require_ptr(cos, op, "cos");
+    require_ptr(sin, op, "sin");
+    if (M == 0) return kOk;
+    // The epilogue reads the tables as cos at both columns of a rotary pair and
+    // (-sin, +sin); they are rebuilt from rope()'s layout for this call.
+    float* t = static_cast<float*>(pool_malloc((size_t)(2 * S * 128) * sizeof(float)));
+    try {
+      op_rope_pair_tables(cos, sin, t, t + S * 128, S);
+      QkvRope r{};
+      r.S = (int)S;
+      r.Dq = (int)Dq;
+      r.gq = gq;
+      r.gk = gk;
+      r.cs = t;
+      r.sn = t + S * 128;
+      r.eps = eps;
+      r.q16 = q16;
+      r.k16 = k16;
+      r.v16 = v16;
+      gemm_bf16_qkv_rope_impl(M, K, X, ldx, x_bf16 != 0, Wqkv, ldw, bias, r);
+    } catch (...) {
+      pool_free(t);
+      throw;
+    }
+    // Stream-ordered: the next user of this block is issued on the same stream.
+    pool_free(t);
+  })
+}
+
 int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                      int heads, int kv_heads, int64_t d, int causal) {
   SDB_GUARD({

@@ -227,6 +227,27 @@ __device__ __forceinline__ void rotate(float& u, float& w, float ca, float sa, f
   u = nu;
   w = nw;
 }
+// Rotary tables of rope() (cos / sin [S, 128], interleaved: pair i of row s uses column
+// 2i) -> the operand layout of the fused QKV epilogue (Epi::kQkvRope): cs holds cos at
+// 2i and 2i + 1, sn holds (-sin, +sin). One unit is one pair.
+struct OpRopePairTables {
+  const float* cos;
+  const float* sin;
+  float* cs;
+  float* sn;
+  __device__ void one(int64_t u) const {
+    const int64_t o = 2 * u;  // row s * 128 + column 2i
+    const float c = cos[o], sv = sin[o];
+    cs[o] = c;
+    cs[o + 1] = c;
+    sn[o] = -sv;
+    sn[o + 1] = sv;
+  }
+  __device__ void four(int64_t j) const {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) one(4 * j + q);
+  }
+};
 struct OpRope {
   float* x;
   const float* cs;
@@ -455,6 +476,9 @@ void op_rope(float* x, int64_t N, int64_t S, int64_t inner, int64_t dim, const f
   const int64_t pairs = N * S * (inner / dim) * (dim / 2);
   const bool vec = (dim / 2) % 4 == 0 && inner % 4 == 0 && al16(x) && al16(cs) && al16(sn);
   run_pointwise(OpRope{x, cs, sn, S, inner, dim, interleaved ? 1 : 0}, pairs, vec, "rope");
+}
+void op_rope_pair_tables(const float* cos, const float* sin, float* cs, float* sn, int64_t S) {
+  run_pointwise(OpRopePairTables{cos, sin, cs, sn}, S * 64, 1, "rope_pair_tables");
 }
 void op_upsample2x(const float* x, float* y, int64_t NC, int64_t H, int64_t W) {
   run_pointwise(OpUpsample2x{x, y, W}, NC * H * W, W % 4 == 0 && al16(x) && al16(y), "upsample_nearest2x");

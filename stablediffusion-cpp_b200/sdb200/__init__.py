@@ -73,6 +73,8 @@ _SIGS = {
     "sdb200_set_operand_cache": ([_i], _i),
     "sdb200_operand_cache_entries": ([], _i64),
     "sdb200_gemm_bf16_epilogue": ([_i64, _i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i, _v, _i], _i),
+    "sdb200_gemm_bf16_qkv_rope": ([_i64, _i64, _v, _i64, _i, _v, _i64, _v, _i64, _i64, _v, _v, _v, _v, _f, _v, _v, _v],
+                                  _i),
     "sdb200_set_attention_path": ([_i], _i),
     "sdb200_attention_f16": ([_v, _v, _v, _v, _i, _i64, _i64, _i64, _i, _i, _i64, _i64, _i], _i),
     "sdb200_pack_heads_f16": ([_v, _v, _i64, _i, _i64, _i64], _i),

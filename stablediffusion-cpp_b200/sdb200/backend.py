@@ -99,6 +99,25 @@ def gemm_bf16_epilogue(A, B, bias=None, epi=0, y_bf16=False, Y=None):
     return Y
 
 
+def gemm_bf16_qkv_rope(X, Wqkv, cos, sin, gq=None, gk=None, bias=None, eps=1e-5):
+    """Fused-QKV projection: X [M, K] (fp32 or bf16) times Wqkv [3 Dq, K] (bf16, rows
+    q | k | v) (+bias), then the per-head RMS norm (gq / gk) and the interleaved rotary
+    embedding (cos / sin [S, 128], row m uses m % S) of q and k. Returns fp16 (q, k, v),
+    each [M, Dq]."""
+    x_bf16 = X.dtype == torch.bfloat16
+    _need(Wqkv, torch.bfloat16, "Wqkv")
+    _need(cos, torch.float32, "cos")
+    _need(sin, torch.float32, "sin")
+    M, K = X.shape
+    Dq = Wqkv.shape[0] // 3
+    S = cos.shape[0]
+    q, k, v = (torch.empty((M, Dq), device=X.device, dtype=torch.float16) for _ in range(3))
+    bind_stream()
+    check(lib().sdb200_gemm_bf16_qkv_rope(M, K, _p(X), X.stride(0), int(x_bf16), _p(Wqkv), Wqkv.stride(0), _p(bias),
+                                          Dq, S, _p(cos), _p(sin), _p(gq), _p(gk), eps, _p(q), _p(k), _p(v)))
+    return q, k, v
+
+
 def interleave_gated(first, second, block=16):
     """Interleaves the rows of two [D, K] weights in blocks of `block`:
     rows [2jb, 2jb+b) from `first`, [2jb+b, 2jb+2b) from `second`. For SwiGLU

@@ -316,3 +316,67 @@ def test_gemv_small_m(sdb, orc, M, N, K, pad, f32):
         want = orc.gemm_nt_bf16(A, Wh, bias, C0, M, N, K, ldb=K + pad)
         be.gemm_nt_bf16(_t(A), _bf16_t(Wh), _t(bias), C, True, M=M, N=N, K=K, ldb=K + pad)
     assert rel_fro(_np(C), want) <= TOL_EXACT
+
+
+def _qkv_rope_oracle(orc, X, Wh, bias, Dq, cos, sin, gq, gk, eps, rows):
+    """The reference's sequence for the fused projection (zimage.cpp:113-120): linear,
+    rms_norm_heads, then rope() with the interleaved pairs, on the given rows only (row m
+    at position m % S)."""
+    y = orc.gemm_nt_bf16(np.ascontiguousarray(X[rows]), Wh, bias)
+    pos = rows % cos.shape[0]
+    out = []
+    for part, g in ((0, gq), (1, gk)):
+        x = orc.rms_norm_heads(y[:, part * Dq:(part + 1) * Dq], 128, g, eps)
+        out.append(orc.rope(x[None], 128, cos[pos], sin[pos], True)[0])
+    out.append(y[:, 2 * Dq:])
+    return out
+
+
+@pytest.mark.parametrize("case", ["bf16_x", "f32_x", "unaligned_gamma", "zimage_1024"])
+def test_fused_qkv_rope_epilogue(sdb, orc, case):
+    """sdb200_gemm_bf16_qkv_rope (the DiT's QKV projection with QK-norm, RoPE and the fp16
+    attention-operand pack in the GEMM epilogue) against the reference's separate linear,
+    rms_norm_heads and rope on the CPU oracle. With bf16 X both sides use the same operand
+    values, so the gate is the fp16 rounding of the outputs (1e-3); with fp32 X the GEMM
+    gate applies (2e-3) plus the fp16 rounding. Covers ragged M, rows wrapping the rotary
+    table (S < M), bias, absent and unaligned gammas, and the Z-Image width at 1024^2
+    (30 heads, 4224 tokens, sampled rows)."""
+    import torch
+
+    from sdb200.workloads import f32_to_bf16_bits
+
+    rng = np.random.default_rng({"bf16_x": 1, "f32_x": 2, "unaligned_gamma": 3, "zimage_1024": 4}[case])
+    if case == "zimage_1024":
+        M, K, Dq, S = 4224, 3840, 3840, 4224
+    else:
+        M, K, Dq, S = 300, 256, 256, 150
+    eps = 1e-5
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    if case != "f32_x":
+        X = f32_to_bf16_bits(X).astype(np.uint32) << 16
+        X = X.view(np.float32)
+    Wh = f32_to_bf16_bits((0.02 * rng.standard_normal((3 * Dq, K))).astype(np.float32))
+    bias = (0.05 * rng.standard_normal(3 * Dq)).astype(np.float32)
+    ang = rng.uniform(0.0, 40.0, (S, 64))
+    cos = np.repeat(np.cos(ang), 2, axis=1).astype(np.float32)
+    sin = np.repeat(np.sin(ang), 2, axis=1).astype(np.float32)
+    gq = (1.0 + 0.3 * rng.standard_normal(128)).astype(np.float32)
+    gk = (1.0 + 0.3 * rng.standard_normal(128)).astype(np.float32)
+    if case == "f32_x":
+        gq = gk = None
+    Xd = _t(X) if case == "f32_x" else _t(X).to(torch.bfloat16)
+    if case == "unaligned_gamma":
+        buf = _t(np.concatenate([[0.0], gq, gk]).astype(np.float32))
+        gqd, gkd = buf[1:129], buf[129:257]  # 4-byte aligned only: the per-element gamma loads
+    else:
+        gqd = None if gq is None else _t(gq)
+        gkd = None if gk is None else _t(gk)
+    q, k, v = sdb.backend.gemm_bf16_qkv_rope(Xd, _bf16_t(Wh), _t(cos), _t(sin), gqd, gkd, _t(bias), eps)
+    rows = np.arange(M) if M <= 1024 else np.sort(np.random.default_rng(9).choice(M, 64, replace=False))
+    want = _qkv_rope_oracle(orc, X, Wh, bias, Dq, cos, sin, gq, gk, eps, rows)
+    tol = 1e-3 if case != "f32_x" else TOL_BF16 + 1e-3
+    for name, got, w in zip("qkv", (q, k, v), want):
+        g = _np(got).astype(np.float32)[rows]
+        assert np.isfinite(g).all(), name
+        assert rel_fro(g, w) <= tol, (case, name, rel_fro(g, w))
+    assert sdb.backend.device_error_word() == 0
