@@ -380,3 +380,29 @@ def test_fused_qkv_rope_epilogue(sdb, orc, case):
         assert np.isfinite(g).all(), name
         assert rel_fro(g, w) <= tol, (case, name, rel_fro(g, w))
     assert sdb.backend.device_error_word() == 0
+
+
+@pytest.mark.parametrize("epi,y_bf16", [(0, False), (0, True), (1, True)])
+def test_epilogue_bias_alignment_paths(sdb, epi, y_bf16):
+    """The epilogue adds the bias with float4 loads when it is 16-byte aligned and per
+    element otherwise; both add the same values in the same order, so the outputs must be
+    bit-identical. The ragged N (not a multiple of 32 output columns for epi 0) also covers
+    the masked tail chunk."""
+    import torch
+
+    from sdb200.workloads import f32_to_bf16_bits
+
+    rng = np.random.default_rng(31 + epi)
+    M, K = 260, 192
+    N = 1000 if epi == 0 else 1024
+    A = _t(rng.standard_normal((M, K)).astype(np.float32))
+    W = _bf16_t(f32_to_bf16_bits((0.05 * rng.standard_normal((N, K))).astype(np.float32)))
+    b = rng.standard_normal(N).astype(np.float32)
+    aligned = _t(b)
+    buf = _t(np.concatenate([[0.0], b]).astype(np.float32))
+    unaligned = buf[1:]
+    assert unaligned.data_ptr() % 16 != 0
+    y0 = sdb.backend.gemm_bf16_epilogue(A, W, aligned, epi=epi, y_bf16=y_bf16)
+    y1 = sdb.backend.gemm_bf16_epilogue(A, W, unaligned, epi=epi, y_bf16=y_bf16)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
