@@ -159,10 +159,14 @@ template <int W>
 __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
     const float* __restrict__ slots, long long slot_rows, long long row0, float* __restrict__ x, int D,
     const float* __restrict__ gamma2, const float* __restrict__ g, const float* __restrict__ gamma_n,
-    const float* __restrict__ scale_n, BcastDst hd, float eps) {
+    const float* __restrict__ scale_n, BcastDst hd, float eps, long long rows, int rpb) {
   __shared__ float red[32];
-  const long long lr = blockIdx.x, row = row0 + lr;
   const int D4 = D >> 2;
+  // rpb consecutive rows per block: with peers to write (W > 1) one system-scope fence then
+  // covers rpb rows instead of one.
+  const long long r_end = min(rows, ((long long)blockIdx.x + 1) * rpb);
+  for (long long lr = (long long)blockIdx.x * rpb; lr < r_end; ++lr) {
+  const long long row = row0 + lr;
   const float4* src = reinterpret_cast<const float4*>(slots + lr * D);
   const long long sstride4 = (slot_rows * D) >> 2;
   float4* y = reinterpret_cast<float4*>(x + row * D);
@@ -212,7 +216,7 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
       ss2 += xn.x * xn.x + xn.y * xn.y + xn.z * xn.z + xn.w * xn.w;
     }
   }
-  if (hd.n == 0) return;
+  if (hd.n == 0) continue;
   const float rstd2 = rsqrtf(block_sum256(ss2, red) / (float)D + eps);
   const float4* gn = reinterpret_cast<const float4*>(gamma_n);
   const float4* sc = reinterpret_cast<const float4*>(scale_n);
@@ -232,6 +236,7 @@ __global__ void __launch_bounds__(kRowThreads) k_post_norm_mod_bcast_v4(
 #pragma unroll
       for (int q = 0; q < W; ++q) *reinterpret_cast<uint2*>(hd.p[q] + row * D + 4 * i4) = w;
     }
+  }
   }
   // Stores into peers' memory are visible system-wide before this kernel completes (with
   // one rank every destination is local and kernel completion orders the stores).
@@ -361,6 +366,10 @@ void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, i
   hd.n = nh;
   for (int q = 0; q < nh; ++q) hd.p[q] = hdst[q];
   const dim3 grid((unsigned)rows);
+  // Rows per block of the register-resident form: 4 when peers are written (one fence per
+  // block), else 1.
+  const int rpb = (world > 1 && nh > 0) ? 4 : 1;
+  const dim3 grid4((unsigned)((rows + rpb - 1) / rpb));
   const size_t sm = (size_t)D * 4;
   cudaStream_t st = ctx().stream;
   // The register-resident form needs 16-byte rows and vectors (all cudaMalloc'd / pool).
@@ -374,8 +383,8 @@ void dit_post_norm_mod_bcast(const float* slots, int64_t slot_rows, int world, i
 #define SDB_PNMB(W)                                                                                             \
   case W:                                                                                                       \
     if (v4 && hd_ok)                                                                                            \
-      k_post_norm_mod_bcast_v4<W><<<grid, kRowThreads, 0, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n, \
-                                                                scale_n, hd, eps);                              \
+      k_post_norm_mod_bcast_v4<W><<<grid4, kRowThreads, 0, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n, \
+                                                                 scale_n, hd, eps, rows, rpb);                  \
     else                                                                                                        \
       k_post_norm_mod_bcast<W><<<grid, kRowThreads, sm, st>>>(slots, slot_rows, row0, x, D, gamma2, g, gamma_n,   \
                                                              scale_n, hd, eps);                                 \
