@@ -182,13 +182,15 @@ int sdb200_set_conv_implicit(int enable);
  * out [N, Sq, heads*d]; softmax(q k^T / sqrt(d)) v per head, query head h reads kv
  * head h / (heads / kv_heads); causal keeps keys j <= query row i. Head dims <= 128 run
  * on the flash kernel (fp16 operands), larger ones as tf32 GEMM -> softmax -> tf32 GEMM
- * in query-row chunks (the reference GPU backend's scheme on tensor cores). */
+ * in query-row chunks (the reference GPU backend's scheme on tensor cores). Skv = 0 gives
+ * a zero output (the reference's empty score matrix times V); N = 0 or Sq = 0 does nothing. */
 int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                      int heads, int kv_heads, int64_t d, int causal);
 
 /* Extension of backend_cuda.h:58-59 for producers that already emit fp16 operands:
  * q [N, Sq, heads, dp], k/v [N, Skv, kv_heads, dp] fp16 (dp = 64 for d <= 64, else 128,
- * zero padded beyond d); out [N, Sq, heads*d] fp32, or bf16 when out_bf16 != 0. */
+ * zero padded beyond d); out [N, Sq, heads*d] fp32, or bf16 when out_bf16 != 0. Skv = 0
+ * gives a zero output. */
 int sdb200_attention_f16(const void* q, const void* k, const void* v, void* out, int out_bf16, int64_t N, int64_t Sq,
                          int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp, int causal);
 /* fp32 x [rows, heads*d] -> fp16 y [rows, heads, dp] (zero padded, |x| > 65504 saturates). */

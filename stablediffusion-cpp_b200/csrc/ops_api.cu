@@ -430,11 +430,17 @@ int sdb200_attention(const float* q, const float* k, const float* v, float* out,
     require(N >= 0 && Sq >= 0 && Skv >= 0 && d > 0, op, "bad shape");
     require(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, op, "heads must be a multiple of kv_heads");
     if (N == 0 || Sq == 0) return kOk;
-    require(Skv > 0, op, "Skv == 0");
+    require_ptr(out, op, "out");
+    if (Skv == 0) {
+      // No keys: the reference's score matrix is empty and its P V product a K = 0 GEMM
+      // that leaves zeros (tensor.cpp:354-394, :776-810), so out is zero.
+      check_cuda(cudaMemsetAsync(out, 0, (size_t)(N * Sq * heads * d) * sizeof(float), ctx().stream),
+                 "cudaMemsetAsync(attention)");
+      return kOk;
+    }
     require_ptr(q, op, "q");
     require_ptr(k, op, "k");
     require_ptr(v, op, "v");
-    require_ptr(out, op, "out");
     launch_attention(q, k, v, out, N, Sq, Skv, heads, kv_heads, d, causal != 0);
   })
 }
@@ -443,15 +449,21 @@ int sdb200_attention_f16(const void* q, const void* k, const void* v, void* out,
                          int64_t Skv, int heads, int kv_heads, int64_t d, int64_t dp, int causal) {
   SDB_GUARD({
     const char* op = "attention_f16";
-    require(N >= 0 && Sq >= 0 && Skv > 0 && d > 0, op, "bad shape");
+    require(N >= 0 && Sq >= 0 && Skv >= 0 && d > 0, op, "bad shape");
     require(heads > 0 && kv_heads > 0 && heads % kv_heads == 0, op, "heads must be a multiple of kv_heads");
     require((dp == 64 && d <= 64) || (dp == 128 && d <= 128), op, "dp must be 64 (d <= 64) or 128 (d <= 128)");
+    require_ptr(out, op, "out");
+    if (N == 0 || Sq == 0) return kOk;
+    if (Skv == 0) {  // no keys: zero output, as sdb200_attention
+      const size_t esz = out_bf16 ? 2 : 4;
+      check_cuda(cudaMemsetAsync(out, 0, (size_t)(N * Sq * heads * d) * esz, ctx().stream),
+                 "cudaMemsetAsync(attention_f16)");
+      return kOk;
+    }
     require_ptr(q, op, "q");
     require_ptr(k, op, "k");
     require_ptr(v, op, "v");
-    require_ptr(out, op, "out");
     require(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16 == 0, op, "q/k/v must be 16-byte aligned");
-    if (N == 0 || Sq == 0) return kOk;
     launch_attention_f16(q, k, v, out, (long long)heads * d, (long long)Sq * heads * d, out_bf16 != 0, N, Sq, Skv,
                          heads, kv_heads, d, dp, causal != 0);
   })

@@ -61,6 +61,45 @@ def test_golden_attention_tensor_cores(sdb, attention_path):
         assert rel_fro(_np(o), g["out"]) <= 2e-3, f
 
 
+@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("d", [40, 128, 160])
+def test_attention_no_keys_is_zero(sdb, orc, attention_path, path, d):
+    """Skv = 0: the reference's score matrix is empty and its P V product a K = 0 GEMM, so
+    the output is zero (the oracle agrees). Every path (flash kernel, wide-head GEMM form,
+    exact kernel) writes zeros over whatever the buffer held; N = 0 and Sq = 0 are no-ops."""
+    import torch
+
+    attention_path(path)
+    L = sdb.lib()
+    N, Sq, H, KVH = 2, 37, 4, 2
+    q = torch.randn((N, Sq, H * d), device="cuda")
+    k = torch.empty((N, 0, KVH * d), device="cuda")
+    out = torch.full((N, Sq, H * d), float("nan"), device="cuda")
+    sdb.backend.bind_stream()
+    for causal in (0, 1):
+        out.fill_(float("nan"))
+        sdb.check(L.sdb200_attention(q.data_ptr(), k.data_ptr(), k.data_ptr(), out.data_ptr(), N, Sq, 0, H, KVH, d,
+                                     causal))
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(out).item() == 0
+    want = orc.attention(_np(q), np.zeros((N, 0, KVH * d), np.float32), np.zeros((N, 0, KVH * d), np.float32), H,
+                         KVH, False)
+    assert np.array_equal(_np(out), want)
+    out.fill_(7.0)
+    sdb.check(L.sdb200_attention(q.data_ptr(), k.data_ptr(), k.data_ptr(), out.data_ptr(), 0, Sq, 5, H, KVH, d, 0))
+    sdb.check(L.sdb200_attention(q.data_ptr(), k.data_ptr(), k.data_ptr(), out.data_ptr(), N, 0, 5, H, KVH, d, 0))
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
+    if d <= 128:  # the fp16-operand entry point
+        dp = 64 if d <= 64 else 128
+        for bf16 in (0, 1):
+            o = torch.full((N * Sq * H * d,), -1, dtype=torch.int16 if bf16 else torch.int32, device="cuda")
+            sdb.check(L.sdb200_attention_f16(q.data_ptr(), k.data_ptr(), k.data_ptr(), o.data_ptr(), bf16, N, Sq, 0, H,
+                                             KVH, d, dp, 0))
+            torch.cuda.synchronize()
+            assert torch.count_nonzero(o).item() == 0
+
+
 @pytest.mark.parametrize("N,Sq,Skv,H,KVH,d,causal", [
     (1, 4224, 4224, 4, 4, 128, False),   # Z-Image joint sequence at 1024^2 (4 of 30 heads)
     (1, 640, 640, 30, 30, 128, False),   # all 30 heads, shorter sequence
