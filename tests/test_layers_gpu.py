@@ -444,3 +444,43 @@ def test_elementwise_and_layout(sdb):
     back = torch.empty_like(lt)
     sdb.check(L.sdb200_unpatchify(tok.data_ptr(), back.data_ptr(), 16, 6, 8, 2))
     assert np.array_equal(_np(back), lat)
+
+
+def test_empty_shapes_are_no_ops(sdb):
+    """Zero-size problems through the C ABI return SDB200_OK and touch nothing, as the
+    reference's CPU loops do (its GPU backend would launch an empty grid): GEMMs with M or N
+    zero, convolution with no images, norms, softmax, RoPE and the value-wise and layout ops
+    with no rows or elements."""
+    import torch
+
+    L = sdb.lib()
+    buf = torch.full((4096,), 5.0, device="cuda")
+    w16 = torch.zeros((4096,), dtype=torch.int16, device="cuda")
+    p, h = buf.data_ptr(), w16.data_ptr()
+    calls = [
+        lambda: L.sdb200_gemm_nt_f32(0, 64, 32, p, 32, p, 32, p, 64, None, 0),
+        lambda: L.sdb200_gemm_nt_f32(64, 0, 32, p, 32, p, 32, p, 1, None, 0),
+        lambda: L.sdb200_gemm_nt_bf16(0, 64, 32, p, 32, h, 32, p, 64, None, 0),
+        lambda: L.sdb200_gemm_nt_bf16(16, 0, 32, p, 32, h, 32, p, 1, None, 0),
+        lambda: L.sdb200_conv2d(p, 0, 4, 8, 8, p, 4, 3, 3, None, 1, 1, p, 8, 8),
+        lambda: L.sdb200_group_norm(p, p, 0, 32, 64, 32, p, p, 1e-6),
+        lambda: L.sdb200_layer_norm(p, p, 0, 64, p, p, 1e-5),
+        lambda: L.sdb200_rms_norm(p, p, 0, 64, p, 1e-5),
+        lambda: L.sdb200_rms_norm_heads(p, 0, 64, p, 1e-5),
+        lambda: L.sdb200_softmax_rows(p, 0, 64, 1.0, 0),
+        lambda: L.sdb200_rope(p, 0, 8, 64, 64, p, p, 1),
+        lambda: L.sdb200_geglu(p, p, 0, 32),
+        lambda: L.sdb200_swiglu(p, p, p, 0),
+        lambda: L.sdb200_silu(p, 0),
+        lambda: L.sdb200_add(p, p, 0),
+        lambda: L.sdb200_mul_rows(p, p, 0, 64),
+        lambda: L.sdb200_add_channel_bias(p, p, 0, 4, 64),
+        lambda: L.sdb200_upsample_nearest2x(p, p, 0, 8, 8),
+        lambda: L.sdb200_nchw_to_nlc(p, p, 0, 4, 64),
+    ]
+    for i, call in enumerate(calls):
+        rc = call()
+        assert rc == sdb.OK, (i, rc, L.sdb200_last_error())
+    torch.cuda.synchronize()
+    assert bool((buf == 5.0).all())
+    assert sdb.backend.device_error_word() == 0
