@@ -406,3 +406,29 @@ def test_epilogue_bias_alignment_paths(sdb, epi, y_bf16):
     y1 = sdb.backend.gemm_bf16_epilogue(A, W, unaligned, epi=epi, y_bf16=y_bf16)
     torch.cuda.synchronize()
     assert torch.equal(y0, y1)
+
+
+def test_gemm_output_beyond_2g_elements(sdb, orc):
+    """An output of more than 2^31 elements (65541 x 33000 fp32, 8.65 GB): every store
+    offset past 2^31 must be formed in 64 bits. Sampled rows, the last ones included, are
+    checked against the oracle at the GEMM gate."""
+    import torch
+
+    from sdb200.workloads import f32_to_bf16_bits
+
+    M, N, K = 65541, 33000, 64
+    if torch.cuda.mem_get_info()[0] < 12 * (1 << 30):
+        pytest.skip("needs 12 GB of free device memory")
+    rng = np.random.default_rng(77)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    Wh = f32_to_bf16_bits((0.05 * rng.standard_normal((N, K))).astype(np.float32))
+    bias = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    C = torch.empty((M, N), device="cuda")
+    sdb.backend.gemm_nt_bf16(_t(A), _bf16_t(Wh), _t(bias), C=C, M=M, N=N, K=K, lda=K, ldb=K, ldc=N)
+    rows = np.concatenate([np.sort(rng.choice(M - 8, 24, replace=False)), np.arange(M - 8, M)])
+    got = _np(C[torch.from_numpy(rows).cuda()])
+    del C
+    torch.cuda.empty_cache()
+    want = orc.gemm_nt_bf16(np.ascontiguousarray(A[rows]), Wh, bias)
+    assert np.isfinite(got).all()
+    assert rel_fro(got, want) <= TOL_BF16

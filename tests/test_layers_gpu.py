@@ -484,3 +484,32 @@ def test_empty_shapes_are_no_ops(sdb):
     torch.cuda.synchronize()
     assert bool((buf == 5.0).all())
     assert sdb.backend.device_error_word() == 0
+
+
+def test_attention_output_beyond_2g_elements(sdb, orc, attention_path):
+    """More than 2^31 output elements: 520 samples of the 1024^2 joint sequence (4224 tokens)
+    with 8 heads of 128, 2.25 G elements (9 GB fp32) per tensor, so the last samples' offsets
+    need 64 bits. Two heads of the first and the last sample are checked against the oracle
+    at the contraction gate."""
+    import torch
+
+    attention_path(0)
+    N, S, H, d = 520, 4224, 8, 128
+    if torch.cuda.mem_get_info()[0] < 48 * (1 << 30):
+        pytest.skip("needs 48 GB of free device memory")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    q = torch.randn((N, S, H * d), generator=g, device="cuda")
+    k = torch.randn((N, S, H * d), generator=g, device="cuda")
+    v = torch.randn((N, S, H * d), generator=g, device="cuda")
+    out = sdb.backend.attention(q, k, v, H, False, H)
+    torch.cuda.synchronize()
+    assert N * S * H * d > 2 ** 31
+    for n in (0, N - 1):
+        qs, ks, vs = (_np(t[n:n + 1, :, :2 * d]) for t in (q, k, v))  # heads 0 and 1
+        want = orc.attention(qs, ks, vs, 2, 2, False)
+        got = _np(out[n:n + 1, :, :2 * d])
+        assert np.isfinite(got).all()
+        assert rel_fro(got, want) <= 2e-3, n
+    del q, k, v, out
+    torch.cuda.empty_cache()
