@@ -164,6 +164,17 @@ int sdb200_gemm_bf16_qkv_rope(int64_t M, int64_t K, const void* X, int64_t ldx, 
                               int64_t ldw, const float* bias, int64_t Dq, int64_t S, const float* cos, const float* sin,
                               const float* gq, const float* gk, float eps, void* q16, void* k16, void* v16);
 
+/* The DiT block's post-norm step (extension; the reference runs these as separate calls,
+ * zimage.cpp:122-126 / :131-135 and the next block's :113-115), one row per output row:
+ *   a  = sum over s < world of partials[(s * slot_rows + r) * D + :]  (row-parallel parts)
+ *   x[row0 + r] += gate * (rms_norm(a, eps) * gamma2)   (gate, gamma2 [D] or null for 1)
+ *   h  = bf16(rms_norm(x[row0 + r], eps) * gamma_next * scale_next)   (each [D] or null)
+ * h is stored at row row0 + r of each of the n_dst buffers h_dst[i] (n_dst = 0: no h; else
+ * n_dst = world, the tensor-parallel ranks' copies). x and h are [*, D] with row pitch D. */
+int sdb200_dit_post_norm(const float* partials, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,
+                         int64_t D, const float* gamma2, const float* gate, const float* gamma_next,
+                         const float* scale_next, uint16_t* const* h_dst, int n_dst, float eps);
+
 /* Tuning extension (no reference counterpart): forces the GEMM tile width N (64, 128,
  * 192 or 256) for later calls of this process; 0 restores the automatic choice. */
 int sdb200_set_gemm_tile(int bn);

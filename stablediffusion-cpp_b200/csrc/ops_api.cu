@@ -423,6 +423,24 @@ int sdb200_gemm_bf16_qkv_rope(int64_t M, int64_t K, const void* X, int64_t ldx, 
   })
 }
 
+int sdb200_dit_post_norm(const float* partials, int64_t slot_rows, int world, int64_t row0, int64_t rows, float* x,
+                         int64_t D, const float* gamma2, const float* gate, const float* gamma_next,
+                         const float* scale_next, uint16_t* const* h_dst, int n_dst, float eps) {
+  SDB_GUARD({
+    const char* op = "dit_post_norm";
+    require(rows >= 0 && row0 >= 0 && D > 0 && D <= 12288, op, "bad shape (0 < D <= 12288)");
+    require(world >= 1 && world <= 8 && slot_rows >= rows, op, "world must be 1..8 and slot_rows >= rows");
+    require(n_dst == 0 || n_dst == world, op, "n_dst must be 0 or world");
+    if (rows == 0) return kOk;
+    require_ptr(partials, op, "partials");
+    require_ptr(x, op, "x");
+    if (n_dst) require_ptr(h_dst, op, "h_dst");
+    for (int i = 0; i < n_dst; ++i) require_ptr(h_dst[i], op, "h_dst[i]");
+    dit_post_norm_mod_bcast(partials, slot_rows, world, row0, rows, x, (int)D, gamma2, gate, gamma_next, scale_next,
+                            h_dst, n_dst, eps);
+  })
+}
+
 int sdb200_attention(const float* q, const float* k, const float* v, float* out, int64_t N, int64_t Sq, int64_t Skv,
                      int heads, int kv_heads, int64_t d, int causal) {
   SDB_GUARD({

@@ -64,6 +64,7 @@ _SIGS = {
     "sdb200_synchronize": ([], _i),
     "sdb200_set_gemm_tile": ([_i], _i),
     "sdb200_set_gemm_pair": ([_i], _i),
+    "sdb200_dit_post_norm": ([_v, _i64, _i, _i64, _i64, _v, _i64, _v, _v, _v, _v, _v, _i, _f], _i),
     "sdb200_set_conv_implicit": ([_i], _i),
     "sdb200_gemm_nt_f32": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
     "sdb200_gemm_nt_bf16": ([_i64, _i64, _i64, _v, _i64, _v, _i64, _v, _i64, _v, _i], _i),
